@@ -1,0 +1,360 @@
+#!/usr/bin/env python
+"""Benchmark: greedy speculative decoding, random-init Gemma-7B target + Gemma-2B draft,
+k = 4, batch 1, prompt of 128 random tokens (the 1-GPU sd workload of the verify path).
+
+One bench step = one speculative iteration: k draft forwards of the 2B, one
+verify forward of the 7B over k+1 tokens, fused greedy acceptance, page
+rollback of both caches, and the 8-byte read of (accepted, recovery).
+
+Prints ONE JSON line (rank 0).  ``value`` = committed tokens/s over the K timed
+steps (all ranks, device-timed with CUDA events, max over ranks); ``e2e`` = the
+same metric for a whole ``SpeculativeDecoder.generate`` call from a host prompt
+list to host tokens (prefill included); ``verify_step_us`` / ``verify_hbm_gbs``
+describe the verify forward alone; ``roofline`` covers the dominant kernel (the
+weight-streaming projections).  With N > 1 (torchrun) each rank decodes its own
+sequence (replicas; no data-path collective).
+
+``--impl reference`` times the CPU restatement of the same path (numpy oracle:
+the reference's own JAX code cannot run here) on a bounded layer sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ssd-tpu-_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Gemma-7B/2B sd tokens/sec at TP 1/2/4/8 B200; verify-step µs; HBM GB/s"
+WORKLOAD = "gemma-7b target + gemma-2b draft, random-init bf16, sd greedy k=4, batch 1, prompt 128"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--k", type=int, default=4)
+    ap.add_argument("--prompt-len", type=int, default=128)
+    ap.add_argument("--e2e-new-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        p = json.loads(PEAKS.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU leg
+def cpu_sample_rate(k: int, tokens_per_step: float, target_w=None, draft_w=None, prompt_len: int = 128):
+    """Time the numpy oracle on a layer sample of the workload and scale to full depth.
+
+    Sample: 2 of the 28 Gemma-7B layers + its LM head (verify over k+1 tokens)
+    and 1 of the 18 Gemma-2B layers + its LM head (one draft decode), both
+    after a prompt of ``prompt_len`` tokens, fp32 numpy with all host threads.
+    Returns (tokens/s, step seconds, description).
+    """
+    import numpy as np
+
+    from oracle.gemma import GemmaShape as OShape
+    from oracle.gemma import OracleGemma, init_weights, new_pages
+
+    full_t, full_d = 28, 18
+    st = OShape(2, 3072, 16, 16, 256, 24576, 256000)
+    sd = OShape(1, 2048, 8, 1, 256, 16384, 256000)
+    wt = target_w if target_w is not None else init_weights(st, 1)
+    wd = draft_w if draft_w is not None else init_weights(sd, 2)
+    mt, md = OracleGemma(st, wt, "fp32"), OracleGemma(sd, wd, "fp32")
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, 256000, prompt_len)[None]
+    nb = (prompt_len + 64) // 16 + 2
+    table = np.arange(nb, dtype=np.int32)[None]
+    pt, pd = new_pages(st, nb, 16), new_pages(sd, nb, 16)
+    mt.forward(prompt, pt, table, [0], with_head=False)
+    md.forward(prompt, pd, table, [0], with_head=False)
+    tv, td = {}, {}
+    mt.forward(rng.integers(0, 256000, (1, k + 1)), pt, table, [prompt_len], timings=tv)
+    md.forward(rng.integers(0, 256000, (1, 1)), pd, table, [prompt_len], timings=td)
+    verify_s = tv["layers_s"] * full_t / st.num_layers + tv["head_s"]
+    draft_s = td["layers_s"] * full_d / sd.num_layers + td["head_s"]
+    step_s = k * draft_s + verify_s
+    desc = (f"numpy oracle, fp32: 2/28 Gemma-7B layers + LM head (verify, {k + 1} tokens) and 1/18 Gemma-2B "
+            f"layers + LM head (draft decode) after a {prompt_len}-token prompt, layer time scaled to full "
+            f"depth; step = {k} draft decodes + 1 verify; {tokens_per_step:.2f} tokens/step")
+    return tokens_per_step / step_s, step_s, desc
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle.gemma import GemmaShape as OShape
+    from oracle.gemma import init_weights
+
+    wt = init_weights(OShape(2, 3072, 16, 16, 256, 24576, 256000), 1)
+    wd = init_weights(OShape(1, 2048, 8, 1, 256, 16384, 256000), 2)
+    rates, steps = [], []
+    t0 = time.perf_counter()
+    n = 0
+    for i in range(args.warmup + args.steps):
+        rate, step_s, desc = cpu_sample_rate(args.k, 1.0, wt, wd, args.prompt_len)
+        if i >= args.warmup:
+            rates.append(rate)
+            steps.append(step_s)
+            n += 1
+        if time.perf_counter() - t0 > 90 and n >= 1:
+            break
+    value = float(np.mean(rates))
+    cores = os.cpu_count()
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * float(np.mean(steps)), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": args.prompt_len,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": desc + f"; {n} timed samples (1 accepted+recovery token per step assumed)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU leg
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from ssd_b200.models.gemma import PRESETS, GemmaRunner, GemmaWeights, ProjectionTimer
+    from ssd_b200.runtime.speculative import SpeculativeDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    k = args.k
+    st_, sd_ = PRESETS["gemma-7b"], PRESETS["gemma-2b"]
+    target = GemmaWeights.random(st_, seed=1000 + rank)
+    draft = GemmaWeights.random(sd_, seed=2000 + rank)
+    rng = np.random.default_rng(rank)
+    prompt = [int(x) for x in rng.integers(0, st_.vocab, args.prompt_len)]
+    total_steps = args.warmup + args.steps
+    max_seq = args.prompt_len + (total_steps + 2) * (k + 1) + 32
+    max_seq = max(max_seq, args.prompt_len + args.e2e_new_tokens * (k + 1) + 32)
+    dec = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq)
+    dec.start(prompt)
+    for _ in range(args.warmup):
+        dec.step()
+    timer = ProjectionTimer(capacity=4 * st_.num_layers + 8)
+    stream = torch.cuda.current_stream()
+    vev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    ctx_before = dec.t.n
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tokens = 0
+    accepted = 0
+    ctx_sum = 0
+    for i in range(args.steps):
+        ctx_sum += dec.t.n + k + 1
+        new = dec.step(events=vev[i], prof=timer)
+        timer.flush()
+        tokens += len(new)
+        accepted += dec.last_accept
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    verify_ms = [a.elapsed_time(b) for a, b in vev]
+    # max time / total tokens over ranks
+    t = torch.tensor([ms, float(tokens)], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = t[0:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t[1:2].clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        ms_max, tok_all = float(tmax.item()), float(tsum.item())
+    else:
+        ms_max, tok_all = ms, float(tokens)
+    value = tok_all / (ms_max / 1000.0)
+
+    # verify-step bytes: all target weights once + KV rows read (+ logits written)
+    wbytes = target.weight_bytes()
+    kv_tok = st_.kv_bytes_per_token()
+    mean_ctx = ctx_sum / args.steps
+    verify_bytes = wbytes + kv_tok * mean_ctx + (k + 1) * st_.vocab * 4
+    verify_us = 1000.0 * statistics.mean(verify_ms)
+    hbm_peak, peak_kind = peaks()
+
+    # dominant kernel: the weight-streaming projections inside the timed verify forwards
+    M = k + 1
+    d, hq, hkv, D, F, V = st_.d_model, st_.num_heads, st_.num_kv_heads, st_.head_dim, st_.ffn, st_.vocab
+    shapes = {"qkv": ((hq + 2 * hkv) * D, d, 2), "o": (d, hq * D, 2), "gate_up": (2 * F, d, 2),
+              "down": (d, F, 2), "lm_head": (V, d, 4)}
+    proj_bytes = 0.0
+    proj_ms = 0.0
+    per_kind = {}
+    for kind, (n_, k_, ob) in shapes.items():
+        nl = timer.launches[kind]
+        if nl == 0:
+            continue
+        out_cols = n_ // 2 if kind == "gate_up" else n_
+        b1 = n_ * k_ * 2 + M * k_ * 2 + M * out_cols * ob + (M * n_ * 2 if kind in ("o", "down") else 0)
+        proj_bytes += b1 * nl
+        proj_ms += timer.total_ms[kind]
+        per_kind[kind] = {"launches": nl, "us_per_launch": 1000.0 * timer.total_ms[kind] / nl,
+                          "gbs": b1 * nl / (timer.total_ms[kind] / 1000.0) / 1e9}
+    n_launch = sum(timer.launches.values())
+    achieved = proj_bytes / (proj_ms / 1000.0) / 1e9
+    lpf_t = GemmaRunner.launches_per_forward(st_, True, False)
+    lpf_d = GemmaRunner.launches_per_forward(sd_, True, True)
+    launches_per_step = k * (lpf_d + 1) + 1 + (1 + lpf_t + 1) + 2
+
+    # e2e: one whole generate() from a host prompt list to host tokens
+    dec2 = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    out, info = dec2.generate(prompt, args.e2e_new_tokens)
+    torch.cuda.synchronize()
+    w1 = time.perf_counter()
+    e2e_local = torch.tensor([w1 - w0, float(len(out))], dtype=torch.float64, device=dev)
+    if world > 1:
+        a = e2e_local[0:1].clone()
+        dist.all_reduce(a, op=dist.ReduceOp.MAX)
+        b = e2e_local[1:2].clone()
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+        e2e_val = float(b.item()) / float(a.item())
+    else:
+        e2e_val = len(out) / (w1 - w0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            wt = target.to_canonical(layers=2)
+            wd = draft.to_canonical(layers=1)
+            rate, step_s, desc = cpu_sample_rate(k, tokens / args.steps, wt, wd, args.prompt_len)
+            cpu = {"value": rate, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+        except Exception as exc:  # the CPU leg is a reported baseline only
+            cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {exc!r}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
+            "random prompt ids)",
+            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": args.prompt_len, "k": k,
+                       "parallelism": "replicas" if world > 1 else "tp1",
+                       "l2": "inputs larger than L2: 17.1 GB of target weights + 5.0 GB of draft weights "
+                             "streamed per step"},
+            "verify_step_us": verify_us,
+            "verify_hbm_gbs": verify_bytes / (verify_us / 1e6) / 1e9,
+            "verify_roofline_frac": (verify_bytes / (verify_us / 1e6) / 1e9) / hbm_peak,
+            "accept_rate": accepted / (args.steps * k),
+            "tokens_per_step": tokens / args.steps,
+            "roofline": {"bound": "hbm", "kernel": "skinny projections (QKV, O, gate/up, down, LM head), "
+                         f"M = {M}", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                         "per_launch_bytes": proj_bytes / max(n_launch, 1), "per_kind": per_kind},
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": 16 * 4 + 8 * 4,
+                    "d2h_bytes_per_step": 2 * 4 + (k + 1) * 4, "new_tokens": len(out),
+                    "api": "SpeculativeDecoder.generate(prompt list) -> token list"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

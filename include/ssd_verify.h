@@ -1,0 +1,288 @@
+/*
+ * ssd_verify.h — C ABI of the B200 (sm_100a) speculative-decoding verify path.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer argument is DEVICE memory unless the comment says "host".
+ *   - Calls are stream-ordered on `stream` and never allocate device memory:
+ *     buffers, including `workspace`, are owned by the caller.
+ *   - Workspaces must be zero-filled once when the caller allocates them; every
+ *     call leaves its workspace zero-filled again (self-resetting counters), so a
+ *     workspace can be reused by later calls on the same stream.  Calls that
+ *     share one workspace must not overlap on the GPU.
+ *   - Return value: SSD_OK (0) or an SSD_ERR_* code; invalid sizes are rejected
+ *     on the host before any launch.
+ *   - bf16 tensors are passed as `ssd_bf16` (raw bfloat16 bits); `dtype`
+ *     selects SSD_DTYPE_BF16 or SSD_DTYPE_F32 storage where both exist.
+ *
+ * Citations are to TinevimboMusingadi/ssd-tpu- (paths within that project).
+ */
+#ifndef SSD_VERIFY_H_
+#define SSD_VERIFY_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef struct CUstream_st* ssd_stream_t; /* == cudaStream_t */
+typedef uint16_t ssd_bf16;
+
+enum {
+  SSD_OK = 0,
+  SSD_ERR_INVALID = 1,     /* bad size / null pointer / unsupported shape */
+  SSD_ERR_LAUNCH = 2,      /* CUDA launch error */
+  SSD_ERR_TIMEOUT = 3,     /* a bounded device-side wait gave up */
+  SSD_ERR_UNSUPPORTED = 4, /* shape outside the compiled kernel limits */
+  SSD_ERR_WORKSPACE = 5    /* workspace too small */
+};
+
+enum { SSD_DTYPE_BF16 = 0, SSD_DTYPE_F32 = 1 };
+
+/* Human-readable text for a status code (static storage). */
+const char* ssd_status_string(int status);
+/* ABI version: (major << 16) | minor. */
+int ssd_abi_version(void);
+
+/* ------------------------------------------------------------------ K4: acceptance */
+
+/* Workspace bytes for ssd_verify_greedy / ssd_argmax_rows. */
+size_t ssd_verify_greedy_workspace_size(int B, int K, int V);
+
+/*
+ * Greedy verification over K+1 positions.
+ * Replaces jax_ssd/algorithm/verify.py:18-59 (verify_greedy) and
+ * reference/cuda_ssd/verify_torch.py:8-45.
+ *   logits_p      [B, K+1, V] fp32 target logits
+ *   speculations  [B, K+1] int32; column 0 = previous recovery, 1..K = draft
+ *   accept_until  [B] int32 out: leading draft tokens equal to the target argmax
+ *   recovery      [B] int32 out: target argmax at position accept_until
+ *   accepted_mask [B, K+1] uint8 out (may be NULL): [b,0]=0, [b,j+1]=(j<accept_until)
+ *   target_tokens [B, K+1] int32 out (may be NULL): argmax of every row
+ * argmax ties resolve to the first index.
+ */
+int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t* speculations,
+                      int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
+                      int32_t* target_tokens, void* workspace, size_t workspace_bytes, int B, int K,
+                      int V);
+
+/*
+ * Row-wise argmax (first index on ties) of x[rows, V] (row stride `ld`
+ * elements), e.g. the draft's greedy token.  Replaces the jnp.argmax calls of
+ * jax_ssd/runtime/engine.py:224 and jax_ssd/models/gemma_adapter.py:127.
+ * Uses the ssd_verify_greedy workspace sizing with B=rows, K=0.
+ */
+int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, int32_t* out,
+                    void* workspace, size_t workspace_bytes);
+
+/* Workspace bytes for ssd_verify_sample. */
+size_t ssd_verify_sample_workspace_size(int B, int K, int V);
+
+enum { SSD_ALIGN_REFERENCE = 0, SSD_ALIGN_STANDARD = 1 };
+
+/*
+ * Sampling-mode verification (rejection sampling, bonus token, residual).
+ * Replaces jax_ssd/algorithm/verify.py:68-120 (verify_sample, _verify_sample_row)
+ * with the JAX threefry draws replaced by explicit uniforms:
+ *   u_accept [B, K] in [0,1): draft token j is accepted iff u < min(1, p/max(q,1e-12))
+ *   u_gumbel [B, V] in (0,1): categorical draw = argmax(log(r + 1e-12) - log(-log u))
+ *   logits_q [B, K, V] fp32 draft logits; temperatures must be > 0.
+ *   alignment SSD_ALIGN_REFERENCE judges draft token j+1 with target row j+1
+ *   (verify.py:103 as written); SSD_ALIGN_STANDARD uses row j.
+ */
+int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, const float* logits_q,
+                      const int32_t* speculations, const float* u_accept, const float* u_gumbel,
+                      float temperature_p, float temperature_q, float sampler_x, int alignment,
+                      int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
+                      void* workspace, size_t workspace_bytes, int B, int K, int V);
+
+/*
+ * Fill out[n] with counter-based uniforms in (0,1): a stateless hash of
+ * (seed, offset + i).  Stands in for jax.random.split/uniform
+ * (jax_ssd/algorithm/verify.py:80,100,107) when the caller passes a seed.
+ */
+int ssd_uniform_fill(ssd_stream_t stream, float* out, int64_t n, uint64_t seed, uint64_t offset);
+
+/* ---------------------------------------------------------- K5: paged-KV blocks */
+/*
+ * Device mirror of the host page manager (jax_ssd/runtime/page_manager.py).
+ * State: block_tables [B, max_blocks] int32 (unused entries -1), table_lens [B],
+ * free_list [num_blocks] used as a stack free_list[0:*free_top] (pop/push at the
+ * top, i.e. the END of the reference's Python list), ref_counts [num_blocks]
+ * (0 = absent from the reference's dict).  Sequences are processed in index
+ * order, exactly as successive per-sequence calls of the reference.
+ */
+
+/* PageManager.allocate / allocate_draft (page_manager.py:21-47): grow each table to
+ * ceil((num_tokens+num_new)/block_size) blocks popped from the free-list top;
+ * a sequence that does not fit is left unchanged and gets ok[b]=0. */
+int ssd_page_allocate(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens,
+                      int max_blocks, int32_t* free_list, int32_t* free_top, int32_t* ref_counts,
+                      int num_blocks, const int32_t* num_tokens, const int32_t* num_new,
+                      uint8_t* ok, int block_size, int B);
+
+/* PageManager.rollback_speculative (page_manager.py:49-56, _free_block :66-70):
+ * pop blocks from the END of each table while len > ceil((num_tokens+accepted)/bs);
+ * each popped block's ref count drops (absent counts as 1) and at 0 it is pushed
+ * on the free list.  kv_lens (may be NULL) receives num_tokens+accepted, the
+ * truncated valid KV length. */
+int ssd_page_rollback(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens,
+                      int max_blocks, int32_t* free_list, int32_t* free_top, int32_t* ref_counts,
+                      int num_blocks, const int32_t* num_tokens, const int32_t* accepted,
+                      int32_t* kv_lens, int block_size, int B);
+
+/* PageManager.free_sequence (page_manager.py:58-64) for every b with
+ * release[b] != 0: target table in forward order, then the draft table
+ * (draft_tables may be NULL). */
+int ssd_page_free(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens, int max_blocks,
+                  int32_t* draft_tables, int32_t* draft_lens, int draft_max_blocks,
+                  int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks,
+                  const uint8_t* release, int B);
+
+/* --------------------------------------------------------------- K2: KV write */
+/*
+ * Write K/V rows of new tokens into the paged cache.
+ * Replaces jax_ssd/kernels/kv_cache.py:39-58 (write_kv_slots); layout
+ * kv_cache.py:13,28-31: pages [2, num_layers, num_blocks, block_size, Hkv, D].
+ *   positions [B, T] int32 (-1 = skip); slot = block_tables[b][p/bs]*bs + p%bs
+ *   k, v      [B, T, Hkv, D] in the cache dtype
+ */
+int ssd_kv_write(ssd_stream_t stream, void* pages, int dtype, int num_layers, int num_blocks,
+                 int block_size, int num_kv_heads, int head_dim, int layer,
+                 const int32_t* block_tables, int max_blocks, const int32_t* positions,
+                 const void* k, const void* v, int B, int T);
+
+/* --------------------------------------------------- K1: paged verify attention */
+
+size_t ssd_paged_attention_workspace_size(int B, int T, int num_heads, int num_kv_heads,
+                                          int head_dim, int max_seq_len);
+
+/*
+ * Multi-query attention of each sequence's new tokens against its pages.
+ * Replaces jax_ssd/kernels/attention_ref.py:9-21 with the mask of
+ * jax_ssd/kernels/masks.py:33-40 and the page layout of kv_cache.py:13.
+ *   q        [B, T, Hq, D]; out [B, T, Hq, D] (cache dtype)
+ *   seq_lens [B]: cached tokens INCLUDING the new ones (already written)
+ *   q_lens   [B] or NULL (= T): valid new tokens; new token t sits at position
+ *            seq_lens[b] - q_lens[b] + t and sees positions 0..that position.
+ *   GQA: query head h reads KV head h / (Hq / Hkv).  max_seq_len bounds seq_lens.
+ *   Rows t >= q_lens[b] are written as zeros.
+ */
+int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, const void* pages, int dtype,
+                               int num_layers, int num_blocks, int block_size, int num_kv_heads,
+                               int head_dim, int layer, const int32_t* block_tables, int max_blocks,
+                               const int32_t* seq_lens, const int32_t* q_lens, void* out,
+                               float scale, int B, int T, int num_heads, int max_seq_len,
+                               void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------- K3: skinny projections */
+
+enum {
+  SSD_EPI_STORE = 0,     /* y[M,N] = x w^T in the activation dtype */
+  SSD_EPI_STORE_F32 = 1, /* y[M,N] fp32 (logits) */
+  SSD_EPI_RESIDUAL = 2,  /* y[M,N] (in/out) = round(y + round(x w^T)) */
+  SSD_EPI_GEGLU = 3      /* w rows interleaved (gate_i, up_i): y[M,N/2] =
+                            round(round(gelu_tanh(round(g))) * round(u)) */
+};
+
+size_t ssd_linear_workspace_size(int M, int N, int K);
+/* Largest M (tokens x sequences) one ssd_linear / ssd_gemma_forward call takes. */
+int ssd_linear_max_m(void);
+
+/*
+ * y = epilogue(x[M,K] w[N,K]^T) with fp32 accumulation; w row-major like the
+ * reference's Gemma projections (HF Flax Gemma, called from
+ * jax_ssd/models/gemma_adapter.py:81-102).
+ */
+int ssd_linear(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y,
+               int epilogue, int M, int N, int K, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------ fused small ops of the forward */
+
+/* x[m] = round(embed[tokens[m]] * round(sqrt(d))) ; tokens [M] int32 */
+int ssd_embed(ssd_stream_t stream, const int32_t* tokens, const void* embed, int dtype, void* x,
+              int M, int d, int vocab);
+/* y[m] = round(x * rsqrt(mean(x^2) + eps) * (1 + w)) (Gemma RMSNorm) */
+int ssd_rmsnorm(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y, int M,
+                int d, float eps);
+/*
+ * RoPE (rotate-half, table cos/sin [max_pos, D/2] fp32) on the q and k parts
+ * of qkv [B*T, (Hq+2Hkv)*D], q written to q_out [B*T, Hq, D], rotated k and v
+ * written into the pages (fused K2).  positions as in ssd_kv_write.
+ */
+int ssd_rope_kv_write(ssd_stream_t stream, const void* qkv, void* q_out, void* pages, int dtype,
+                      int num_layers, int num_blocks, int block_size, int num_heads,
+                      int num_kv_heads, int head_dim, int layer, const int32_t* block_tables,
+                      int max_blocks, const int32_t* positions, const float* rope_cos,
+                      const float* rope_sin, int rope_max_pos, int B, int T);
+
+/* --------------------------------------------------- whole-model verify forward */
+
+typedef struct {
+  int num_layers, d_model, num_heads, num_kv_heads, head_dim, ffn, vocab;
+  float eps;
+  int dtype;                       /* storage dtype of weights, activations and KV */
+  const void* embed;               /* [vocab, d] (tied LM head) */
+  const void* final_norm;          /* [d] */
+  const void* const* attn_norm;    /* host array [L] of device [d] */
+  const void* const* w_qkv;        /* host array [L] of device [(Hq+2Hkv)*D, d] */
+  const void* const* w_o;          /* host array [L] of device [d, Hq*D] */
+  const void* const* mlp_norm;     /* host array [L] of device [d] */
+  const void* const* w_gate_up;    /* host array [L] of device [2F, d], rows (gate_i, up_i) */
+  const void* const* w_down;       /* host array [L] of device [d, F] */
+  const float* rope_cos;           /* [rope_max_pos, D/2] */
+  const float* rope_sin;
+  int rope_max_pos;
+} ssd_gemma_weights;
+
+typedef struct {
+  int B, T;                        /* sequences, new tokens per sequence (padded) */
+  const int32_t* tokens;           /* [B, T] */
+  const int32_t* seq_lens_before;  /* [B] tokens already cached */
+  const int32_t* q_lens;           /* [B] valid new tokens, or NULL (= T) */
+  void* kv_pages;                  /* [2, L, num_blocks, block_size, Hkv, D] */
+  int num_blocks, block_size;
+  const int32_t* block_tables;     /* [B, max_blocks] */
+  int max_blocks;
+  int max_seq_len;                 /* bound on seq_lens_before + T */
+  float* logits;                   /* [B, T, V] fp32, [B, V] with logits_last_only, or NULL
+                                      (prompt chunks: K/V only, no final norm / LM head) */
+  int logits_last_only;            /* 1: logits of each sequence's last valid token only */
+  void* scratch;                   /* activations + workspaces, zero-filled once */
+  size_t scratch_bytes;
+  /* Optional launch timing of the projections (all NULL/0 to disable): host
+   * array of 2*prof_capacity cudaEvent_t; event 2i / 2i+1 are recorded on
+   * `stream` around the i-th projection, prof_kind[i] names it (0 qkv, 1 o,
+   * 2 gate_up, 3 down, 4 lm_head) and *prof_count receives the number used. */
+  void* const* prof_events;
+  int prof_capacity;
+  int* prof_count;
+  int* prof_kind;
+} ssd_gemma_batch;
+
+size_t ssd_gemma_scratch_size(const ssd_gemma_weights* w, int B, int T, int max_seq_len);
+
+/*
+ * Target (or draft) forward over the new tokens of B sequences against the paged
+ * cache: writes their K/V rows and the fp32 logits.  Replaces
+ * DecodeModelAdapter.verify/prefill/decode (jax_ssd/models/base.py:34-58) as
+ * implemented by GemmaAdapter (jax_ssd/models/gemma_adapter.py:81-143).
+ * `w` and the pointer arrays it holds are host memory read during the call.
+ */
+int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w, const ssd_gemma_batch* b);
+
+/* Seeded N(0, std^2) init of n elements (counter-based hash + Box-Muller). */
+int ssd_normal_fill(ssd_stream_t stream, void* out, int dtype, int64_t n, float std, uint64_t seed);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSD_VERIFY_H_ */

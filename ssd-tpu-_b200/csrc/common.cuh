@@ -1,0 +1,135 @@
+// Shared device helpers for the verify-step kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/ssd_verify.h"
+
+namespace ssd {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(bf16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ bf16 from_f<bf16>(float x) { return __float2bfloat16_rn(x); }
+
+// Round an fp32 value to bf16 precision, staying in fp32.
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <typename T> __device__ __forceinline__ float store_round(float x) { return x; }
+template <> __device__ __forceinline__ float store_round<bf16>(float x) { return round_bf16(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+
+// Order-preserving map of fp32 onto uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+// (value, index) packed so that max() picks the larger value, then the SMALLER index
+// (first-occurrence argmax, as numpy/jnp/torch argmax).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  return ((unsigned long long)float_key(v) << 32) | (unsigned long long)(0xffffffffu - idx);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) {
+  return 0xffffffffu - (uint32_t)(k & 0xffffffffu);
+}
+__device__ __forceinline__ float argmax_key_value(unsigned long long k) {
+  return key_float((uint32_t)(k >> 32));
+}
+
+// Block-wide reductions; every thread receives the result.  `scratch` must hold
+// 32 entries and may be reused after the call returns.
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) scratch[wid] = v;
+  __syncthreads();
+  T r = scratch[0];
+  for (int i = 1; i < nw; ++i) r = op(r, scratch[i]);
+  return r;
+}
+
+struct OpSum { template <typename T> __device__ T operator()(T a, T b) const { return a + b; } };
+struct OpMax {
+  __device__ float operator()(float a, float b) const { return fmaxf(a, b); }
+  __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a > b ? a : b; }
+};
+
+// "Last block done" ticket: returns true in exactly one block of the group once
+// all `total` blocks of the group have called it.  The counter is reset to 0 by
+// that block, so the workspace stays reusable without a memset.  Each block must
+// have written its partial results before calling (a __threadfence is issued).
+__device__ __forceinline__ bool last_block_of(unsigned int* counter, unsigned int total, bool* smem_flag) {
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int prev = atomicAdd(counter, 1u);
+    bool last = (prev == total - 1);
+    if (last) atomicExch(counter, 0u);
+    *smem_flag = last;
+  }
+  __syncthreads();
+  bool last = *smem_flag;
+  if (last) __threadfence();
+  return last;
+}
+
+// 16-byte aligned vector of 8 bf16 values.
+struct alignas(16) bf16x8 { __nv_bfloat162 h[4]; };
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+}  // namespace ssd
+
+#define SSD_CHECK_LAUNCH()                               \
+  do {                                                   \
+    cudaError_t e__ = cudaGetLastError();                \
+    if (e__ != cudaSuccess) return SSD_ERR_LAUNCH;       \
+  } while (0)

@@ -1,0 +1,292 @@
+// Whole-model verify forward (native runtime) and the small fused ops it uses.
+//
+// ssd_gemma_forward replaces DecodeModelAdapter.verify / prefill / decode
+// (jax_ssd/models/base.py:34-58) as implemented by GemmaAdapter
+// (jax_ssd/models/gemma_adapter.py:81-143): one host call issues the whole
+// layer stack on one stream, so it can be captured into a CUDA graph.  Per
+// layer: RMSNorm -> QKV projection -> RoPE + K/V page write (fused) -> paged
+// attention -> O projection with the residual add fused -> RMSNorm -> gate/up
+// projection with GeGLU fused -> down projection with the residual add fused.
+// Numerics: bf16 storage between these ops, fp32 math inside them.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "linear.cuh"
+
+namespace ssd {
+namespace {
+
+template <typename T>
+__global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __restrict__ E, T* __restrict__ x, int d,
+                             int vocab, float scale) {
+  const int m = blockIdx.x;
+  int tok = tokens[m];
+  tok = tok < 0 ? 0 : (tok >= vocab ? vocab - 1 : tok);
+  const T* e = E + (int64_t)tok * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) x[(int64_t)m * d + i] = from_f<T>(__fmul_rn(to_f(e[i]), scale));
+}
+
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int d, float eps) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const T* xr = x + (int64_t)m * d;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = to_f(xr[i]);
+    s = fmaf(v, v, s);
+  }
+  s = block_reduce(s, red, OpSum());
+  const float ms = __fdiv_rn(s, (float)d);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    y[(int64_t)m * d + i] = from_f<T>(__fmul_rn(__fmul_rn(to_f(xr[i]), inv), __fadd_rn(1.0f, to_f(w[i]))));
+}
+
+// positions[b*T+t] = seq_lens_before[b] + t for t < q_lens[b], else -1; seq_after[b].
+__global__ void positions_kernel(const int32_t* __restrict__ slb, const int32_t* __restrict__ ql, int B, int T,
+                                 int32_t* __restrict__ pos, int32_t* __restrict__ seq_after,
+                                 int32_t* __restrict__ qlen_out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * T; i += gridDim.x * blockDim.x) {
+    const int b = i / T, t = i % T;
+    const int q = ql ? ql[b] : T;
+    pos[i] = t < q ? slb[b] + t : -1;
+    if (t == 0) {
+      seq_after[b] = slb[b] + q;
+      qlen_out[b] = q;
+    }
+  }
+}
+
+// rows[b] = h[b*T + q_lens[b]-1]  (last valid token per sequence)
+template <typename T>
+__global__ void gather_last_kernel(const T* __restrict__ h, const int32_t* __restrict__ qlen, int tq, int d,
+                                   T* __restrict__ out) {
+  const int b = blockIdx.x;
+  const int t = min(max(qlen[b] - 1, 0), tq - 1);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)b * d + i] = h[((int64_t)b * tq + t) * d + i];
+}
+
+inline size_t a256(size_t x) { return align_up256(x); }
+
+struct Scratch {
+  void *x, *h, *qkv, *q, *attn, *act, *hl;
+  int32_t *pos, *seq_after, *qlen;
+  void* lin_ws;
+  size_t lin_ws_bytes;
+  void* attn_ws;
+  size_t attn_ws_bytes;
+  size_t total;
+};
+
+int max_m() { return 16; }
+
+size_t linear_ws_any(int M, int N, int K, int dtype) {
+  if (dtype == SSD_DTYPE_BF16 && linear_tc_supported(M, N, K)) return linear_tc_workspace(M, N, K);
+  return linear_cc_workspace(M, N, K, dtype == SSD_DTYPE_BF16 ? 2 : 4);
+}
+
+Scratch carve(const ssd_gemma_weights* w, int B, int T, int max_seq_len, char* base) {
+  Scratch s{};
+  const size_t es = w->dtype == SSD_DTYPE_BF16 ? 2 : 4;
+  const int M = B * T;
+  const int d = w->d_model, D = w->head_dim, hq = w->num_heads, hkv = w->num_kv_heads, F = w->ffn;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char* p = base ? base + off : nullptr; off += a256(bytes); return (void*)p; };
+  s.x = take(es * M * d);
+  s.h = take(es * M * d);
+  s.qkv = take(es * (size_t)M * (hq + 2 * hkv) * D);
+  s.q = take(es * (size_t)M * hq * D);
+  s.attn = take(es * (size_t)M * hq * D);
+  s.act = take(es * (size_t)M * F);
+  s.hl = take(es * (size_t)B * d);
+  s.pos = (int32_t*)take(sizeof(int32_t) * M);
+  s.seq_after = (int32_t*)take(sizeof(int32_t) * B);
+  s.qlen = (int32_t*)take(sizeof(int32_t) * B);
+  size_t lw = 0;
+  auto upd = [&](int m, int n, int k) { lw = std::max(lw, linear_ws_any(m, n, k, w->dtype)); };
+  upd(M, (hq + 2 * hkv) * D, d);
+  upd(M, d, hq * D);
+  upd(M, 2 * F, d);
+  upd(M, d, F);
+  upd(M, w->vocab, d);
+  upd(B, w->vocab, d);
+  s.lin_ws_bytes = lw;
+  s.lin_ws = take(lw);
+  s.attn_ws_bytes = ssd_paged_attention_workspace_size(B, T, hq, hkv, D, max_seq_len);
+  s.attn_ws = take(s.attn_ws_bytes);
+  s.total = off;
+  return s;
+}
+
+}  // namespace
+
+int linear_dispatch(cudaStream_t st, const void* x, const void* w, int dtype, void* y, int epi, int M, int N, int K,
+                    void* ws, size_t ws_bytes) {
+  if (dtype == SSD_DTYPE_BF16) {
+    if (linear_tc_supported(M, N, K)) return linear_tc(st, x, w, y, epi, M, N, K, ws, ws_bytes);
+    return linear_cc<bf16>(st, x, w, y, epi, M, N, K, ws, ws_bytes);
+  }
+  return linear_cc<float>(st, x, w, y, epi, M, N, K, ws, ws_bytes);
+}
+
+}  // namespace ssd
+
+using namespace ssd;
+
+extern "C" const char* ssd_status_string(int status) {
+  switch (status) {
+    case SSD_OK: return "ok";
+    case SSD_ERR_INVALID: return "invalid argument";
+    case SSD_ERR_LAUNCH: return "CUDA launch error";
+    case SSD_ERR_TIMEOUT: return "device-side wait timed out";
+    case SSD_ERR_UNSUPPORTED: return "shape outside compiled kernel limits";
+    case SSD_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int ssd_abi_version(void) { return (1 << 16) | 0; }
+
+extern "C" int ssd_linear_max_m(void) { return max_m(); }
+
+extern "C" size_t ssd_linear_workspace_size(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  // large enough for either storage dtype
+  return std::max(linear_ws_any(M, N, K, SSD_DTYPE_BF16), linear_ws_any(M, N, K, SSD_DTYPE_F32));
+}
+
+extern "C" int ssd_linear(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y, int epilogue, int M,
+                          int N, int K, void* workspace, size_t workspace_bytes) {
+  if (M <= 0 || N <= 0 || K <= 0 || !x || !w || !y) return SSD_ERR_INVALID;
+  if (M > max_m()) return SSD_ERR_UNSUPPORTED;
+  if (epilogue < SSD_EPI_STORE || epilogue > SSD_EPI_GEGLU) return SSD_ERR_INVALID;
+  if (epilogue == SSD_EPI_GEGLU && (N & 1)) return SSD_ERR_INVALID;
+  if (dtype != SSD_DTYPE_BF16 && dtype != SSD_DTYPE_F32) return SSD_ERR_INVALID;
+  const int vn = dtype == SSD_DTYPE_BF16 ? 8 : 4;
+  if (K % vn) return SSD_ERR_UNSUPPORTED;
+  return linear_dispatch((cudaStream_t)stream, x, w, dtype, y, epilogue, M, N, K, workspace, workspace_bytes);
+}
+
+extern "C" int ssd_embed(ssd_stream_t stream, const int32_t* tokens, const void* embed, int dtype, void* x, int M,
+                         int d, int vocab) {
+  if (M <= 0 || d <= 0 || vocab <= 0 || !tokens || !embed || !x) return SSD_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  float scale = sqrtf((float)d);
+  if (dtype == SSD_DTYPE_BF16) {
+    scale = __bfloat162float(__float2bfloat16_rn(scale));
+    embed_kernel<bf16><<<M, 256, 0, st>>>(tokens, (const bf16*)embed, (bf16*)x, d, vocab, scale);
+  } else if (dtype == SSD_DTYPE_F32) {
+    embed_kernel<float><<<M, 256, 0, st>>>(tokens, (const float*)embed, (float*)x, d, vocab, scale);
+  } else {
+    return SSD_ERR_INVALID;
+  }
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+extern "C" int ssd_rmsnorm(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y, int M, int d,
+                           float eps) {
+  if (M <= 0 || d <= 0 || !x || !w || !y) return SSD_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == SSD_DTYPE_BF16)
+    rmsnorm_kernel<bf16><<<M, 256, 0, st>>>((const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
+  else if (dtype == SSD_DTYPE_F32)
+    rmsnorm_kernel<float><<<M, 256, 0, st>>>((const float*)x, (const float*)w, (float*)y, d, eps);
+  else
+    return SSD_ERR_INVALID;
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+static bool weights_ok(const ssd_gemma_weights* w) {
+  if (!w || w->num_layers <= 0 || w->d_model <= 0 || w->num_heads <= 0 || w->num_kv_heads <= 0 ||
+      w->num_heads % w->num_kv_heads || w->head_dim <= 0 || w->ffn <= 0 || w->vocab <= 0)
+    return false;
+  if (w->dtype != SSD_DTYPE_BF16 && w->dtype != SSD_DTYPE_F32) return false;
+  if (!w->embed || !w->final_norm || !w->attn_norm || !w->w_qkv || !w->w_o || !w->mlp_norm || !w->w_gate_up ||
+      !w->w_down || !w->rope_cos || !w->rope_sin || w->rope_max_pos <= 0)
+    return false;
+  for (int l = 0; l < w->num_layers; ++l)
+    if (!w->attn_norm[l] || !w->w_qkv[l] || !w->w_o[l] || !w->mlp_norm[l] || !w->w_gate_up[l] || !w->w_down[l])
+      return false;
+  return true;
+}
+
+extern "C" size_t ssd_gemma_scratch_size(const ssd_gemma_weights* w, int B, int T, int max_seq_len) {
+  if (!w || B <= 0 || T <= 0 || max_seq_len <= 0) return 0;
+  return carve(w, B, T, max_seq_len, nullptr).total;
+}
+
+extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w, const ssd_gemma_batch* bt) {
+  if (!weights_ok(w) || !bt) return SSD_ERR_INVALID;
+  const int B = bt->B, T = bt->T, M = B * T;
+  if (B <= 0 || T <= 0 || !bt->tokens || !bt->seq_lens_before || !bt->kv_pages || !bt->block_tables ||
+      !bt->scratch || bt->max_seq_len <= 0 || bt->num_blocks <= 0 || bt->block_size <= 0)
+    return SSD_ERR_INVALID;
+  if (M > max_m()) return SSD_ERR_UNSUPPORTED;
+  if ((int64_t)bt->max_blocks * bt->block_size < bt->max_seq_len) return SSD_ERR_INVALID;
+  if (bt->max_seq_len > w->rope_max_pos) return SSD_ERR_INVALID;
+  const Scratch s = carve(w, B, T, bt->max_seq_len, reinterpret_cast<char*>(bt->scratch));
+  if (bt->scratch_bytes < s.total) return SSD_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int dt = w->dtype;
+  const int d = w->d_model, D = w->head_dim, hq = w->num_heads, hkv = w->num_kv_heads, F = w->ffn;
+  const int L = w->num_layers;
+  const float scale = 1.0f / sqrtf((float)D);
+  int rc;
+#define SSD_TRY(expr)              \
+  do {                             \
+    rc = (expr);                   \
+    if (rc != SSD_OK) return rc;   \
+  } while (0)
+  int nprof = 0;
+  auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k) {
+    const bool rec = bt->prof_events && nprof < bt->prof_capacity;
+    if (rec) cudaEventRecord((cudaEvent_t)bt->prof_events[2 * nprof], st);
+    const int r = linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes);
+    if (rec) {
+      cudaEventRecord((cudaEvent_t)bt->prof_events[2 * nprof + 1], st);
+      if (bt->prof_kind) bt->prof_kind[nprof] = kind;
+      ++nprof;
+      if (bt->prof_count) *bt->prof_count = nprof;
+    }
+    return r;
+  };
+  if (bt->prof_count) *bt->prof_count = 0;
+
+  positions_kernel<<<(M + 255) / 256, 256, 0, st>>>(bt->seq_lens_before, bt->q_lens, B, T, s.pos, s.seq_after,
+                                                     s.qlen);
+  SSD_CHECK_LAUNCH();
+  SSD_TRY(ssd_embed(stream, bt->tokens, w->embed, dt, s.x, M, d, w->vocab));
+  for (int l = 0; l < L; ++l) {
+    SSD_TRY(ssd_rmsnorm(stream, s.x, w->attn_norm[l], dt, s.h, M, d, w->eps));
+    SSD_TRY(proj(0, s.h, w->w_qkv[l], s.qkv, SSD_EPI_STORE, M, (hq + 2 * hkv) * D, d));
+    SSD_TRY(ssd_rope_kv_write(stream, s.qkv, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hq, hkv, D, l,
+                              bt->block_tables, bt->max_blocks, s.pos, w->rope_cos, w->rope_sin, w->rope_max_pos, B,
+                              T));
+    SSD_TRY(ssd_paged_verify_attention(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
+                                       bt->block_tables, bt->max_blocks, s.seq_after, s.qlen, s.attn, scale, B, T,
+                                       hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes));
+    SSD_TRY(proj(1, s.attn, w->w_o[l], s.x, SSD_EPI_RESIDUAL, M, d, hq * D));
+    SSD_TRY(ssd_rmsnorm(stream, s.x, w->mlp_norm[l], dt, s.h, M, d, w->eps));
+    SSD_TRY(proj(2, s.h, w->w_gate_up[l], s.act, SSD_EPI_GEGLU, M, 2 * F, d));
+    SSD_TRY(proj(3, s.act, w->w_down[l], s.x, SSD_EPI_RESIDUAL, M, d, F));
+  }
+  if (!bt->logits) return SSD_OK;  // prompt chunk: only the K/V rows were needed
+  SSD_TRY(ssd_rmsnorm(stream, s.x, w->final_norm, dt, s.h, M, d, w->eps));
+  if (bt->logits_last_only) {
+    if (dt == SSD_DTYPE_BF16)
+      gather_last_kernel<bf16><<<B, 256, 0, st>>>((const bf16*)s.h, s.qlen, T, d, (bf16*)s.hl);
+    else
+      gather_last_kernel<float><<<B, 256, 0, st>>>((const float*)s.h, s.qlen, T, d, (float*)s.hl);
+    SSD_CHECK_LAUNCH();
+    SSD_TRY(proj(4, s.hl, w->embed, bt->logits, SSD_EPI_STORE_F32, B, w->vocab, d));
+  } else {
+    SSD_TRY(proj(4, s.h, w->embed, bt->logits, SSD_EPI_STORE_F32, M, w->vocab, d));
+  }
+#undef SSD_TRY
+  return SSD_OK;
+}

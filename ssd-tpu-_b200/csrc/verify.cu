@@ -1,0 +1,482 @@
+// K4: fused acceptance kernels — greedy verify, row argmax, rejection sampling
+// with bonus / residual draw — plus the counter-based uniform / normal fills.
+//
+// Greedy follows jax_ssd/algorithm/verify.py:18-59; sampling follows
+// verify.py:68-120 (see include/ssd_verify.h for the argument contract).
+//
+// All of these are HBM-bound vocabulary scans.  Each scan splits a row of V
+// logits into `nchunks` slices so that the grid covers every SM several times;
+// each CTA reduces its slice to a partial (argmax key, or max/sum-exp pair) in
+// the workspace, and the last CTA of a group (atomic ticket, self-resetting)
+// folds the partials in fixed chunk order, so results are deterministic.
+#include "common.cuh"
+
+namespace ssd {
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kTargetCtas = 148 * 4;
+
+inline int scan_chunks(int rows, int V) {
+  if (rows <= 0 || V <= 0) return 1;
+  int want = (kTargetCtas + rows - 1) / rows;
+  int cap = (V + 2047) / 2048;  // at least 2K elements per CTA
+  if (cap < 1) cap = 1;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return want;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Chunk [lo, hi) of a row of V elements; bounds are multiples of 4 except the end.
+__device__ __forceinline__ void chunk_bounds(int V, int nchunks, int c, int& lo, int& hi) {
+  int per = (V + nchunks - 1) / nchunks;
+  per = (per + 3) & ~3;
+  lo = min(c * per, V);
+  hi = min(lo + per, V);
+}
+
+// Thread-local first-occurrence argmax over x[lo:hi).
+__device__ __forceinline__ void scan_argmax(const float* __restrict__ row, int lo, int hi, bool vec_ok,
+                                            float& best, int& bidx) {
+  best = -INFINITY;
+  bidx = 0x7fffffff;
+  if (vec_ok) {
+    const int nv = (hi - lo) >> 2;
+    const float4* p = reinterpret_cast<const float4*>(row + lo);
+    int i = threadIdx.x;
+    for (; i + 3 * kScanThreads < nv; i += 4 * kScanThreads) {
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(p + i + u * kScanThreads);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int base = lo + 4 * (i + u * kScanThreads);
+        if (a[u].x > best) { best = a[u].x; bidx = base; }
+        if (a[u].y > best) { best = a[u].y; bidx = base + 1; }
+        if (a[u].z > best) { best = a[u].z; bidx = base + 2; }
+        if (a[u].w > best) { best = a[u].w; bidx = base + 3; }
+      }
+    }
+    for (; i < nv; i += kScanThreads) {
+      float4 a = __ldg(p + i);
+      const int base = lo + 4 * i;
+      if (a.x > best) { best = a.x; bidx = base; }
+      if (a.y > best) { best = a.y; bidx = base + 1; }
+      if (a.z > best) { best = a.z; bidx = base + 2; }
+      if (a.w > best) { best = a.w; bidx = base + 3; }
+    }
+    for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) {
+      float v = __ldg(row + j);
+      if (v > best) { best = v; bidx = j; }
+    }
+  } else {
+    for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
+      float v = __ldg(row + j);
+      if (v > best) { best = v; bidx = j; }
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned long long thread_key(float best, int bidx) {
+  // A thread that saw no element contributes the minimum key.
+  return bidx == 0x7fffffff ? 0ull : argmax_key(best, (uint32_t)bidx);
+}
+
+// ---------------------------------------------------------------- greedy
+// grid (nchunks, rows); rows = B*(K+1) (verify) or rows (argmax_rows, K = 0).
+// group = b for verify (all K+1 rows), row for argmax_rows.
+__global__ void __launch_bounds__(kScanThreads)
+greedy_scan_kernel(const float* __restrict__ x, int64_t ld, int V, int kp1, int nchunks,
+                   bool vec_ok, unsigned int* __restrict__ counters,
+                   unsigned long long* __restrict__ partial, const int32_t* __restrict__ spec,
+                   int32_t* __restrict__ accept_until, int32_t* __restrict__ recovery,
+                   uint8_t* __restrict__ mask, int32_t* __restrict__ target_tokens,
+                   int32_t* __restrict__ argmax_out) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool is_last;
+  __shared__ int tt[64];
+  const int row = blockIdx.y, c = blockIdx.x;
+  int lo, hi;
+  chunk_bounds(V, nchunks, c, lo, hi);
+  float best;
+  int bidx;
+  scan_argmax(x + (int64_t)row * ld, lo, hi, vec_ok, best, bidx);
+  unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
+  if (threadIdx.x == 0) partial[(int64_t)row * nchunks + c] = key;
+
+  const int group = row / kp1;
+  if (!last_block_of(&counters[group], (unsigned)(kp1 * nchunks), &is_last)) return;
+
+  // Fold the partials of every row of the group in chunk order.
+  for (int r = 0; r < kp1; ++r) {
+    unsigned long long k = 0ull;
+    for (int i = threadIdx.x; i < nchunks; i += blockDim.x) {
+      unsigned long long v = __ldcg(&partial[(int64_t)(group * kp1 + r) * nchunks + i]);
+      k = v > k ? v : k;
+    }
+    k = block_reduce(k, red, OpMax());
+    if (threadIdx.x == 0) tt[r] = (int)argmax_key_index(k);
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  if (argmax_out) {  // argmax_rows: kp1 == 1
+    argmax_out[group] = tt[0];
+    return;
+  }
+  const int K = kp1 - 1;
+  const int b = group;
+  int acc = 0;
+  while (acc < K && spec[(int64_t)b * kp1 + acc + 1] == tt[acc]) ++acc;
+  accept_until[b] = acc;
+  recovery[b] = tt[acc];  // == tt[K] when every draft token is accepted
+  if (mask) {
+    mask[(int64_t)b * kp1] = 0;
+    for (int j = 0; j < K; ++j) mask[(int64_t)b * kp1 + j + 1] = (j < acc) ? 1 : 0;
+  }
+  if (target_tokens)
+    for (int j = 0; j < kp1; ++j) target_tokens[(int64_t)b * kp1 + j] = tt[j];
+}
+
+// ---------------------------------------------------------------- sampling
+struct SampleDecision {
+  int acc;        // accepted draft tokens
+  int bonus;      // 1: all accepted, draw from softmax(lp[K]/Tp)
+  int prow, qrow; // rows used for the final draw
+  float mp, sp, mq, sq;  // softmax max / sum of those rows (temperature applied)
+  float rsum;     // max(sum(residual), 1e-12)
+  float pad[3];
+};
+
+// fp32 ops written out so the compiler cannot contract them into FMAs: the
+// oracle evaluates the same expressions with separate roundings.
+__device__ __forceinline__ float prob_of(float logit, float temp, float m, float s) {
+  return __fdiv_rn(expf(__fsub_rn(__fdiv_rn(logit, temp), m)), s);
+}
+
+// Pass 1: per-row (max, sum exp) of x/T for the rows the acceptance test reads,
+// then (last CTA per sequence) the accept loop.  Rows per sequence: nP target
+// rows (lp[off .. K]) followed by K draft rows (lq[0 .. K-1]).
+__global__ void __launch_bounds__(kScanThreads)
+sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, int K, int V,
+                    int off, int nchunks, bool vec_ok, float tp, float tq,
+                    unsigned int* __restrict__ counters, float2* __restrict__ part,
+                    const int32_t* __restrict__ spec, const float* __restrict__ u_accept,
+                    SampleDecision* __restrict__ dec) {
+  __shared__ float redf[32];
+  __shared__ bool is_last;
+  __shared__ float2 stats[130];
+  const int nP = K + 1 - off, nR = nP + K;
+  const int b = blockIdx.y / nR, r = blockIdx.y % nR;
+  const bool is_p = r < nP;
+  const float* row = is_p ? lp + ((int64_t)b * (K + 1) + off + r) * V
+                          : lq + ((int64_t)b * K + (r - nP)) * V;
+  const float temp = is_p ? tp : tq;
+  int lo, hi;
+  chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
+  // One pass, online per thread: (m, s) with s = sum exp(v - m), v = x / T.
+  float m = -INFINITY, s = 0.f;
+  auto push = [&](float x) {
+    const float v = __fdiv_rn(x, temp);
+    if (v > m) { s = (m == -INFINITY ? 0.f : s * expf(__fsub_rn(m, v))) + 1.f; m = v; }
+    else s += expf(__fsub_rn(v, m));
+  };
+  if (vec_ok) {
+    const int nv = (hi - lo) >> 2;
+    const float4* p = reinterpret_cast<const float4*>(row + lo);
+    for (int i = threadIdx.x; i < nv; i += kScanThreads) {
+      float4 a = __ldg(p + i);
+      push(a.x); push(a.y); push(a.z); push(a.w);
+    }
+    for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) push(__ldg(row + j));
+  } else {
+    for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) push(__ldg(row + j));
+  }
+  const float M = block_reduce(m, redf, OpMax());
+  float sc = (m == -INFINITY) ? 0.f : s * expf(__fsub_rn(m, M));
+  sc = block_reduce(sc, redf, OpSum());
+  m = M;
+  s = sc;
+  if (threadIdx.x == 0) part[(int64_t)blockIdx.y * nchunks + blockIdx.x] = make_float2(m, s);
+
+  if (!last_block_of(&counters[b], (unsigned)(nR * nchunks), &is_last)) return;
+  // Fold chunk partials per row: M = max m_i, S = sum s_i * exp(m_i - M), chunk order.
+  for (int rr = threadIdx.x; rr < nR; rr += blockDim.x) {
+    const float2* pr = part + (int64_t)(b * nR + rr) * nchunks;
+    float M = -INFINITY;
+    for (int i = 0; i < nchunks; ++i) M = fmaxf(M, __ldcg(&pr[i].x));
+    float S = 0.f;
+    for (int i = 0; i < nchunks; ++i) {
+      float2 v = __ldcg(&pr[i]);
+      if (v.y > 0.f) S += v.y * expf(v.x - M);
+    }
+    stats[rr] = make_float2(M, S);
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  int acc = 0;
+  for (int j = 0; j < K; ++j) {
+    const int tok = spec[(int64_t)b * (K + 1) + j + 1];
+    const float2 pst = stats[j];  // target row j+off is stored at index j
+    const float2 qst = stats[nP + j];
+    const float pv = prob_of(__ldg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok), tp, pst.x, pst.y);
+    const float qv = prob_of(__ldg(lq + ((int64_t)b * K + j) * V + tok), tq, qst.x, qst.y);
+    const float ratio = fminf(1.0f, __fdiv_rn(pv, fmaxf(qv, 1e-12f)));
+    if (u_accept[(int64_t)b * K + j] < ratio) ++acc; else break;
+  }
+  SampleDecision d;
+  d.acc = acc;
+  d.bonus = (acc == K) ? 1 : 0;
+  d.prow = d.bonus ? K : acc + off;
+  d.qrow = d.bonus ? 0 : acc;
+  const float2 pst = stats[d.prow - off];
+  d.mp = pst.x; d.sp = pst.y;
+  if (!d.bonus) { const float2 q = stats[nP + acc]; d.mq = q.x; d.sq = q.y; } else { d.mq = 0.f; d.sq = 1.f; }
+  d.rsum = 1.f;
+  d.pad[0] = d.pad[1] = d.pad[2] = 0.f;
+  dec[b] = d;
+}
+
+// Pass 2: residual mass sum_v max(p_v - x q_v, 0) (skipped for bonus rows).
+__global__ void __launch_bounds__(kScanThreads)
+sample_residual_kernel(const float* __restrict__ lp, const float* __restrict__ lq, int K, int V,
+                       int nchunks, float tp, float tq, float sx, unsigned int* __restrict__ counters,
+                       float* __restrict__ part, SampleDecision* __restrict__ dec) {
+  __shared__ float redf[32];
+  __shared__ bool is_last;
+  const int b = blockIdx.y;
+  const SampleDecision d = dec[b];
+  if (d.bonus) return;  // uniform over the group: no CTA touches the counter
+  const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
+  const float* qrow = lq + ((int64_t)b * K + d.qrow) * V;
+  int lo, hi;
+  chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
+  float s = 0.f;
+  for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
+    const float p = prob_of(__ldg(prow + j), tp, d.mp, d.sp);
+    const float q = prob_of(__ldg(qrow + j), tq, d.mq, d.sq);
+    s += fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f);
+  }
+  s = block_reduce(s, redf, OpSum());
+  if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = s;
+  if (!last_block_of(&counters[b], (unsigned)nchunks, &is_last)) return;
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < nchunks; ++i) tot += __ldcg(&part[(int64_t)b * nchunks + i]);
+    dec[b].rsum = fmaxf(tot, 1e-12f);
+  }
+}
+
+// Pass 3: Gumbel-max categorical draw over log(r + 1e-12).
+__global__ void __launch_bounds__(kScanThreads)
+sample_draw_kernel(const float* __restrict__ lp, const float* __restrict__ lq,
+                   const float* __restrict__ u_gumbel, int K, int V, int nchunks, float tp, float tq,
+                   float sx, unsigned int* __restrict__ counters, unsigned long long* __restrict__ part,
+                   const SampleDecision* __restrict__ dec, int32_t* __restrict__ accept_until,
+                   int32_t* __restrict__ recovery, uint8_t* __restrict__ mask) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool is_last;
+  const int b = blockIdx.y;
+  const SampleDecision d = dec[b];
+  const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
+  const float* qrow = lq + ((int64_t)b * K + d.qrow) * V;
+  const float* urow = u_gumbel + (int64_t)b * V;
+  int lo, hi;
+  chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
+    const float p = prob_of(__ldg(prow + j), tp, d.mp, d.sp);
+    float r;
+    if (d.bonus) {
+      r = p;
+    } else {
+      const float q = prob_of(__ldg(qrow + j), tq, d.mq, d.sq);
+      r = __fdiv_rn(fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f), d.rsum);
+    }
+    const float g = -logf(-logf(__ldg(urow + j)));
+    const float score = __fadd_rn(logf(__fadd_rn(r, 1e-12f)), g);
+    if (score > best) { best = score; bidx = j; }
+  }
+  unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
+  if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = key;
+  if (!last_block_of(&counters[b], (unsigned)nchunks, &is_last)) return;
+  if (threadIdx.x == 0) {
+    unsigned long long k = 0ull;
+    for (int i = 0; i < nchunks; ++i) {
+      unsigned long long v = __ldcg(&part[(int64_t)b * nchunks + i]);
+      k = v > k ? v : k;
+    }
+    accept_until[b] = d.acc;
+    recovery[b] = (int32_t)argmax_key_index(k);
+    if (mask) {
+      mask[(int64_t)b * (K + 1)] = 0;
+      for (int j = 0; j < K; ++j) mask[(int64_t)b * (K + 1) + j + 1] = (j < d.acc) ? 1 : 0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- RNG fills
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  // SplitMix64 finaliser (Steele, Lea, Flood 2014).
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t i) {
+  const uint64_t h = mix64(seed ^ mix64(i));
+  return ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0,1), 24-bit grid
+}
+
+__global__ void uniform_fill_kernel(float* out, int64_t n, uint64_t seed, uint64_t offset) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = hash_uniform(seed, offset + (uint64_t)i);
+}
+
+template <typename T>
+__global__ void normal_fill_kernel(T* out, int64_t n, float std, uint64_t seed) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float u1 = hash_uniform(seed, 2 * (uint64_t)i);
+    const float u2 = hash_uniform(seed, 2 * (uint64_t)i + 1);
+    const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);  // Box-Muller
+    out[i] = from_f<T>(z * std);
+  }
+}
+
+}  // namespace
+}  // namespace ssd
+
+using namespace ssd;
+
+// ------------------------------------------------------------------ C ABI
+extern "C" size_t ssd_verify_greedy_workspace_size(int B, int K, int V) {
+  if (B <= 0 || K < 0 || V <= 0) return 0;
+  const int rows = B * (K + 1);
+  const int nch = scan_chunks(rows, V);
+  return align256(sizeof(unsigned int) * (size_t)rows) + sizeof(unsigned long long) * (size_t)rows * nch;
+}
+
+static int launch_greedy(cudaStream_t st, const float* x, int64_t ld, int rows, int kp1, int V,
+                         const int32_t* spec, int32_t* acc, int32_t* rec, uint8_t* mask, int32_t* tt,
+                         int32_t* amax, void* ws, size_t ws_bytes) {
+  const int nch = scan_chunks(rows, V);
+  const size_t need = align256(sizeof(unsigned int) * (size_t)rows) + sizeof(unsigned long long) * (size_t)rows * nch;
+  if (ws_bytes < need || ws == nullptr) return SSD_ERR_WORKSPACE;
+  unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
+  unsigned long long* part = reinterpret_cast<unsigned long long*>(
+      reinterpret_cast<char*>(ws) + align256(sizeof(unsigned int) * (size_t)rows));
+  const bool vec_ok = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  dim3 grid(nch, rows);
+  greedy_scan_kernel<<<grid, kScanThreads, 0, st>>>(x, ld, V, kp1, nch, vec_ok, counters, part, spec, acc,
+                                                     rec, mask, tt, amax);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+extern "C" int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t* speculations,
+                                 int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
+                                 int32_t* target_tokens, void* workspace, size_t workspace_bytes, int B,
+                                 int K, int V) {
+  if (B <= 0 || K < 0 || K > 63 || V <= 0 || !logits_p || !speculations || !accept_until || !recovery)
+    return SSD_ERR_INVALID;
+  if ((int64_t)B * (K + 1) > 65535) return SSD_ERR_UNSUPPORTED;
+  return launch_greedy((cudaStream_t)stream, logits_p, V, B * (K + 1), K + 1, V, speculations, accept_until,
+                       recovery, accepted_mask, target_tokens, nullptr, workspace, workspace_bytes);
+}
+
+extern "C" int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, int32_t* out,
+                               void* workspace, size_t workspace_bytes) {
+  if (rows <= 0 || rows > 65535 || V <= 0 || ld < V || !x || !out) return SSD_ERR_INVALID;
+  return launch_greedy((cudaStream_t)stream, x, ld, rows, 1, V, nullptr, nullptr, nullptr, nullptr, nullptr, out,
+                       workspace, workspace_bytes);
+}
+
+static void sample_layout(int B, int K, int V, int& nR, int& nch, size_t& off_part, size_t& off_dec,
+                          size_t& total) {
+  nR = 2 * K + 1;  // upper bound over both alignments
+  nch = scan_chunks(B * nR, V);
+  // the residual and draw passes scan B rows: give them the same chunk count
+  off_part = align256(sizeof(unsigned int) * (size_t)B * 3);
+  const size_t p1 = sizeof(float2) * (size_t)B * nR * nch;
+  const size_t p2 = sizeof(unsigned long long) * (size_t)B * scan_chunks(B, V);
+  off_dec = off_part + align256(p1 > p2 ? p1 : p2);
+  total = off_dec + align256(sizeof(SampleDecision) * (size_t)B);
+}
+
+extern "C" size_t ssd_verify_sample_workspace_size(int B, int K, int V) {
+  if (B <= 0 || K <= 0 || V <= 0) return 0;
+  int nR, nch;
+  size_t a, b, t;
+  sample_layout(B, K, V, nR, nch, a, b, t);
+  return t;
+}
+
+extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, const float* logits_q,
+                                 const int32_t* speculations, const float* u_accept, const float* u_gumbel,
+                                 float temperature_p, float temperature_q, float sampler_x, int alignment,
+                                 int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
+                                 void* workspace, size_t workspace_bytes, int B, int K, int V) {
+  if (B <= 0 || K <= 0 || K > 63 || V <= 0 || !logits_p || !logits_q || !speculations || !u_accept ||
+      !u_gumbel || !accept_until || !recovery)
+    return SSD_ERR_INVALID;
+  if (!(temperature_p > 0.f) || !(temperature_q > 0.f)) return SSD_ERR_INVALID;
+  if (alignment != SSD_ALIGN_REFERENCE && alignment != SSD_ALIGN_STANDARD) return SSD_ERR_INVALID;
+  int nR, nch;
+  size_t off_part, off_dec, total;
+  sample_layout(B, K, V, nR, nch, off_part, off_dec, total);
+  if (!workspace || workspace_bytes < total) return SSD_ERR_WORKSPACE;
+  const int off = alignment == SSD_ALIGN_REFERENCE ? 1 : 0;
+  const int rows = B * (2 * K + 1 - off);
+  if (rows > 65535) return SSD_ERR_UNSUPPORTED;
+  char* w = reinterpret_cast<char*>(workspace);
+  unsigned int* c0 = reinterpret_cast<unsigned int*>(w);
+  unsigned int* c1 = c0 + B;
+  unsigned int* c2 = c1 + B;
+  float2* part = reinterpret_cast<float2*>(w + off_part);
+  SampleDecision* dec = reinterpret_cast<SampleDecision*>(w + off_dec);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool vec_ok = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits_p) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(logits_q) & 15) == 0);
+  sample_stats_kernel<<<dim3(nch, rows), kScanThreads, 0, st>>>(logits_p, logits_q, K, V, off, nch, vec_ok,
+                                                                temperature_p, temperature_q, c0, part,
+                                                                speculations, u_accept, dec);
+  SSD_CHECK_LAUNCH();
+  const int nch_b = scan_chunks(B, V);
+  sample_residual_kernel<<<dim3(nch_b, B), kScanThreads, 0, st>>>(logits_p, logits_q, K, V, nch_b, temperature_p,
+                                                                  temperature_q, sampler_x, c1,
+                                                                  reinterpret_cast<float*>(part), dec);
+  SSD_CHECK_LAUNCH();
+  sample_draw_kernel<<<dim3(nch_b, B), kScanThreads, 0, st>>>(
+      logits_p, logits_q, u_gumbel, K, V, nch_b, temperature_p, temperature_q, sampler_x, c2,
+      reinterpret_cast<unsigned long long*>(part), dec, accept_until, recovery, accepted_mask);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+extern "C" int ssd_uniform_fill(ssd_stream_t stream, float* out, int64_t n, uint64_t seed, uint64_t offset) {
+  if (n < 0 || (n > 0 && !out)) return SSD_ERR_INVALID;
+  if (n == 0) return SSD_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  uniform_fill_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(out, n, seed, offset);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+extern "C" int ssd_normal_fill(ssd_stream_t stream, void* out, int dtype, int64_t n, float std, uint64_t seed) {
+  if (n < 0 || (n > 0 && !out)) return SSD_ERR_INVALID;
+  if (n == 0) return SSD_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == SSD_DTYPE_BF16)
+    normal_fill_kernel<bf16><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<bf16*>(out), n, std, seed);
+  else if (dtype == SSD_DTYPE_F32)
+    normal_fill_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<float*>(out), n, std, seed);
+  else
+    return SSD_ERR_INVALID;
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}

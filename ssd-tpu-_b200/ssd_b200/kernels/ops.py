@@ -1,0 +1,50 @@
+"""Thin wrappers over the fused forward ops of libssdverify.so (projections, norms, RoPE)."""
+
+from __future__ import annotations
+
+import torch
+
+from .._lib import (SSD_EPI_GEGLU, SSD_EPI_RESIDUAL, SSD_EPI_STORE, SSD_EPI_STORE_F32, check, dtype_code,
+                    lib, ptr, stream_ptr)
+from ..workspace import workspace
+
+EPILOGUES = {"store": SSD_EPI_STORE, "store_f32": SSD_EPI_STORE_F32, "residual": SSD_EPI_RESIDUAL,
+             "geglu": SSD_EPI_GEGLU}
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, epilogue: str = "store", out: torch.Tensor | None = None,
+           ws_key: str = "linear") -> torch.Tensor:
+    """epilogue(x[M,K] w[N,K]^T); ``residual`` accumulates into ``out`` in place."""
+    m, k = x.shape
+    n = w.shape[0]
+    epi = EPILOGUES[epilogue]
+    if out is None:
+        if epi == SSD_EPI_RESIDUAL:
+            raise ValueError("residual epilogue needs out=")
+        cols = n // 2 if epi == SSD_EPI_GEGLU else n
+        out = torch.empty((m, cols), dtype=torch.float32 if epi == SSD_EPI_STORE_F32 else x.dtype, device=x.device)
+    ws = workspace(x.device, ws_key, lib().ssd_linear_workspace_size(m, n, k))
+    check(lib().ssd_linear(stream_ptr(), ptr(x), ptr(w), dtype_code(w.dtype), ptr(out), epi, m, n, k, ptr(ws),
+                           ws.numel()), "ssd_linear")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    m, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    check(lib().ssd_rmsnorm(stream_ptr(), ptr(x), ptr(w), dtype_code(x.dtype), ptr(out), m, d, float(eps)),
+          "ssd_rmsnorm")
+    return out
+
+
+def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    m = tokens.numel()
+    v, d = table.shape
+    out = torch.empty((m, d), dtype=table.dtype, device=table.device) if out is None else out
+    check(lib().ssd_embed(stream_ptr(), ptr(tokens), ptr(table), dtype_code(table.dtype), ptr(out), m, d, v),
+          "ssd_embed")
+    return out
+
+
+def max_tokens_per_forward() -> int:
+    return int(lib().ssd_linear_max_m())

@@ -1,0 +1,101 @@
+"""GPU numerics: skinny projections (K3) with fused epilogues vs a plain fp32 reference."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle.gemma import bf16_round, gelu_tanh
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_close(got, exp, ulps=1.0, atol=1e-6):
+    """|got - exp| within `ulps` bf16 ulps of |exp| (fp32 accumulation order differs)."""
+    tol = np.abs(exp) * (2.0 ** -8) * ulps + atol
+    bad = np.abs(got - exp) > tol
+    assert not bad.any(), (np.abs(got - exp)[bad][:5], exp[bad][:5])
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 12288, 3072), (1, 3072, 4096), (5, 3072, 24576), (16, 1000, 512),
+                                   (7, 2048, 2048)])
+def test_store_bf16(cuda, m, n, k):
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(m * n + k)
+    x = torch.randn((m, k), device="cuda", generator=g).bfloat16()
+    w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).bfloat16()
+    y = linear(x, w, "store")
+    ref = (x.float() @ w.float().T).cpu().numpy()  # plain PyTorch fp32 reference
+    _bf16_close(y.float().cpu().numpy(), bf16_round(ref), ulps=1.0, atol=1e-3)
+
+
+def test_store_f32_logits(cuda):
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn((5, 3072), device="cuda", generator=g).bfloat16()
+    w = (0.005 * torch.randn((256000, 3072), device="cuda", generator=g)).bfloat16()
+    y = linear(x, w, "store_f32")
+    ref = x.float() @ w.float().T
+    assert y.dtype == torch.float32
+    torch.testing.assert_close(y, ref, rtol=1e-4, atol=1e-4)
+
+
+def test_residual_and_geglu(cuda):
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    m, d, f = 5, 3072, 24576
+    x = torch.randn((m, d), device="cuda", generator=g).bfloat16()
+    wgu = (torch.randn((2 * f, d), device="cuda", generator=g) / d ** 0.5).bfloat16()
+    a = linear(x, wgu, "geglu")
+    assert a.shape == (m, f)
+    acc = (x.float() @ wgu.float().T).cpu().numpy()
+    gate, up = bf16_round(acc[:, 0::2]), bf16_round(acc[:, 1::2])
+    exp = bf16_round(bf16_round(gelu_tanh(gate)) * up)
+    # the gate/up accumulators may round differently by one bf16 ulp; compare loosely then on average
+    got = a.float().cpu().numpy()
+    assert np.abs(got - exp).max() < 0.05
+    assert np.mean(got == exp) > 0.97
+    wd = (torch.randn((d, f), device="cuda", generator=g) / f ** 0.5).bfloat16()
+    res = torch.randn((m, d), device="cuda", generator=g).bfloat16()
+    res0 = res.clone()
+    linear(a, wd, "residual", out=res)
+    acc2 = bf16_round((a.float() @ wd.float().T).cpu().numpy())
+    exp2 = bf16_round(res0.float().cpu().numpy() + acc2)
+    _bf16_close(res.float().cpu().numpy(), exp2, ulps=2.0, atol=2e-2)
+
+
+@pytest.mark.parametrize("n,k", [(12288, 3072), (3072, 24576), (256000, 3072)])
+def test_rows_are_batch_invariant(cuda, n, k):
+    """Row i of an M-row projection equals the same row projected alone, bit for bit."""
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(n)
+    x = torch.randn((5, k), device="cuda", generator=g).bfloat16()
+    w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).bfloat16()
+    full = linear(x, w, "store_f32")
+    for i in (0, 3, 4):
+        one = linear(x[i:i + 1].contiguous(), w, "store_f32")
+        assert torch.equal(one[0], full[i])
+
+
+def test_fp32_weights_toy(cuda):
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn((5, 256), device="cuda", generator=g)
+    w = torch.randn((1024, 256), device="cuda", generator=g) * 0.06
+    y = linear(x, w, "store")
+    torch.testing.assert_close(y, x @ w.T, rtol=1e-5, atol=1e-5)

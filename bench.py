@@ -49,6 +49,11 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--e2e-new-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["linear", "attention", "verify", "sample"], default=None,
+                    help="time one kernel family on its op-level workload instead of the decode loop")
+    ap.add_argument("--m", type=int, default=5)
+    ap.add_argument("--n", type=int, default=49152)
+    ap.add_argument("--kdim", type=int, default=3072)
     return ap.parse_args()
 
 
@@ -213,13 +218,14 @@ def run_ours(args):
     total_steps = args.warmup + args.steps
     max_seq = args.prompt_len + (total_steps + 2) * (k + 1) + 32
     max_seq = max(max_seq, args.prompt_len + args.e2e_new_tokens * (k + 1) + 32)
-    dec = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq)
+    timer = ProjectionTimer(capacity=4 * st_.num_layers + 8)
+    dec = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq, timer=timer)
     dec.start(prompt)
     for _ in range(args.warmup):
         dec.step()
-    timer = ProjectionTimer(capacity=4 * st_.num_layers + 8)
+    timer.reset()
     stream = torch.cuda.current_stream()
-    vev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    verify_ms = []
     clocks = ClockSampler(local)
     ctx_before = dec.t.n
     if world > 1:
@@ -228,22 +234,23 @@ def run_ours(args):
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    torch.cuda.nvtx.range_push("timed")
     tokens = 0
     accepted = 0
     ctx_sum = 0
     for i in range(args.steps):
         ctx_sum += dec.t.n + k + 1
-        new = dec.step(events=vev[i], prof=timer)
-        timer.flush()
+        new = dec.step()
+        verify_ms.append(dec.last_verify_ms)
         tokens += len(new)
         accepted += dec.last_accept
+    torch.cuda.nvtx.range_pop()
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    verify_ms = [a.elapsed_time(b) for a, b in vev]
     # max time / total tokens over ranks
     t = torch.tensor([ms, float(tokens)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -348,8 +355,89 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------- op-level legs
+def run_op(args):
+    """Op-level workloads (one JSON line each): the projection streamer on one shape, the
+    paged verify attention (B=8, ctx U[512,4096], 16x256 heads, 5 queries) and the acceptance
+    kernels (B=8, K=4, V=256000, logits ~ N(0, 3^2)).  Inputs exceed L2 or are rotated so
+    every timed launch reads from HBM."""
+    import numpy as np
+    import torch
+
+    from ssd_b200.algorithm.verify import verify_greedy, verify_sample
+    from ssd_b200.kernels.kv_cache import KVCacheState, paged_verify_attention
+    from ssd_b200.kernels.ops import linear
+
+    torch.cuda.set_device(0)
+    hbm, kind = peaks()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    reps = max(args.steps, 1)
+    st = torch.cuda.current_stream()
+
+    def timed(fn, nrot):
+        for i in range(args.warmup):
+            fn(i % nrot)
+        torch.cuda.synchronize()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for i in range(reps):
+            fn(i % nrot)
+        b_.record(st)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b_) / reps
+
+    if args.op == "linear":
+        m, n, k = args.m, args.n, args.kdim
+        nrot = max(1, int(np.ceil(512e6 / (n * k * 2))))  # rotate weights over > 4x L2
+        ws = [(torch.randn((n, k), device="cuda", generator=g) * 0.02).bfloat16() for _ in range(nrot)]
+        x = torch.randn((m, k), device="cuda", generator=g).bfloat16()
+        y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        ms = timed(lambda i: linear(x, ws[i], "store", out=y), nrot)
+        nbytes = n * k * 2 + m * k * 2 + m * n * 2
+        line = {"op": "linear", "m": m, "n": n, "k": k, "us": ms * 1000, "gbs": nbytes / ms / 1e6,
+                "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind, "weights_rotated": nrot}
+    elif args.op == "attention":
+        b, t, hq, hkv, d, bs = 8, 5, 16, 16, 256, 16
+        rng = np.random.default_rng(0)
+        ctx = rng.integers(512, 4097, b)
+        mb = int((ctx.max() + bs - 1) // bs)
+        nb = b * mb
+        cache = KVCacheState.allocate(1, nb, bs, hkv, d)
+        cache.pages.normal_(generator=g)
+        perm = torch.randperm(nb, generator=torch.Generator().manual_seed(0)).int().view(b, mb).cuda()
+        q = torch.randn((b, t, hq, d), device="cuda", generator=g).bfloat16()
+        sl = torch.tensor(ctx, dtype=torch.int32, device="cuda")
+        out = torch.empty_like(q)
+        ms = timed(lambda i: paged_verify_attention(q, cache, 0, perm, sl, max_seq_len=mb * bs, out=out), 1)
+        nbytes = int(ctx.sum()) * hkv * d * 2 * 2 + 2 * q.numel() * 2
+        line = {"op": "paged_attention", "B": b, "ctx": ctx.tolist(), "us": ms * 1000, "gbs": nbytes / ms / 1e6,
+                "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind, "kv_bytes": nbytes,
+                "note": "KV pages (302 MB expected) exceed L2; one layer"}
+    else:
+        b, k, v = 8, 4, 256000
+        nrot = 4
+        lps = [3.0 * torch.randn((b, k + 1, v), device="cuda", generator=g) for _ in range(nrot)]
+        spec = torch.randint(0, v, (b, k + 1), device="cuda", generator=g, dtype=torch.int32)
+        if args.op == "verify":
+            ms = timed(lambda i: verify_greedy(lps[i], spec), nrot)
+            nbytes = b * (k + 1) * v * 4
+        else:
+            lqs = [3.0 * torch.randn((b, k, v), device="cuda", generator=g) for _ in range(nrot)]
+            ua = torch.rand((b, k), device="cuda", generator=g)
+            ug = torch.rand((b, v), device="cuda", generator=g).clamp_(1e-7, 1 - 1e-7)
+            ms = timed(lambda i: verify_sample(lps[i], lqs[i], spec, (ua, ug)), nrot)
+            nbytes = b * k * v * 4 + b * k * v * 4 + b * v * 4
+        line = {"op": "verify_" + ("greedy" if args.op == "verify" else "sample"), "B": b, "K": k, "V": v,
+                "us": ms * 1000, "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind,
+                "algorithmic_bytes": nbytes}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.op is not None:
+        run_op(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

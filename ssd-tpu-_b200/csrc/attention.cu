@@ -27,7 +27,7 @@ namespace {
 constexpr int kAttnThreads = 256;
 constexpr int kRows = 16;      // query rows per CTA
 constexpr int kTile = 32;      // positions per smem tile
-constexpr int kChunk = 256;    // positions per split (fixed => batch invariant)
+constexpr int kChunk = 128;    // positions per split (fixed => batch invariant)
 constexpr int kParts = 8;      // dim partitions for q.k (one warp each)
 
 template <typename T> struct Vec16;
@@ -68,6 +68,59 @@ struct RowInfo {
   int nrows;        // rows in this CTA
   int pos[kRows];   // absolute position of each row's token (-1 = padding row)
 };
+
+// Fold the split partials of one (sequence, KV head, row group) in split order.
+// Only splits that start before seq_len can hold keys; the per-row weights
+// w_s = exp(m_s - M) and the normaliser L are computed once per row by one warp
+// (lane-strided over splits, xor-tree sums: adding an empty split's exact zeros
+// leaves them unchanged, so the result does not depend on how many empty splits
+// exist), then every output element sums w_s * o_s in split order with
+// independent loads in flight.
+template <typename KV, int D>
+__device__ __forceinline__ void attention_fold(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
+                                               KV* __restrict__ out, int64_t grp_id, int nsplit, int seq_len,
+                                               int nrows, int row0, int G, int T, int hq, int kvh, int b,
+                                               float* wsm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ns = max(1, min(nsplit, (seq_len + kChunk - 1) / kChunk));
+  __shared__ float inv_l[kRows];
+  // wsm: [kRows][ns] weights (ns <= 256 fits the score-partial region)
+  for (int r = warp; r < nrows; r += kAttnThreads / 32) {
+    const int64_t rb = grp_id * nsplit * kRows + r;
+    float mloc = -INFINITY;
+    for (int s = lane; s < ns; s += 32) mloc = fmaxf(mloc, __ldcg(&ws_ml[rb + (int64_t)s * kRows]).x);
+    const float M = warp_max(mloc);
+    float lsum = 0.f;
+    for (int s = lane; s < ns; s += 32) {
+      const float2 ml = __ldcg(&ws_ml[rb + (int64_t)s * kRows]);
+      const float w = (ml.x == -INFINITY || M == -INFINITY) ? 0.f : expf(ml.x - M);
+      wsm[r * 256 + s] = w;
+      lsum += ml.y * w;
+    }
+    const float L = warp_sum(lsum);
+    if (lane == 0) inv_l[r] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < nrows * D; i += kAttnThreads) {
+    const int r = i / D, d = i % D;
+    const int64_t rb = grp_id * nsplit * kRows + r;
+    const float* wr = wsm + r * 256;
+    float O = 0.f;
+    int s = 0;
+    for (; s + 4 <= ns; s += 4) {
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = wr[s + j] != 0.f ? __ldcg(&ws_o[(rb + (int64_t)(s + j) * kRows) * D + d]) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) O += wr[s + j] * v[j];
+    }
+    for (; s < ns; ++s) O += wr[s] != 0.f ? wr[s] * __ldcg(&ws_o[(rb + (int64_t)s * kRows) * D + d]) : 0.f;
+    const float L = inv_l[r];
+    const float res = (L > 0.f) ? O / L : 0.f;
+    const int gr = row0 + r, t = gr / G, g = gr % G;
+    out[(((int64_t)b * T + t) * hq + kvh * G + g) * D + d] = from_f<KV>(res);
+  }
+}
 
 template <typename KV, int D>
 __global__ void __launch_bounds__(kAttnThreads)
@@ -119,6 +172,16 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
   const int k_begin = split * kChunk;
   // positions beyond the table's reach are never read (guards a seq_len larger than the pages)
   const int k_end = min(min(min(k_begin + kChunk, kmax), seq_len), max_blocks * block_size);
+
+  const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
+  if (k_end <= k_begin) {
+    // No key of this split is visible to any row: mark the rows empty (m = -inf,
+    // l = 0; the fold then never reads their o) and take the ticket.
+    if (tid < nrows) ws_ml[(grp_id * nsplit + split) * kRows + tid] = make_float2(-INFINITY, 0.f);
+    if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+    attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, spart);
+    return;
+  }
 
   // q rows -> fp32 smem (zeros for padding rows)
   for (int i = tid; i < kRows * D; i += kAttnThreads) {
@@ -245,7 +308,6 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
   }
 
   // ---- partials: ws_o[(((b*hkv + kvh)*row_groups + rg)*nsplit + split)*kRows + r][D]
-  const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
   const int64_t base = (grp_id * nsplit + split) * kRows;
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
@@ -259,26 +321,7 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
 
   if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
 
-  // ---- fold splits in order, normalise, store
-  for (int i = tid; i < nrows * D; i += kAttnThreads) {
-    const int r = i / D, d = i % D;
-    const int64_t rb = grp_id * nsplit * kRows + r;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(&ws_ml[rb + (int64_t)s * kRows]).x);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < nsplit; ++s) {
-        const float2 ml = __ldcg(&ws_ml[rb + (int64_t)s * kRows]);
-        if (ml.x == -INFINITY) continue;
-        const float w = expf(ml.x - M);
-        L += ml.y * w;
-        O += __ldcg(&ws_o[(rb + (int64_t)s * kRows) * D + d]) * w;
-      }
-    }
-    const float res = (L > 0.f) ? O / L : 0.f;
-    const int gr = row0 + r, t = gr / G, g = gr % G;
-    out[(((int64_t)b * T + t) * hq + kvh * G + g) * D + d] = from_f<KV>(res);
-  }
+  attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, spart);
 }
 
 // ---------------------------------------------------------------- K2
@@ -303,13 +346,14 @@ __global__ void kv_write_kernel(KV* __restrict__ pages, int num_layers, int num_
 }
 
 // RoPE on q and k of a fused qkv row, q -> q_out, k (rotated) and v -> pages.
+// grid (Hq + Hkv, T, B): one CTA per head of one token, one thread per rotation pair.
 template <typename KV>
 __global__ void rope_kv_write_kernel(const KV* __restrict__ qkv, KV* __restrict__ q_out, KV* __restrict__ pages,
                                      int num_layers, int num_blocks, int block_size, int hq, int hkv, int D,
                                      int layer, const int32_t* __restrict__ block_tables, int max_blocks,
                                      const int32_t* __restrict__ positions, const float* __restrict__ cos_t,
                                      const float* __restrict__ sin_t, int rope_max_pos, int T) {
-  const int b = blockIdx.y, t = blockIdx.x;
+  const int h = blockIdx.x, t = blockIdx.y, b = blockIdx.z;
   const int64_t m = (int64_t)b * T + t;
   const int p = positions[m];
   const int half = D / 2;
@@ -320,18 +364,16 @@ __global__ void rope_kv_write_kernel(const KV* __restrict__ qkv, KV* __restrict_
   const float* sr = sin_t + (int64_t)pc * half;
   const int64_t plane = (int64_t)num_layers * num_blocks * block_size * hkv * D;
   KV* dst = nullptr;
-  if (p >= 0 && p / block_size < max_blocks) {
+  if (h >= hq && p >= 0 && p / block_size < max_blocks) {
     const int blk = block_tables[(int64_t)b * max_blocks + p / block_size];
     if ((unsigned)blk < (unsigned)num_blocks)
       dst = pages + (((int64_t)layer * num_blocks + blk) * block_size + p % block_size) * hkv * D;
   }
-  // rotation pairs: (head, i) with i < D/2, for the hq q heads then the hkv k heads
-  for (int idx = threadIdx.x; idx < (hq + hkv) * half; idx += blockDim.x) {
-    const int h = idx / half, i = idx % half;
-    const KV* src = row + h * D;
+  const KV* src = row + h * D;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const float x1 = to_f(src[i]), x2 = to_f(src[i + half]);
     const float c = cr[i], s = sr[i];
-    // written as separate products so the oracle's float32 expression matches
+    // separate products, as the oracle's float32 expression evaluates them
     const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
     const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     if (h < hq) {
@@ -344,9 +386,10 @@ __global__ void rope_kv_write_kernel(const KV* __restrict__ qkv, KV* __restrict_
       ko[i + half] = from_f<KV>(y2);
     }
   }
-  if (dst) {
-    const KV* vsrc = row + (hq + hkv) * D;
-    for (int i = threadIdx.x; i < hkv * D; i += blockDim.x) dst[plane + i] = vsrc[i];
+  if (dst) {  // the matching V head
+    const KV* vsrc = row + (hq + hkv + (h - hq)) * D;
+    KV* vo = dst + plane + (h - hq) * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) vo[i] = vsrc[i];
   }
 }
 
@@ -354,7 +397,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct AttnLayout {
   int row_groups, nsplit;
-  size_t off_ml, off_cnt, total;
+  size_t groups, off_cnt, off_o, off_ml, total;
 };
 
 inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_len) {
@@ -362,12 +405,14 @@ inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_
   const int G = hq / hkv;
   L.row_groups = (G * T + kRows - 1) / kRows;
   L.nsplit = (max_seq_len + kChunk - 1) / kChunk;
-  if (L.nsplit < 1) L.nsplit = 1;
+  if (L.nsplit < 1) L.nsplit = 1;  // <= 256 (checked by the caller): the fold keeps one weight per split
   const size_t groups = (size_t)B * hkv * L.row_groups;
   const size_t rows = groups * L.nsplit * kRows;
-  L.off_ml = align256(sizeof(float) * rows * D);
-  L.off_cnt = L.off_ml + align256(sizeof(float2) * rows);
-  L.total = L.off_cnt + align256(sizeof(unsigned int) * groups);
+  L.groups = groups;
+  L.off_cnt = 0;
+  L.off_o = kCounterBytes;
+  L.off_ml = L.off_o + align256(sizeof(float) * rows * D);
+  L.total = L.off_ml + align256(sizeof(float2) * rows);
   return L;
 }
 
@@ -385,7 +430,7 @@ int launch_attention(cudaStream_t st, const void* q, const void* pages, int num_
   kern<<<grid, kAttnThreads, S::total, st>>>(
       reinterpret_cast<const KV*>(q), reinterpret_cast<const KV*>(pages), num_layers, num_blocks, block_size, hkv,
       layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<KV*>(out), scale, T, hq, L.row_groups,
-      L.nsplit, reinterpret_cast<float*>(w), reinterpret_cast<float2*>(w + L.off_ml),
+      L.nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
       reinterpret_cast<unsigned int*>(w + L.off_cnt));
   SSD_CHECK_LAUNCH();
   return SSD_OK;
@@ -414,10 +459,12 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
       !block_tables || !seq_lens)
     return SSD_ERR_INVALID;
   if ((int64_t)max_blocks * block_size < max_seq_len) return SSD_ERR_INVALID;
+  if (max_seq_len > 256 * kChunk) return SSD_ERR_UNSUPPORTED;  // 32768 positions
   if (B > 65535 || (int64_t)num_kv_heads * ((num_heads / num_kv_heads * T + kRows - 1) / kRows) > 65535)
     return SSD_ERR_UNSUPPORTED;
   const AttnLayout L = attn_layout(B, T, num_heads, num_kv_heads, head_dim, max_seq_len);
   if (!workspace || workspace_bytes < L.total) return SSD_ERR_WORKSPACE;
+  if (L.groups > (size_t)kCounterCap) return SSD_ERR_UNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
 #define SSD_ATTN_CASE(KVT, DD)                                                                                  \
   return launch_attention<KVT, DD>(st, q, pages, num_layers, num_blocks, block_size, num_kv_heads, layer,       \
@@ -467,16 +514,17 @@ extern "C" int ssd_rope_kv_write(ssd_stream_t stream, const void* qkv, void* q_o
   if (B <= 0 || T <= 0 || layer < 0 || layer >= num_layers || head_dim % 2 || !qkv || !q_out || !pages ||
       !block_tables || !positions || !rope_cos || !rope_sin || rope_max_pos <= 0)
     return SSD_ERR_INVALID;
-  if (B > 65535) return SSD_ERR_UNSUPPORTED;
-  dim3 grid(T, B);
+  if (B > 65535 || T > 65535) return SSD_ERR_UNSUPPORTED;
+  dim3 grid(num_heads + num_kv_heads, T, B);
+  const int threads = head_dim / 2 < 32 ? 32 : (head_dim / 2 > 256 ? 256 : head_dim / 2);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == SSD_DTYPE_BF16)
-    rope_kv_write_kernel<bf16><<<grid, 256, 0, st>>>(
+    rope_kv_write_kernel<bf16><<<grid, threads, 0, st>>>(
         reinterpret_cast<const bf16*>(qkv), reinterpret_cast<bf16*>(q_out), reinterpret_cast<bf16*>(pages),
         num_layers, num_blocks, block_size, num_heads, num_kv_heads, head_dim, layer, block_tables, max_blocks,
         positions, rope_cos, rope_sin, rope_max_pos, T);
   else if (dtype == SSD_DTYPE_F32)
-    rope_kv_write_kernel<float><<<grid, 256, 0, st>>>(
+    rope_kv_write_kernel<float><<<grid, threads, 0, st>>>(
         reinterpret_cast<const float*>(qkv), reinterpret_cast<float*>(q_out), reinterpret_cast<float*>(pages),
         num_layers, num_blocks, block_size, num_heads, num_kv_heads, head_dim, layer, block_tables, max_blocks,
         positions, rope_cos, rope_sin, rope_max_pos, T);

@@ -106,6 +106,13 @@ __device__ __forceinline__ bool last_block_of(unsigned int* counter, unsigned in
   return last;
 }
 
+// Every workspace starts with a fixed-size region of ticket counters.  It is the
+// only part of a workspace that must hold zeros between calls, and because its
+// size does not depend on the call's shape, calls of different shapes can share
+// one workspace: their partial-result regions never overlap any counter.
+constexpr int kCounterCap = 16384;
+constexpr size_t kCounterBytes = sizeof(unsigned int) * kCounterCap;
+
 // 16-byte aligned vector of 8 bf16 values.
 struct alignas(16) bf16x8 { __nv_bfloat162 h[4]; };
 

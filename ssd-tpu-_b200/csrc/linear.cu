@@ -165,7 +165,7 @@ LinearPlan plan_linear_cc(int N, int K, int elem_bytes) {
 size_t linear_cc_workspace(int M, int N, int K, int elem_bytes) {
   const LinearPlan p = plan_linear_cc(N, K, elem_bytes);
   if (p.splits == 1) return 256;
-  return align_up256(sizeof(float) * (size_t)p.splits * M * N) + align_up256(sizeof(unsigned int) * p.tiles_max);
+  return kCounterBytes + align_up256(sizeof(float) * (size_t)p.splits * M * N);
 }
 
 template <typename T, int MMAX, int ROWS>
@@ -174,12 +174,12 @@ static int launch_cc(cudaStream_t st, const void* x, const void* w, void* y, int
   const int tiles = (N + kWarps * ROWS - 1) / (kWarps * ROWS);
   const size_t smem = sizeof(T) * (size_t)M * p.kc;
   auto kern = linear_cc_kernel<T, MMAX, ROWS>;
-  if (smem > 48 * 1024 &&
+  // opt in whenever the dynamic part alone comes near the 48 KB default (static smem adds to it)
+  if (smem > 32 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SSD_ERR_LAUNCH;
-  float* part = reinterpret_cast<float*>(ws);
-  unsigned int* counters = reinterpret_cast<unsigned int*>(
-      reinterpret_cast<char*>(ws) + align_up256(sizeof(float) * (size_t)p.splits * M * N));
+  unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
   kern<<<dim3(tiles, p.splits), kLinThreads, smem, st>>>(reinterpret_cast<const T*>(x), reinterpret_cast<const T*>(w),
                                                          y, epi, M, N, K, p.splits, p.kc, part, counters);
   SSD_CHECK_LAUNCH();
@@ -189,9 +189,11 @@ static int launch_cc(cudaStream_t st, const void* x, const void* w, void* y, int
 template <typename T>
 int linear_cc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
               size_t ws_bytes) {
+  if (M > 16) return SSD_ERR_UNSUPPORTED;
   const LinearPlan p = plan_linear_cc(N, K, sizeof(T));
   if (p.splits > 1 && (!ws || ws_bytes < linear_cc_workspace(M, N, K, sizeof(T)))) return SSD_ERR_WORKSPACE;
   if (sizeof(T) * (size_t)M * p.kc > 200 * 1024) return SSD_ERR_UNSUPPORTED;
+  if (p.splits > 1 && p.tiles_max > kCounterCap) return SSD_ERR_UNSUPPORTED;
   if (M <= 1) return launch_cc<T, 1, 8>(st, x, w, y, epi, M, N, K, p, ws);
   if (M <= 2) return launch_cc<T, 2, 8>(st, x, w, y, epi, M, N, K, p, ws);
   if (M <= 4) return launch_cc<T, 4, 8>(st, x, w, y, epi, M, N, K, p, ws);

@@ -1,10 +1,500 @@
-// tcgen05 weight-streaming projection (bf16) — placeholder until the kernel lands.
+// K3 on the 5th-generation tensor cores: y = epilogue(x[M,K] w[N,K]^T), bf16 in,
+// fp32 accumulation in TMEM, for M <= 256 token rows.
+//
+// The verify forward is a weight stream (M = k+1 = 5 rows against every weight
+// byte), so the kernel is built to keep HBM busy, not the tensor pipe:
+//   * swap-AB: the weight tile is the UMMA A operand (M_mma = 128 weight rows),
+//     the token rows are B (N_mma = MP = M rounded up to 16); D[128 x MP] fp32
+//     lives in TMEM, double-buffered so one tile's epilogue overlaps the next
+//     tile's loads;
+//   * persistent stream-K: one CTA per SM walks a contiguous range of
+//     (tile, 64-wide k-block) units, so every SM streams the same number of
+//     weight bytes whatever N and K are;
+//   * warp 0 issues TMA loads of 128x64 weight blocks and MPx64 token blocks
+//     (SWIZZLE_128B, no multicast) into a STAGES-deep ring of shared memory;
+//     warp 1 (one thread) issues tcgen05.mma and commits each stage back to the
+//     producer; warps 2-5 read the accumulator with tcgen05.ld and run the fused
+//     epilogue (store / fp32 store / residual add / GeGLU).
+//   * a tile cut by a CTA boundary is finished by its last-arriving contributor
+//     (atomic ticket), which sums the fp32 partials in CTA (= K) order, so the
+//     result is deterministic and, because the unit split depends on (N, K) and
+//     the SM count only, independent of M.
+// Every mbarrier wait is bounded: on timeout the kernel records an error code,
+// stops issuing work, drains what it issued and releases its TMEM.
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+
 #include "linear.cuh"
 
 namespace ssd {
-bool linear_tc_supported(int, int, int) { return false; }
-size_t linear_tc_workspace(int, int, int) { return 0; }
-int linear_tc(cudaStream_t, const void*, const void*, void*, int, int, int, int, void*, size_t) {
-  return SSD_ERR_UNSUPPORTED;
+namespace tc {
+
+constexpr int BM = 128;       // weight rows per tile (UMMA M)
+constexpr int BK = 64;        // bf16 per k-block: one 128-byte swizzle row
+constexpr int kThreads = 192; // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
+constexpr int kEpiThreads = 128;
+constexpr uint32_t kWaitLimit = 1u << 24;  // polls before a wait gives up (~seconds)
+
+struct Params {
+  void* y;
+  int epi, M, N, K;
+  int KB;        // k-blocks per tile
+  int U;         // total units = tiles * KB
+  int base, rem; // units per CTA; the first `rem` CTAs take one more
+  float* part;   // [grid][2][M][BM] partial tiles
+  unsigned int* counters;  // per tile (self-resetting)
+  unsigned int* err;       // error word
+};
+
+__host__ __device__ inline int unit_begin(const Params& p, int c) { return c * p.base + (c < p.rem ? c : p.rem); }
+__device__ inline int cta_of_unit(const Params& p, int u) {
+  const int big = p.rem * (p.base + 1);
+  return u < big ? u / (p.base + 1) : p.rem + (u - big) / p.base;
 }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) { return (uint32_t)__cvta_generic_to_shared(ptr); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false when the CTA has been told to abort or when the
+// poll budget runs out (then it raises the abort flag and records `code`).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             unsigned int* err, unsigned int code) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicExch(err, code);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 TMEM lanes x 16 fp32 columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major, M = 128, N = MP.
+template <int MP>
+__host__ __device__ constexpr uint32_t idesc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MP >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int MP>
+struct Cfg {
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = MP * BK * 2;
+  static constexpr uint32_t STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = MP <= 16 ? 10 : MP <= 32 ? 9 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
+  static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;
+  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int MP>
+__global__ void __launch_bounds__(kThreads, 1)
+linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                 const Params p) {
+  using C = Cfg<MP>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + S * C::STAGE;
+  auto full = [&](int s) { return bars + 8u * s; };
+  auto empty = [&](int s) { return bars + 8u * (S + s); };
+  auto accf = [&](int b) { return bars + 8u * (2 * S + b); };
+  auto acce = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * C::STAGE + 8 * (2 * S + 4));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const int u0 = unit_begin(p, cta), u1 = unit_begin(p, cta + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf(b), 1);
+      mbar_init(acce(b), kEpiThreads);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int u = u0; u < u1; ++u) {
+        const int tile = u / p.KB, kb = u - tile * p.KB;
+        if (!wait_bounded(empty(stage), phase ^ 1u, abort_flag, p.err, 1)) break;
+        mbar_expect_tx(full(stage), C::STAGE);
+        const uint32_t dst = base + stage * C::STAGE;
+        tma_load_2d(dst, &wmap, full(stage), kb * BK, tile * BM);
+        tma_load_2d(dst + C::A_BYTES, &xmap, full(stage), kb * BK, 0);
+        ++issued;
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+      if (*abort_flag) {
+        // drain: wait (bounded, ignoring the abort flag) for the loads still in flight
+        for (int i = 0; i < S && i < issued; ++i) {
+          if (--stage < 0) { stage = S - 1; phase ^= 1u; }
+          for (uint32_t t = 0; t < kWaitLimit && !mbar_try_wait(full(stage), phase); ++t) {}
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16<MP>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int seg = 0;
+      int u = u0;
+      bool ok = true;
+      while (ok && u < u1) {
+        const int tile = u / p.KB;
+        const int seg_end = min(u1, (tile + 1) * p.KB);
+        const int buf = seg & 1;
+        const uint32_t use = (uint32_t)(seg >> 1);
+        if (!wait_bounded(acce(buf), (use & 1u) ^ 1u, abort_flag, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t dcol = tmem + (uint32_t)(buf * MP);
+        bool first = true;
+        for (; u < seg_end; ++u) {
+          if (!wait_bounded(full(stage), phase, abort_flag, p.err, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = base + stage * C::STAGE;
+          const uint64_t ad = sw128_desc(a), bd = sw128_desc(a + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // +32 bytes along K inside the swizzle row
+            umma_bf16(dcol, ad + 2 * k, bd + 2 * k, idesc, (first && k == 0) ? 0u : 1u);
+          first = false;
+          umma_commit(empty(stage));
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(accf(buf));
+        ++seg;
+      }
+      if (!ok || *abort_flag) {
+        // let every issued MMA retire before TMEM is released: commit to an
+        // accumulator barrier nobody else waits on any more and wait for it.
+        const int buf = seg & 1;
+        umma_commit(accf(buf));
+        const uint32_t par = (uint32_t)((seg >> 1) & 1);
+        for (uint32_t t = 0; t < kWaitLimit && !mbar_try_wait(accf(buf), par); ++t) {}
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may read
+    const int row = q * 32 + lane;
+    int seg = 0;
+    int u = u0;
+    const int first_tile = u0 / p.KB;
+    while (u < u1) {
+      const int tile = u / p.KB;
+      const int kb_begin = u - tile * p.KB;
+      const int seg_end = min(u1, (tile + 1) * p.KB);
+      const int kb_end = seg_end - tile * p.KB;
+      u = seg_end;
+      const int buf = seg & 1;
+      const uint32_t use = (uint32_t)(seg >> 1);
+      ++seg;
+      if (!wait_bounded(accf(buf), use & 1u, abort_flag, p.err, 4)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * MP);
+      const int n = tile * BM + row;
+      const bool whole = (kb_begin == 0 && kb_end == p.KB);
+      float* mine = p.part + ((size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.M) * BM;
+#pragma unroll 1
+      for (int c0 = 0; c0 < MP; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+        tmem_ld_wait();
+        if (c0 >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = c0 + j;
+          const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
+          if (m >= p.M) continue;
+          if (whole) {
+            if (n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1)))
+              epilogue_store<bf16>(p.epi, p.y, p.N, m, n, v[j], up);
+          } else {
+            mine[(size_t)m * BM + row] = v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce(buf));
+      if (whole) continue;
+      // ---- split tile: ticket, then the last contributor folds all partials in K order
+      __threadfence();
+      epi_bar();
+      const int c_first = cta_of_unit(p, tile * p.KB);
+      const int c_last = cta_of_unit(p, tile * p.KB + p.KB - 1);
+      if (threadIdx.x == 64) {
+        const unsigned int prev = atomicAdd(&p.counters[tile], 1u);
+        const bool last = prev == (unsigned int)(c_last - c_first);
+        if (last) atomicExch(&p.counters[tile], 0u);
+        *last_flag = last ? 1 : 0;
+      }
+      epi_bar();
+      const bool last = *last_flag != 0;
+      epi_bar();  // everyone has read the flag before the next tile may rewrite it
+      if (!last) continue;
+      __threadfence();
+      // Fold the contributors in CTA (= K) order.  Rows are taken 16 at a time and
+      // contributors 4 at a time so up to 64 independent L2 loads are in flight
+      // per thread; the summation order per output stays c_first .. c_last.
+      for (int m0 = 0; m0 < p.M; m0 += 16) {
+        const int mn = min(16, p.M - m0);
+        float s[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) s[i] = 0.f;
+        for (int c = c_first; c <= c_last; c += 4) {
+          float v[4][16];
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int ci = c + cc;
+            const int e = (ci <= c_last && tile == unit_begin(p, ci) / p.KB) ? 0 : 1;
+            const float* src = p.part + ((size_t)(ci * 2 + e) * p.M + m0) * BM + row;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[cc][i] = (ci <= c_last && i < mn) ? __ldcg(src + (size_t)i * BM) : 0.f;
+          }
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) s[i] += v[cc][i];
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float up = __shfl_down_sync(0xffffffffu, s[i], 1);
+          if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1)))
+            epilogue_store<bf16>(p.epi, p.y, p.N, m0 + i, n, s[i], up);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(f);
+  });
+  return fn;
+}
+
+// rows x K bf16 row-major, box = box_rows x 64, 128-byte swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_rows) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct MapKey {
+  const void* p;
+  int n, k;
+  bool operator==(const MapKey& o) const { return p == o.p && n == o.n && k == o.k; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.p) ^ ((size_t)k.n * 0x9E3779B97F4A7C15ull) ^ (size_t)k.k;
+  }
+};
+
+bool weight_map(CUtensorMap* out, const void* w, int N, int K) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  std::lock_guard<std::mutex> g(mu);
+  MapKey key{w, N, K};
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return true;
+  }
+  if (!make_map(out, w, N, K, BM)) return false;
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
+  return true;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  return n;
+}
+
+void plan(int M, int N, int K, int sms, Params& p, int& grid) {
+  const int tiles = (N + BM - 1) / BM;
+  p.KB = (K + BK - 1) / BK;
+  p.U = tiles * p.KB;
+  grid = p.U < sms ? p.U : sms;
+  p.base = p.U / grid;
+  p.rem = p.U % grid;
+  (void)M;
+}
+
+size_t workspace_bytes(int M, int N, int K) {
+  Params p{};
+  int grid;
+  plan(M, N, K, num_sms(), p, grid);
+  return kCounterBytes + 256 + sizeof(float) * (size_t)grid * 2 * M * BM;
+}
+
+template <int MP>
+int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws) {
+  using C = Cfg<MP>;
+  CUtensorMap wm, xm;
+  if (!weight_map(&wm, w, N, K)) return SSD_ERR_LAUNCH;
+  if (!make_map(&xm, x, M, K, MP)) return SSD_ERR_LAUNCH;
+  Params p{};
+  int grid;
+  plan(M, N, K, num_sms(), p, grid);
+  p.y = y;
+  p.epi = epi;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  char* wsb = reinterpret_cast<char*>(ws);
+  p.counters = reinterpret_cast<unsigned int*>(wsb);
+  p.err = reinterpret_cast<unsigned int*>(wsb + kCounterBytes);
+  p.part = reinterpret_cast<float*>(wsb + kCounterBytes + 256);
+  auto kern = linear_tc_kernel<MP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
+    return SSD_ERR_LAUNCH;
+  kern<<<grid, kThreads, C::SMEM, st>>>(wm, xm, p);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+}  // namespace tc
+
+bool linear_tc_supported(int M, int N, int K) {
+  return M >= 1 && M <= 256 && N >= 1 && K >= 64 && (K % 8) == 0 && (N + tc::BM - 1) / tc::BM <= kCounterCap &&
+         tc::encode_fn() != nullptr;
+}
+
+size_t linear_tc_workspace(int M, int N, int K) { return tc::workspace_bytes(M, N, K); }
+
+int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
+              size_t ws_bytes) {
+  if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
+  if (M <= 16) return tc::launch<16>(st, x, w, y, epi, M, N, K, ws);
+  if (M <= 32) return tc::launch<32>(st, x, w, y, epi, M, N, K, ws);
+  if (M <= 64) return tc::launch<64>(st, x, w, y, epi, M, N, K, ws);
+  if (M <= 128) return tc::launch<128>(st, x, w, y, epi, M, N, K, ws);
+  return tc::launch<256>(st, x, w, y, epi, M, N, K, ws);
+}
+
 }  // namespace ssd

@@ -28,6 +28,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __rest
   for (int i = threadIdx.x; i < d; i += blockDim.x) x[(int64_t)m * d + i] = from_f<T>(__fmul_rn(to_f(e[i]), scale));
 }
 
+// One CTA per row.  bf16 rows with d % 8 == 0 are read once as 16-byte vectors
+// kept in registers (d <= 8 * 256 * 4); other shapes take the scalar loop.
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int d, float eps) {
   __shared__ float red[32];
@@ -43,6 +45,47 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
   for (int i = threadIdx.x; i < d; i += blockDim.x)
     y[(int64_t)m * d + i] = from_f<T>(__fmul_rn(__fmul_rn(to_f(xr[i]), inv), __fadd_rn(1.0f, to_f(w[i]))));
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                              bf16* __restrict__ y, int d, float eps) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const int nv = d / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)m * d);
+  float v[4][8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      unpack8(xr[i], v[j]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[j][e], v[j][e], s);
+    }
+  }
+  s = block_reduce(s, red, OpSum());
+  const float ms = __fdiv_rn(s, (float)d);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)m * d);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      float wv[8];
+      unpack8(wr[i], wv);
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = __fmul_rn(__fmul_rn(v[j][2 * e], inv), __fadd_rn(1.0f, wv[2 * e]));
+        const float c = __fmul_rn(__fmul_rn(v[j][2 * e + 1], inv), __fadd_rn(1.0f, wv[2 * e + 1]));
+        oh[e] = __floats2bfloat162_rn(a, c);
+      }
+      yr[i] = o;
+    }
+  }
 }
 
 // positions[b*T+t] = seq_lens_before[b] + t for t < q_lens[b], else -1; seq_after[b].
@@ -81,7 +124,7 @@ struct Scratch {
   size_t total;
 };
 
-int max_m() { return 16; }
+int max_m() { return 256; }  // tcgen05 path; the CUDA-core path takes M <= 16
 
 size_t linear_ws_any(int M, int N, int K, int dtype) {
   if (dtype == SSD_DTYPE_BF16 && linear_tc_supported(M, N, K)) return linear_tc_workspace(M, N, K);
@@ -191,7 +234,11 @@ extern "C" int ssd_rmsnorm(ssd_stream_t stream, const void* x, const void* w, in
                            float eps) {
   if (M <= 0 || d <= 0 || !x || !w || !y) return SSD_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == SSD_DTYPE_BF16)
+  const bool vec = (d % 8 == 0) && d <= 8 * 256 * 4 && !(reinterpret_cast<uintptr_t>(x) & 15) &&
+                   !(reinterpret_cast<uintptr_t>(w) & 15) && !(reinterpret_cast<uintptr_t>(y) & 15);
+  if (dtype == SSD_DTYPE_BF16 && vec)
+    rmsnorm_bf16_vec_kernel<<<M, 256, 0, st>>>((const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
+  else if (dtype == SSD_DTYPE_BF16)
     rmsnorm_kernel<bf16><<<M, 256, 0, st>>>((const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
   else if (dtype == SSD_DTYPE_F32)
     rmsnorm_kernel<float><<<M, 256, 0, st>>>((const float*)x, (const float*)w, (float*)y, d, eps);
@@ -243,12 +290,21 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     if (rc != SSD_OK) return rc;   \
   } while (0)
   int nprof = 0;
+  // while the stream is being captured, timing events must be external records
+  // (they stay timed event nodes in the graph); outside capture a plain record
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (bt->prof_events) cudaStreamIsCapturing(st, &cap);
+  const bool capturing = cap == cudaStreamCaptureStatusActive;
+  auto rec_event = [&](void* ev) {
+    if (capturing) cudaEventRecordWithFlags((cudaEvent_t)ev, st, cudaEventRecordExternal);
+    else cudaEventRecord((cudaEvent_t)ev, st);
+  };
   auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k) {
     const bool rec = bt->prof_events && nprof < bt->prof_capacity;
-    if (rec) cudaEventRecord((cudaEvent_t)bt->prof_events[2 * nprof], st);
+    if (rec) rec_event(bt->prof_events[2 * nprof]);
     const int r = linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes);
     if (rec) {
-      cudaEventRecord((cudaEvent_t)bt->prof_events[2 * nprof + 1], st);
+      rec_event(bt->prof_events[2 * nprof + 1]);
       if (bt->prof_kind) bt->prof_kind[nprof] = kind;
       ++nprof;
       if (bt->prof_count) *bt->prof_count = nprof;

@@ -355,18 +355,18 @@ extern "C" size_t ssd_verify_greedy_workspace_size(int B, int K, int V) {
   if (B <= 0 || K < 0 || V <= 0) return 0;
   const int rows = B * (K + 1);
   const int nch = scan_chunks(rows, V);
-  return align256(sizeof(unsigned int) * (size_t)rows) + sizeof(unsigned long long) * (size_t)rows * nch;
+  return kCounterBytes + sizeof(unsigned long long) * (size_t)rows * nch;
 }
 
 static int launch_greedy(cudaStream_t st, const float* x, int64_t ld, int rows, int kp1, int V,
                          const int32_t* spec, int32_t* acc, int32_t* rec, uint8_t* mask, int32_t* tt,
                          int32_t* amax, void* ws, size_t ws_bytes) {
   const int nch = scan_chunks(rows, V);
-  const size_t need = align256(sizeof(unsigned int) * (size_t)rows) + sizeof(unsigned long long) * (size_t)rows * nch;
+  const size_t need = kCounterBytes + sizeof(unsigned long long) * (size_t)rows * nch;
   if (ws_bytes < need || ws == nullptr) return SSD_ERR_WORKSPACE;
+  if (rows > kCounterCap) return SSD_ERR_UNSUPPORTED;
   unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
-  unsigned long long* part = reinterpret_cast<unsigned long long*>(
-      reinterpret_cast<char*>(ws) + align256(sizeof(unsigned int) * (size_t)rows));
+  unsigned long long* part = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ws) + kCounterBytes);
   const bool vec_ok = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   dim3 grid(nch, rows);
   greedy_scan_kernel<<<grid, kScanThreads, 0, st>>>(x, ld, V, kp1, nch, vec_ok, counters, part, spec, acc,
@@ -398,7 +398,7 @@ static void sample_layout(int B, int K, int V, int& nR, int& nch, size_t& off_pa
   nR = 2 * K + 1;  // upper bound over both alignments
   nch = scan_chunks(B * nR, V);
   // the residual and draw passes scan B rows: give them the same chunk count
-  off_part = align256(sizeof(unsigned int) * (size_t)B * 3);
+  off_part = kCounterBytes;
   const size_t p1 = sizeof(float2) * (size_t)B * nR * nch;
   const size_t p2 = sizeof(unsigned long long) * (size_t)B * scan_chunks(B, V);
   off_dec = off_part + align256(p1 > p2 ? p1 : p2);
@@ -429,7 +429,7 @@ extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, con
   if (!workspace || workspace_bytes < total) return SSD_ERR_WORKSPACE;
   const int off = alignment == SSD_ALIGN_REFERENCE ? 1 : 0;
   const int rows = B * (2 * K + 1 - off);
-  if (rows > 65535) return SSD_ERR_UNSUPPORTED;
+  if (rows > 65535 || 3 * B > kCounterCap) return SSD_ERR_UNSUPPORTED;
   char* w = reinterpret_cast<char*>(workspace);
   unsigned int* c0 = reinterpret_cast<unsigned int*>(w);
   unsigned int* c1 = c0 + B;

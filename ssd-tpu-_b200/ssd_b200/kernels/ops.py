@@ -46,5 +46,10 @@ def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = 
     return out
 
 
-def max_tokens_per_forward() -> int:
+def max_tokens_per_forward(dtype=None) -> int:
+    """Largest B*T one forward takes: 256 on the tcgen05 (bf16) path, 16 on the fp32 CUDA-core path."""
+    import torch
+
+    if dtype == torch.float32:
+        return 16
     return int(lib().ssd_linear_max_m())

@@ -250,15 +250,17 @@ class GemmaRunner:
 class ProjectionTimer:
     """CUDA events around every projection launch of a forward (ssd_gemma_batch.prof_*).
 
-    Durations are read after the events complete; ``bytes_per_kind`` gives the
-    algorithmic bytes of each projection launch (weights + activations in/out).
+    ``attach`` binds the event array into the batch struct; the C++ forward
+    records event 2i / 2i+1 around its i-th projection (also inside a captured
+    CUDA graph, where the records become graph nodes).  ``read`` — called after
+    the step has synchronised — adds the elapsed time of the bound pairs.
     """
 
     KINDS = ("qkv", "o", "gate_up", "down", "lm_head")
 
     def __init__(self, capacity: int = 512):
         self.capacity = capacity
-        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(2 * capacity)]
+        self.events = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2 * capacity)]
         st = torch.cuda.current_stream()
         for e in self.events:
             e.record(st)  # materialise the handles
@@ -266,26 +268,25 @@ class ProjectionTimer:
         self._arr = (C.c_void_p * (2 * capacity))(*[e.cuda_event for e in self.events])
         self._count = C.c_int(0)
         self._kind = (C.c_int * capacity)()
-        self.pending = []       # (kind, start, end) of launches not yet read
+        self.bound = []
         self.total_ms = {k: 0.0 for k in self.KINDS}
         self.launches = {k: 0 for k in self.KINDS}
 
     def attach(self, bt) -> None:
-        if self.pending:  # the event array is about to be re-recorded
-            self.flush()
         bt.prof_events = C.cast(self._arr, C.POINTER(C.c_void_p))
         bt.prof_capacity = self.capacity
         bt.prof_count = C.pointer(self._count)
         bt.prof_kind = C.cast(self._kind, C.POINTER(C.c_int))
 
     def collect(self) -> None:
-        n = self._count.value
-        for i in range(n):
-            self.pending.append((self.KINDS[self._kind[i]], self.events[2 * i], self.events[2 * i + 1]))
+        self.bound = [(self.KINDS[self._kind[i]], self.events[2 * i], self.events[2 * i + 1])
+                      for i in range(self._count.value)]
 
-    def flush(self) -> None:
-        for kind, a, b in self.pending:
-            b.synchronize()
+    def read(self) -> None:
+        for kind, a, b in self.bound:
             self.total_ms[kind] += a.elapsed_time(b)
             self.launches[kind] += 1
-        self.pending = []
+
+    def reset(self) -> None:
+        self.total_ms = {k: 0.0 for k in self.KINDS}
+        self.launches = {k: 0 for k in self.KINDS}

@@ -1,5 +1,8 @@
 """Greedy speculative decoding of one sequence on the verify-path kernels.
 
+The device work of a step is replayed from a CUDA graph per draft-feed length
+(1 or 2 tokens) once that shape has been seen twice (the first run is eager).
+
 Per step (the sd loop of jax_ssd/runtime/engine.py:230-252, with the KV
 bookkeeping a real paged cache needs instead of the reference's per-token
 re-commit, gemma_adapter.py:145-152):
@@ -11,10 +14,10 @@ re-commit, gemma_adapter.py:145-152):
 2. verify: one target forward over ``[recovery] + draft[k]`` (k+1 tokens), which
    also writes their K/V rows into the target's pages;
 3. ``ssd_verify_greedy`` -> accepted count and recovery token (device);
-4. one 8-byte device->host read of (accepted, recovery);
-5. ``ssd_page_rollback`` on both caches: target keeps old + 1 + accepted tokens,
-   the draft keeps what it computed for accepted tokens; surplus pages return to
-   the free lists.
+4. one device->host read of (accepted, recovery) and the k+1 verify tokens;
+5. ``ssd_page_rollback`` on both caches (issued at the start of the next step,
+   from host scalars): target keeps old + 1 + accepted tokens, the draft keeps
+   what it computed for accepted tokens; surplus pages return to the free lists.
 
 All device work of a step is stream-ordered with no allocation; the only host
 synchronisation is step 4.
@@ -43,13 +46,14 @@ class _Model:
         self.cache = KVCacheState.allocate(s.num_layers, self.num_blocks, block_size, s.num_kv_heads, s.head_dim,
                                            dtype=weights.dtype, device=weights.device)
         self.pm = PageManager(block_size, self.num_blocks, max_seqs=1, device=weights.device)
-        self.runner = GemmaRunner(weights, 1, max(k + 1, max_tokens_per_forward()), max_seq_len)
+        self.runner = GemmaRunner(weights, 1, max(k + 1, max_tokens_per_forward(weights.dtype)), max_seq_len)
+        self.chunk = min(64, max_tokens_per_forward(weights.dtype))
         self.n = 0  # tokens in the cache
 
 
 class SpeculativeDecoder:
     def __init__(self, target: GemmaWeights, draft: GemmaWeights, k: int = 4, max_seq_len: int = 1024,
-                 block_size: int = 16):
+                 block_size: int = 16, use_graphs: bool = True, timer=None):
         self.k = k
         self.dev = target.device
         self.max_seq_len = max_seq_len
@@ -67,15 +71,22 @@ class SpeculativeDecoder:
         self.mask = torch.empty((1, k + 1), dtype=torch.uint8, device=dev)
         self.host = torch.zeros(2, dtype=torch.int32).pin_memory()
         # host -> device scalars of one step, copied once per step
-        self.h_scal = torch.zeros(16, dtype=torch.int32).pin_memory()
-        self.d_scal = torch.zeros(16, dtype=torch.int32, device=dev)
+        self.h_scal = torch.zeros(16 + k, dtype=torch.int32).pin_memory()
+        self.d_scal = torch.zeros(16 + k, dtype=torch.int32, device=dev)
         self.h_roll = torch.zeros(8, dtype=torch.int32).pin_memory()
         self.d_roll = torch.zeros(8, dtype=torch.int32, device=dev)
         self.spec_host = torch.zeros(k + 1, dtype=torch.int32).pin_memory()
         self.ws_greedy = workspace(dev, "sd_greedy", lib().ssd_verify_greedy_workspace_size(1, k, V))
         self.ws_argmax = workspace(dev, "sd_argmax", lib().ssd_verify_greedy_workspace_size(1, 0, V))
         self.tokens: list[int] = []
-        self.verify_events = None
+        # external: inside a captured step these become real event-record nodes that can be timed
+        self.ev_verify = (torch.cuda.Event(enable_timing=True, external=True),
+                          torch.cuda.Event(enable_timing=True, external=True))
+        self.use_graphs = use_graphs
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._seen: dict[int, int] = {}
+        self._graph_prof = timer  # projection timer bound into the step (eager or captured)
+        self.last_verify_ms = 0.0
 
     # ------------------------------------------------------------------ helpers
     # Host scalars of one step are written into the pinned ``h_scal`` and copied
@@ -86,7 +97,7 @@ class SpeculativeDecoder:
         return self.d_scal[i:i + 1]
 
     def _prefill(self, m: _Model, prompt: torch.Tensor, want_logits: bool):
-        chunk = max_tokens_per_forward()
+        chunk = m.chunk
         n = prompt.shape[1]
         dev = self.dev
         m.pm.allocate_rows(0, 1, torch.zeros(1, dtype=torch.int32, device=dev),
@@ -113,67 +124,95 @@ class SpeculativeDecoder:
         first = int(self.host[0])
         self.seq = list(prompt) + [first]
         self.tokens = [first]
+        # no rollback is pending before the first step: keep both tables as they are
+        self._roll = (self.t.n, 0, self.d.n, 0)
+        self._rec = first
         return first
 
-    def step(self, events=None, prof=None) -> list[int]:
-        """One draft+verify+accept+rollback iteration; returns the committed tokens."""
-        k = self.k
-        t, d = self.t, self.d
-        st = torch.cuda.current_stream()
+    # Host scalar slots (int32), copied to the device once per step:
+    #  0 draft tokens cached | 1 draft tokens to reserve | 2-3 draft feed tokens
+    #  4 target tokens cached | 5 verify tokens (k+1) | 6-7 target rollback
+    #  (num_tokens, accepted) | 8-9 draft rollback | 10 recovery token
+    #  16.. draft forward i: tokens cached before it
+    def _host_scalars(self, nf: int) -> None:
+        k, t, d, h = self.k, self.t, self.d, self.h_scal
         feed = self.seq[d.n:]
-        nf = len(feed)
-        h = self.h_scal
-        # slots: 0 d.n | 1 draft new | 2-3 feed | 4..4+k-1 draft slb | 12 t.n | 13 k+1
         h[0] = d.n
         h[1] = nf + k - 1
         for j, tok in enumerate(feed):
             h[2 + j] = tok
-        h[4] = d.n
+        h[4] = t.n
+        h[5] = k + 1
+        h[6], h[7], h[8], h[9] = self._roll
+        h[10] = self._rec
+        h[16] = d.n
         for i in range(1, k):
-            h[4 + i] = d.n + nf + i - 1
-        h[12] = t.n
-        h[13] = k + 1
-        self.d_scal.copy_(h, non_blocking=True)
-        # ---- draft: k greedy forwards, tokens written into vt[0, 1..k]
+            h[16 + i] = d.n + nf + i - 1
+
+    def _device_step(self, nf: int, prof=None) -> None:
+        """All device work of one step; stream-ordered, no allocation, capturable."""
+        k, t, d = self.k, self.t, self.d
+        st = torch.cuda.current_stream()
+        self.d_scal.copy_(self.h_scal, non_blocking=True)
+        # rollback of the previous verify (no-op values before the first step)
+        t.pm.rollback_rows(0, 1, self._scal(6), self._scal(7))
+        d.pm.rollback_rows(0, 1, self._scal(8), self._scal(9))
+        self.vt[0, 0:1].copy_(self.d_scal[10:11])
+        # draft: k greedy forwards, tokens written into vt[0, 1..k]
         d.pm.allocate_rows(0, 1, self._scal(0), self._scal(1), None)
-        d.runner.forward(self.d_scal[2:2 + nf].view(1, nf), self._scal(4), d.cache.pages, d.pm.tables,
+        d.runner.forward(self.d_scal[2:2 + nf].view(1, nf), self._scal(16), d.cache.pages, d.pm.tables,
                          self.logits_d, last_only=True)
         argmax_rows(self.logits_d, self.vt[0, 1:2])
         for i in range(1, k):
-            d.runner.forward(self.vt[:, i:i + 1], self._scal(4 + i), d.cache.pages, d.pm.tables, self.logits_d,
+            d.runner.forward(self.vt[:, i:i + 1], self._scal(16 + i), d.cache.pages, d.pm.tables, self.logits_d,
                              last_only=True)
             argmax_rows(self.logits_d, self.vt[0, i + 1:i + 2])
-        # ---- verify: target forward over k+1 tokens + fused acceptance
-        if events is not None:
-            events[0].record(st)
-        t.pm.allocate_rows(0, 1, self._scal(12), self._scal(13), None)
-        t.runner.forward(self.vt, self._scal(12), t.cache.pages, t.pm.tables, self.logits_t, last_only=False,
+        # verify: target forward over k+1 tokens + fused greedy acceptance
+        self.ev_verify[0].record(st)
+        t.pm.allocate_rows(0, 1, self._scal(4), self._scal(5), None)
+        t.runner.forward(self.vt, self._scal(4), t.cache.pages, t.pm.tables, self.logits_t, last_only=False,
                          prof=prof)
         check(lib().ssd_verify_greedy(stream_ptr(), ptr(self.logits_t), ptr(self.vt), ptr(self.acc_rec[0:1]),
                                       ptr(self.acc_rec[1:2]), ptr(self.mask), None, ptr(self.ws_greedy),
                                       self.ws_greedy.numel(), 1, k, self.logits_t.shape[2]), "ssd_verify_greedy")
-        if events is not None:
-            events[1].record(st)
+        self.ev_verify[1].record(st)
         self.host.copy_(self.acc_rec, non_blocking=True)
         self.spec_host.copy_(self.vt[0], non_blocking=True)
-        st.synchronize()
+
+    def step(self, prof=None) -> list[int]:
+        """One draft+verify+accept iteration (rollback of it runs first in the next one)."""
+        k, t, d = self.k, self.t, self.d
+        nf = len(self.seq) - d.n
+        self._host_scalars(nf)
+        g = self._graphs.get(nf) if self.use_graphs else None
+        if g is not None:
+            g.replay()
+        elif self.use_graphs and self._seen.get(nf, 0) >= 1:
+            # second sighting of this shape: capture (first run was eager, so every
+            # lazily created buffer and cached tensor map already exists), then replay
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._device_step(nf, prof=self._graph_prof)
+            self._graphs[nf] = g
+            g.replay()
+        else:
+            self._seen[nf] = self._seen.get(nf, 0) + 1
+            self._device_step(nf, prof=self._graph_prof if self.use_graphs else prof)
+        torch.cuda.current_stream().synchronize()
+        if self._graph_prof is not None:
+            self._graph_prof.read()
         acc, rec = int(self.host[0]), int(self.host[1])
         spec = [int(x) for x in self.spec_host[1:].tolist()]
         new = spec[:acc] + [rec]
-        # ---- rollback both caches (second scalar copy: the first one has completed)
         n_seq_old = len(self.seq)
-        r = self.h_roll
-        r[0], r[1], r[2], r[3] = t.n, 1 + acc, n_seq_old, min(acc, k - 1)
-        r[4] = rec
-        self.d_roll.copy_(r, non_blocking=True)
-        t.pm.rollback_rows(0, 1, self.d_roll[0:1], self.d_roll[1:2])
-        d.pm.rollback_rows(0, 1, self.d_roll[2:3], self.d_roll[3:4])
-        self.vt[0, 0:1].copy_(self.d_roll[4:5])
+        self._roll = (t.n, 1 + acc, n_seq_old, min(acc, k - 1))
+        self._rec = rec
         t.n = t.n + 1 + acc
         d.n = n_seq_old + min(acc, k - 1)
         self.seq.extend(new)
         self.tokens.extend(new)
         self.last_accept = acc
+        self.last_verify_ms = self.ev_verify[0].elapsed_time(self.ev_verify[1])
         return new
 
     def generate(self, prompt: list[int], max_new: int) -> tuple[list[int], dict]:
@@ -202,7 +241,7 @@ class GreedyDecoder:
         t, dev, lg = self.t, self.dev, self.lg
         n = len(prompt)
         p = torch.tensor([prompt], dtype=torch.int32, device=dev)
-        chunk = max_tokens_per_forward()
+        chunk = t.chunk
         t.pm.allocate_rows(0, 1, torch.zeros(1, dtype=torch.int32, device=dev),
                            torch.tensor([n], dtype=torch.int32, device=dev), None)
         for c0 in range(0, n, chunk):

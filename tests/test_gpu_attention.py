@@ -12,7 +12,7 @@ from oracle.paged_kv import write_kv as o_write
 pytestmark = pytest.mark.gpu
 
 
-def _setup(b, t, hq, hkv, d, bs, ctx, dtype_name, seed):
+def _setup(b, t, hq, hkv, d, bs, ctx, dtype_name, seed, table_cols=None):
     import torch
 
     from ssd_b200.kernels.kv_cache import KVCacheState
@@ -37,6 +37,8 @@ def _setup(b, t, hq, hkv, d, bs, ctx, dtype_name, seed):
     pos = np.where(np.arange(L)[None, :] < np.array(ctx)[:, None], np.arange(L)[None, :], -1).astype(np.int32)
     o_write(pages_np, 0, tables, pos, k, v)
     cache.pages.copy_(torch.tensor(pages_np).to(tdt))
+    if table_cols is not None and table_cols > tables.shape[1]:  # unused trailing entries stay -1
+        tables = np.concatenate([tables, np.full((b, table_cols - tables.shape[1]), -1, np.int32)], 1)
     return cache, pages_np, tables, q, tdt
 
 
@@ -89,7 +91,7 @@ def test_attention_is_batch_invariant(cuda):
 
     b, t, hq, hkv, d, bs = 1, 5, 16, 16, 256, 16
     ctx = [777]
-    cache, pages_np, tables, q, tdt = _setup(b, t, hq, hkv, d, bs, ctx, "bf16", seed=9)
+    cache, pages_np, tables, q, tdt = _setup(b, t, hq, hkv, d, bs, ctx, "bf16", seed=9, table_cols=128)
     tb = torch.tensor(tables, device="cuda")
     qd = torch.tensor(q).to(device="cuda", dtype=tdt)
     full = paged_verify_attention(qd, cache, 0, tb, torch.tensor(ctx, dtype=torch.int32, device="cuda"),

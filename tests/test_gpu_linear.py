@@ -11,8 +11,11 @@ pytestmark = pytest.mark.gpu
 
 
 def _bf16_close(got, exp, ulps=1.0, atol=1e-6):
-    """|got - exp| within `ulps` bf16 ulps of |exp| (fp32 accumulation order differs)."""
-    tol = np.abs(exp) * (2.0 ** -8) * ulps + atol
+    """|got - exp| within `ulps` bf16 ulps of |exp| (fp32 accumulation order differs).
+
+    A bf16 ulp is 2^(e-7) for |x| in [2^e, 2^(e+1)), i.e. at most |x| * 2^-7.
+    """
+    tol = np.abs(exp) * (2.0 ** -7) * ulps + atol
     bad = np.abs(got - exp) > tol
     assert not bad.any(), (np.abs(got - exp)[bad][:5], exp[bad][:5])
 
@@ -99,3 +102,25 @@ def test_fp32_weights_toy(cuda):
     w = torch.randn((1024, 256), device="cuda", generator=g) * 0.06
     y = linear(x, w, "store")
     torch.testing.assert_close(y, x @ w.T, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 1000, 520), (64, 3072, 3072), (200, 513, 1024), (256, 4096, 256),
+                                   (5, 256000, 3072), (2, 130, 64)])
+def test_tcgen05_shapes_and_tails(cuda, m, n, k):
+    """M up to 256 (UMMA N = 16..256), N and K not multiples of the 128 x 64 tile."""
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+    from ssd_b200.workspace import workspace
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn((m, k), device="cuda", generator=g).bfloat16()
+    w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).bfloat16()
+    y = linear(x, w, "store_f32", ws_key="tc_test")
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(y, ref, rtol=1e-4, atol=1e-4)
+    torch.cuda.synchronize()
+    ws = workspace(x.device, "tc_test", 0)
+    head = ws[: 16384 * 4 + 4].view(torch.int32)
+    assert int(head[:16384].abs().sum()) == 0      # ticket counters reset
+    assert int(head[16384]) == 0                   # no device-side wait gave up

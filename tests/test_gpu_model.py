@@ -33,8 +33,8 @@ def _run_forward(w, prompt, verify_tokens, bs=16):
     nb = (n + bs - 1) // bs + 1
     cache = KVCacheState.allocate(s.num_layers, nb, bs, s.num_kv_heads, s.head_dim, dtype=w.dtype)
     table = torch.arange(nb, dtype=torch.int32, device="cuda")[None]
-    run = GemmaRunner(w, 1, 16, nb * bs)
-    chunk = max_tokens_per_forward()
+    run = GemmaRunner(w, 1, 64, nb * bs)
+    chunk = min(64, max_tokens_per_forward(w.dtype))
     p = torch.tensor([prompt], dtype=torch.int32, device="cuda")
     for c0 in range(0, len(prompt), chunk):
         c1 = min(len(prompt), c0 + chunk)

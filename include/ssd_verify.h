@@ -71,6 +71,25 @@ int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t*
                       int V);
 
 /*
+ * ssd_verify_greedy without a workspace argument, for callers that cannot
+ * allocate device memory (an XLA custom call handed only its operands, code
+ * inside a CUDA graph capture, embedders with a fixed memory budget).  No
+ * counterpart in the reference: it is an addition of this library.
+ * Outputs and argument meaning are those of ssd_verify_greedy; it allocates
+ * nothing.  Its scratch is a 34 KB array in the library's device data that
+ * every GPU loading the library holds until exit.  Limits: B*(K+1) <= 512
+ * (larger calls return SSD_ERR_UNSUPPORTED).  The first call on each device
+ * looks up the array's device address with that device current; make that
+ * first call before any stream capture.  All calls share the array, so calls
+ * that overlap on the GPU (different streams, or different host threads
+ * without ordering) race and give wrong results.
+ */
+int ssd_verify_greedy_noalloc(ssd_stream_t stream, const float* logits_p,
+                              const int32_t* speculations, int32_t* accept_until,
+                              int32_t* recovery, uint8_t* accepted_mask, int32_t* target_tokens,
+                              int B, int K, int V);
+
+/*
  * Row-wise argmax (first index on ties) of x[rows, V] (row stride `ld`
  * elements), e.g. the draft's greedy token.  Replaces the jnp.argmax calls of
  * jax_ssd/runtime/engine.py:224 and jax_ssd/models/gemma_adapter.py:127.

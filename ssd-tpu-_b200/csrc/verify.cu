@@ -9,6 +9,8 @@
 // each CTA reduces its slice to a partial (argmax key, or max/sum-exp pair) in
 // the workspace, and the last CTA of a group (atomic ticket, self-resetting)
 // folds the partials in fixed chunk order, so results are deterministic.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ssd {
@@ -384,6 +386,65 @@ extern "C" int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, con
   if ((int64_t)B * (K + 1) > 65535) return SSD_ERR_UNSUPPORTED;
   return launch_greedy((cudaStream_t)stream, logits_p, V, B * (K + 1), K + 1, V, speculations, accept_until,
                        recovery, accepted_mask, target_tokens, nullptr, workspace, workspace_bytes);
+}
+
+// ------------------------------------------------------------------ no-allocation variant
+// Greedy acceptance for callers that cannot allocate device memory (an XLA
+// custom call that is handed only its operands, code running inside a CUDA
+// graph capture, embedders with a fixed memory budget).  Its scratch -- the
+// ticket counters and the per-chunk argmax partials -- lives in this file-scope
+// device array instead of a caller workspace.  Every GPU that loads the library
+// holds these 34 KB until the process exits.  Host code must not use the array's
+// name as a pointer (on the host it is only a stand-in); the device address comes
+// from cudaGetSymbolAddress, looked up once per device.
+constexpr int kNoAllocMaxRows = 512;       // B * (K + 1)
+constexpr int kNoAllocMaxPartials = 4096;  // rows * chunks (at most 592 + rows in practice)
+constexpr size_t kNoAllocCounterBytes = sizeof(unsigned int) * kNoAllocMaxRows;
+static __device__ __align__(256) unsigned char g_greedy_scratch[kNoAllocCounterBytes +
+                                                                sizeof(unsigned long long) * kNoAllocMaxPartials];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64] = {};
+
+// Device address of g_greedy_scratch on the current device (looked up on the
+// first call per device, with that device current).
+static int greedy_scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSD_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_greedy_scratch) != cudaSuccess || p == nullptr) return SSD_ERR_LAUNCH;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return SSD_OK;
+}
+
+extern "C" int ssd_verify_greedy_noalloc(ssd_stream_t stream, const float* logits_p, const int32_t* speculations,
+                                         int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
+                                         int32_t* target_tokens, int B, int K, int V) {
+  if (B <= 0 || K < 0 || K > 63 || V <= 0 || !logits_p || !speculations || !accept_until || !recovery)
+    return SSD_ERR_INVALID;
+  const int64_t rows = (int64_t)B * (K + 1);
+  if (rows > kNoAllocMaxRows) return SSD_ERR_UNSUPPORTED;
+  const int nch = scan_chunks((int)rows, V);
+  if (rows * nch > kNoAllocMaxPartials) return SSD_ERR_UNSUPPORTED;
+  void* base = nullptr;
+  const int rc = greedy_scratch_address(&base);
+  if (rc != SSD_OK) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // the counters must start at zero whatever an earlier (possibly aborted) call left behind
+  if (cudaMemsetAsync(base, 0, kNoAllocCounterBytes, st) != cudaSuccess) return SSD_ERR_LAUNCH;
+  unsigned int* counters = reinterpret_cast<unsigned int*>(base);
+  unsigned long long* part =
+      reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(base) + kNoAllocCounterBytes);
+  const bool vec_ok = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits_p) & 15) == 0);
+  greedy_scan_kernel<<<dim3(nch, (unsigned)rows), kScanThreads, 0, st>>>(logits_p, V, V, K + 1, nch, vec_ok, counters,
+                                                                         part, speculations, accept_until, recovery,
+                                                                         accepted_mask, target_tokens, nullptr);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
 }
 
 extern "C" int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, int32_t* out,

@@ -3,65 +3,72 @@
 //
 // Semantics: jax_ssd/kernels/attention_ref.py:9-21 (softmax(q k^T * scale +
 // mask) v) with the verify mask of jax_ssd/kernels/masks.py:33-40 and the page
-// layout of jax_ssd/kernels/kv_cache.py:13 — pages[2][L][NB][BS][Hkv][D].
+// layout of jax_ssd/kernels/kv_cache.py:13 -- pages[2][L][NB][BS][Hkv][D].
 //
 // Decomposition (flash-decoding): grid (split, kv_head x row_group, sequence).
-// A CTA owns one KV head of one sequence, a fixed 256-position slice of its
-// context, and up to 16 query rows (the G = Hq/Hkv query heads of that KV head
-// times the T new tokens), so each K/V byte is read once per row group.  K/V
-// tiles of 32 positions are double-buffered into shared memory with cp.async
-// through the page table; scores, online softmax and P.V run on CUDA cores in
-// fp32.  Each CTA leaves an unnormalised partial (o, m, l) per row; the last CTA
-// of the (sequence, head, row group) folds the splits in split order.
+// A CTA owns one KV head of one sequence, a fixed 128-position slice of its
+// context and up to 8 query rows (the G = Hq/Hkv query heads of that KV head
+// times the new tokens), so each K/V byte is read once per row group.  Inside
+// the CTA each of the 8 warps owns 16 consecutive positions and runs start to
+// finish without CTA-wide synchronisation, with all of its loads in flight at
+// once (decode attention is latency-bound: a few hundred positions):
+//   * scores: 4 positions per round, 8 lanes per position each holding 16-byte
+//     pieces of the K row (128-byte contiguous segments), q rows from shared
+//     memory, a 3-step xor reduction per row;
+//   * softmax statistics per row with two warp reductions (lane = position);
+//   * P.V with lane = D/32 head dims: V rows read coalesced, p from a per-warp
+//     shared-memory row.
+// The warps' (m, l, o) are then combined in warp order, the CTA writes one
+// partial per row, and the last CTA of the group folds the splits in split
+// order (atomic ticket).
 //
-// Batch invariance: split and tile boundaries sit at fixed absolute positions,
-// each row's reductions run in a fixed order, and fully masked tiles / empty
-// splits are exact no-ops, so a query's output does not depend on T or on the
-// other rows — the greedy stream of a k+1-token verify equals the one-token
-// decode stream bit for bit.
+// Batch invariance: split and warp boundaries sit at fixed absolute positions,
+// every reduction of a row runs in a fixed order, and fully masked warps or
+// splits contribute exact zeros, so a query's output does not depend on T or
+// on the other rows -- a k+1-token verify reproduces one-token decodes bit for bit.
 #include "common.cuh"
 
 namespace ssd {
 namespace {
 
 constexpr int kAttnThreads = 256;
-constexpr int kRows = 16;      // query rows per CTA
-constexpr int kTile = 32;      // positions per smem tile
-constexpr int kChunk = 128;    // positions per split (fixed => batch invariant)
-constexpr int kParts = 8;      // dim partitions for q.k (one warp each)
+constexpr int kWarpsA = kAttnThreads / 32;
+constexpr int kRows = 8;                       // query rows per CTA
+constexpr int kWarpKeys = 16;                  // positions per warp
+constexpr int kChunk = kWarpsA * kWarpKeys;    // positions per split (fixed => batch invariant)
 
 template <typename T> struct Vec16;
 template <> struct Vec16<bf16> { static constexpr int N = 8; };
 template <> struct Vec16<float> { static constexpr int N = 4; };
 
-__device__ __forceinline__ void load16_to_f(const bf16* p, float* f) {
-  uint4 u = *reinterpret_cast<const uint4*>(p);
-  unpack8(u, f);
+// N consecutive elements (N * sizeof(KV) in {4, 8, 16} bytes, aligned) -> fp32
+template <int N>
+__device__ __forceinline__ void load_n(const bf16* p, float* f) {
+  if constexpr (N == 8) {
+    unpack8(ldg_nc_v4(p), f);
+  } else if constexpr (N == 4) {
+    uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = __bfloat162float(p[i]);
+  }
 }
-__device__ __forceinline__ void load16_to_f(const float* p, float* f) {
-  float4 u = *reinterpret_cast<const float4*>(p);
-  f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+template <int N>
+__device__ __forceinline__ void load_n(const float* p, float* f) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) f[i] = p[i];
 }
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
 
 template <typename KV, int D>
 struct AttnSmem {
-  static constexpr int V16 = Vec16<KV>::N;
-  static constexpr int KPAD = 16 / sizeof(KV);            // +16 B per K row: conflict-free
-  static constexpr int KSTRIDE = D + KPAD;
-  static constexpr size_t k_bytes = sizeof(KV) * kTile * KSTRIDE;
-  static constexpr size_t v_bytes = sizeof(KV) * kTile * D;
-  static constexpr size_t stage_bytes = k_bytes + v_bytes;
   static constexpr size_t q_bytes = sizeof(float) * kRows * D;
-  static constexpr size_t spart_bytes = sizeof(float) * kParts * kRows * kTile;
-  static constexpr size_t p_bytes = sizeof(float) * kRows * kTile;
-  static constexpr size_t total = 2 * stage_bytes + q_bytes + spart_bytes + p_bytes + 3 * sizeof(float) * kRows + 64;
+  static constexpr size_t p_bytes = sizeof(float) * kWarpsA * kRows * kWarpKeys;
+  static constexpr size_t o_bytes = sizeof(float) * kWarpsA * kRows * D;
+  static constexpr size_t ml_bytes = sizeof(float2) * kWarpsA * kRows;
+  static constexpr size_t total = q_bytes + p_bytes + o_bytes + ml_bytes + 64;
 };
 
 struct RowInfo {
@@ -72,10 +79,8 @@ struct RowInfo {
 // Fold the split partials of one (sequence, KV head, row group) in split order.
 // Only splits that start before seq_len can hold keys; the per-row weights
 // w_s = exp(m_s - M) and the normaliser L are computed once per row by one warp
-// (lane-strided over splits, xor-tree sums: adding an empty split's exact zeros
-// leaves them unchanged, so the result does not depend on how many empty splits
-// exist), then every output element sums w_s * o_s in split order with
-// independent loads in flight.
+// (lane-strided over splits, xor-tree sums: an empty split's exact zeros leave
+// them unchanged), then every output element sums w_s * o_s in split order.
 template <typename KV, int D>
 __device__ __forceinline__ void attention_fold(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
                                                KV* __restrict__ out, int64_t grp_id, int nsplit, int seq_len,
@@ -84,8 +89,7 @@ __device__ __forceinline__ void attention_fold(const float* __restrict__ ws_o, c
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ns = max(1, min(nsplit, (seq_len + kChunk - 1) / kChunk));
   __shared__ float inv_l[kRows];
-  // wsm: [kRows][ns] weights (ns <= 256 fits the score-partial region)
-  for (int r = warp; r < nrows; r += kAttnThreads / 32) {
+  for (int r = warp; r < nrows; r += kWarpsA) {
     const int64_t rb = grp_id * nsplit * kRows + r;
     float mloc = -INFINITY;
     for (int s = lane; s < ns; s += 32) mloc = fmaxf(mloc, __ldcg(&ws_ml[rb + (int64_t)s * kRows]).x);
@@ -130,23 +134,19 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
                        KV* __restrict__ out, float scale, int T, int hq, int row_groups, int nsplit,
                        float* __restrict__ ws_o, float2* __restrict__ ws_ml, unsigned int* __restrict__ counters) {
   using S = AttnSmem<KV, D>;
-  constexpr int V16 = S::V16;
+  constexpr int V16 = Vec16<KV>::N;      // elements per 16-byte load
+  constexpr int DPL = D / 32;            // head dims per lane in P.V
+  constexpr int KCH = D / (8 * V16);     // 16-byte K pieces per lane and position (8 lanes per position)
+  static_assert(KCH >= 1, "head_dim too small");
   extern __shared__ __align__(16) unsigned char smem[];
-  KV* kbuf[2];
-  KV* vbuf[2];
-  kbuf[0] = reinterpret_cast<KV*>(smem);
-  vbuf[0] = reinterpret_cast<KV*>(smem + S::k_bytes);
-  kbuf[1] = reinterpret_cast<KV*>(smem + S::stage_bytes);
-  vbuf[1] = reinterpret_cast<KV*>(smem + S::stage_bytes + S::k_bytes);
-  float* qs = reinterpret_cast<float*>(smem + 2 * S::stage_bytes);
-  float* spart = qs + kRows * D;
-  float* ps = spart + kParts * kRows * kTile;
-  float* m_s = ps + kRows * kTile;
-  float* l_s = m_s + kRows;
-  float* a_s = l_s + kRows;
+  float* qs = reinterpret_cast<float*>(smem);                 // [kRows][D]
+  float* ps = qs + kRows * D;                                 // [warp][kRows][kWarpKeys]
+  float* os = ps + kWarpsA * kRows * kWarpKeys;               // [warp][kRows][D]
+  float2* mls = reinterpret_cast<float2*>(os + kWarpsA * kRows * D);  // [warp][kRows]
   __shared__ RowInfo ri;
   __shared__ bool is_last;
 
+  pdl_wait();
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / row_groups, rg = blockIdx.y % row_groups;
   const int b = blockIdx.z;
@@ -175,15 +175,44 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
 
   const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
   if (k_end <= k_begin) {
-    // No key of this split is visible to any row: mark the rows empty (m = -inf,
-    // l = 0; the fold then never reads their o) and take the ticket.
+    // no key of this split is visible to any row: mark the rows empty and take the ticket
     if (tid < nrows) ws_ml[(grp_id * nsplit + split) * kRows + tid] = make_float2(-INFINITY, 0.f);
+    pdl_trigger();
     if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
-    attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, spart);
+    attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, os);
     return;
   }
 
-  // q rows -> fp32 smem (zeros for padding rows)
+  const int64_t plane = (int64_t)num_layers * num_blocks * block_size * hkv * D;  // K -> V plane offset
+  const KV* kbase = pages + (int64_t)layer * num_blocks * block_size * hkv * D;
+  const int32_t* table = block_tables + (int64_t)b * max_blocks;
+  const int t0 = k_begin + warp * kWarpKeys;
+  const int jn = max(0, min(kWarpKeys, k_end - t0));   // positions of this warp that exist
+
+  // Row offsets of this warp's positions: lane j (< kWarpKeys) resolves position t0 + j.
+  int64_t my_off = 0;
+  if (lane < jn) {
+    const int key = t0 + lane;
+    int blk = table[key / block_size];
+    if ((unsigned)blk >= (unsigned)num_blocks) blk = 0;  // unallocated entry: stay in bounds
+    my_off = (((int64_t)blk * block_size + key % block_size) * hkv + kvh) * D;
+  }
+
+  // ---- issue every K load of this warp before any arithmetic: 4 positions per
+  // round (8 lanes each, 128-byte contiguous segments), KCH pieces per lane
+  const int kq = lane >> 3, li = lane & 7;
+  constexpr int ROUNDS = kWarpKeys / 4;
+  uint4 kraw[ROUNDS][KCH];
+#pragma unroll
+  for (int rd = 0; rd < ROUNDS; ++rd) {
+    const int j = rd * 4 + kq;
+    const int64_t off = __shfl_sync(0xffffffffu, my_off, j);
+#pragma unroll
+    for (int c = 0; c < KCH; ++c)
+      kraw[rd][c] = (j < jn) ? ldg_nc_v4(kbase + off + c * 8 * V16 + li * V16) : make_uint4(0, 0, 0, 0);
+  }
+
+  // q rows -> fp32 smem (zeros for padding rows), while the K loads are in flight
   for (int i = tid; i < kRows * D; i += kAttnThreads) {
     const int r = i / D, d = i % D;
     float v = 0.f;
@@ -193,135 +222,365 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
     }
     qs[i] = v;
   }
-  if (tid < kRows) { m_s[tid] = -INFINITY; l_s[tid] = 0.f; }
-
-  // per-thread output accumulators: dim pair dp, rows r = grp + k*groups
-  constexpr int PAIRS = D / 2;
-  constexpr int GROUPS = kAttnThreads / PAIRS;  // 2 (D=256), 4 (128), 8 (64)
-  constexpr int RPT = kRows / GROUPS;           // rows per thread
-  const int dp = tid % PAIRS, grp = tid / PAIRS;
-  float acc0[RPT], acc1[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) { acc0[i] = 0.f; acc1[i] = 0.f; }
-
-  const int64_t plane = (int64_t)num_layers * num_blocks * block_size * hkv * D;  // K -> V plane offset
-  const KV* kbase = pages + (int64_t)layer * num_blocks * block_size * hkv * D;
-  const int32_t* table = block_tables + (int64_t)b * max_blocks;
-
-  auto issue_tile = [&](int stage, int t0) {
-    // 32 positions x D elements of K and of V, 16-byte pieces
-    constexpr int PIECES = D / V16;
-    for (int i = tid; i < kTile * PIECES; i += kAttnThreads) {
-      const int j = i / PIECES, c = i % PIECES;
-      const int p = t0 + j;
-      if (p < k_end) {
-        int blk = table[p / block_size];
-        if ((unsigned)blk >= (unsigned)num_blocks) blk = 0;  // unallocated entry: stay in bounds
-        const KV* src = kbase + (((int64_t)blk * block_size + (p % block_size)) * hkv + kvh) * D + c * V16;
-        cp_async16(kbuf[stage] + j * S::KSTRIDE + c * V16, src);
-        cp_async16(vbuf[stage] + j * D + c * V16, src + plane);
-      }
-    }
-    cp_async_commit();
-  };
-
-  const int ntiles = k_end > k_begin ? (k_end - k_begin + kTile - 1) / kTile : 0;
-  if (ntiles > 0) issue_tile(0, k_begin);
   __syncthreads();
 
-  for (int it = 0; it < ntiles; ++it) {
-    const int stage = it & 1;
-    const int t0 = k_begin + it * kTile;
-    if (it + 1 < ntiles) { issue_tile(stage ^ 1, t0 + kTile); cp_async_wait<1>(); }
-    else cp_async_wait<0>();
-    __syncthreads();
-
-    // ---- scores: warp = dim partition, lane = position
-    {
-      constexpr int DP = D / kParts;
-      const KV* krow = kbuf[stage] + lane * S::KSTRIDE + warp * DP;
-      float kv[DP];
+  // ---- scores: lane (kq, li) dots its pieces, the 8 lanes of a position reduce
+  float* pw = ps + warp * kRows * kWarpKeys;
 #pragma unroll
-      for (int c = 0; c < DP; c += V16) load16_to_f(krow + c, kv + c);
-      for (int r = 0; r < nrows; ++r) {
-        const float* qr = qs + r * D + warp * DP;
-        float s = 0.f;
+  for (int rd = 0; rd < ROUNDS; ++rd) {
+    const int j = rd * 4 + kq;
+    float part[kRows];
 #pragma unroll
-        for (int c = 0; c < DP; ++c) s = fmaf(qr[c], kv[c], s);
-        spart[(warp * kRows + r) * kTile + lane] = s;
-      }
-    }
-    __syncthreads();
-    // ---- online softmax: warp per row, lane = position
-    for (int r = warp; r < nrows; r += kAttnThreads / 32) {
-      const int p = t0 + lane;
-      float s = 0.f;
+    for (int r = 0; r < kRows; ++r) part[r] = 0.f;
 #pragma unroll
-      for (int w = 0; w < kParts; ++w) s += spart[(w * kRows + r) * kTile + lane];
-      const bool ok = (p < k_end) && (p <= ri.pos[r]);
-      s = ok ? s * scale : -INFINITY;
-      const float tmax = warp_max(s);
-      const float m_old = m_s[r];
-      const float m_new = fmaxf(m_old, tmax);
-      float pr = 0.f, alpha = 1.f;
-      if (m_new != -INFINITY) {
-        pr = ok ? expf(s - m_new) : 0.f;
-        alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-      }
-      const float psum = warp_sum(pr);
-      ps[r * kTile + lane] = pr;
-      if (lane == 0) {
-        m_s[r] = m_new;
-        l_s[r] = (m_new == -INFINITY) ? 0.f : l_s[r] * alpha + psum;
-        a_s[r] = alpha;
-      }
-    }
-    __syncthreads();
-    // ---- o = o * alpha + P V
-    {
-      const KV* vb = vbuf[stage];
+    for (int c = 0; c < KCH; ++c) {
+      float kv[V16];
+      if constexpr (V16 == 8) unpack8(kraw[rd][c], kv);
+      else { kv[0] = __uint_as_float(kraw[rd][c].x); kv[1] = __uint_as_float(kraw[rd][c].y);
+             kv[2] = __uint_as_float(kraw[rd][c].z); kv[3] = __uint_as_float(kraw[rd][c].w); }
 #pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const int r = grp + i * GROUPS;
+      for (int r = 0; r < kRows; ++r) {
         if (r < nrows) {
-          const float al = a_s[r];
-          acc0[i] *= al;
-          acc1[i] *= al;
-        }
-      }
-      const int jn = min(kTile, k_end - t0);
-      for (int j = 0; j < jn; ++j) {
-        const float v0 = to_f(vb[j * D + 2 * dp]);
-        const float v1 = to_f(vb[j * D + 2 * dp + 1]);
+          const float* qr = qs + r * D + c * 8 * V16 + li * V16;
 #pragma unroll
-        for (int i = 0; i < RPT; ++i) {
-          const int r = grp + i * GROUPS;
-          if (r < nrows) {
-            const float pj = ps[r * kTile + j];
-            acc0[i] = fmaf(pj, v0, acc0[i]);
-            acc1[i] = fmaf(pj, v1, acc1[i]);
-          }
+          for (int e = 0; e < V16; ++e) part[r] = fmaf(qr[e], kv[e], part[r]);
         }
       }
     }
-    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (r < nrows) {
+        float v = part[r];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (li == 0) pw[r * kWarpKeys + j] = v;
+      }
+    }
   }
 
-  // ---- partials: ws_o[(((b*hkv + kvh)*row_groups + rg)*nsplit + split)*kRows + r][D]
-  const int64_t base = (grp_id * nsplit + split) * kRows;
+  // ---- V loads for P.V (lane = DPL dims), issued before the softmax math
+  float vv[kWarpKeys][DPL];
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const int r = grp + i * GROUPS;
-    if (r < nrows) {
-      ws_o[(base + r) * D + 2 * dp] = acc0[i];
-      ws_o[(base + r) * D + 2 * dp + 1] = acc1[i];
+  for (int j = 0; j < kWarpKeys; ++j) {
+    const int64_t off = __shfl_sync(0xffffffffu, my_off, j);
+    if (j < jn) load_n<DPL>(kbase + plane + off + lane * DPL, vv[j]);
+    else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) vv[j][e] = 0.f;
     }
   }
-  if (tid < nrows) ws_ml[base + tid] = make_float2(m_s[tid], l_s[tid]);
+  __syncwarp();
+
+  // ---- softmax statistics of this warp's positions, per row (lane = position)
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    if (r < nrows) {
+      const int key = t0 + lane;
+      const bool ok = lane < jn && key <= ri.pos[r];
+      const float sc = ok ? pw[r * kWarpKeys + (lane & (kWarpKeys - 1))] * scale : -INFINITY;
+      const float m = warp_max(sc);
+      const float pr = (ok && m != -INFINITY) ? expf(sc - m) : 0.f;
+      const float l = warp_sum(pr);
+      __syncwarp();
+      if (lane < kWarpKeys) pw[r * kWarpKeys + lane] = pr;
+      if (lane == 0) mls[warp * kRows + r] = make_float2(m, l);
+    }
+  }
+  __syncwarp();
+
+  // ---- o = P.V
+  float o[kRows][DPL];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) o[r][e] = 0.f;
+#pragma unroll
+  for (int j = 0; j < kWarpKeys; ++j) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (r < nrows) {
+        const float pj = pw[r * kWarpKeys + j];
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(pj, vv[j][e], o[r][e]);
+      }
+    }
+  }
+  float* ow = os + warp * kRows * D;
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+    if (r < nrows)
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) ow[r * D + lane * DPL + e] = o[r][e];
+  __syncthreads();
+
+  // ---- combine the warps in warp order -> this split's partial per row
+  const int64_t base = (grp_id * nsplit + split) * kRows;
+  for (int i = tid; i < nrows * D; i += kAttnThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsA; ++w) M = fmaxf(M, mls[w * kRows + r].x);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarpsA; ++w) {
+        const float2 ml = mls[w * kRows + r];
+        const float wt = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
+        L += ml.y * wt;
+        O += os[(w * kRows + r) * D + d] * wt;
+      }
+    }
+    ws_o[(base + r) * D + d] = O;
+    if (d == 0) ws_ml[base + r] = make_float2(M, L);
+  }
+  pdl_trigger();
 
   if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+  attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, os);
+}
 
-  attention_fold<KV, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, spart);
+// ---------------------------------------------------------------- K1, bf16 on tensor cores
+// Same decomposition and partial/fold protocol as paged_attention_kernel, but
+// each warp's 16 positions go through mma.sync m16n8k16 (bf16 in, fp32
+// accumulate): S[16 rows x 16 positions] = Q K^T over D/16 k-steps, the row
+// softmax of the warp's positions on the S fragments, then O[16 x D] += P V with
+// P re-packed from the S accumulators as the A operand.  K/V rows of the warp are
+// staged in shared memory with cp.async (positions past the end are
+// zero-filled, so P = 0 never meets stale data), Q once per CTA; fragments come
+// from ldmatrix (.trans for V).  P is rounded to bf16 before P.V.
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D>
+struct TcSmem {
+  static constexpr int STRIDE = D + 8;                         // bf16 elements per row (+16 B: ldmatrix conflict-free)
+  static constexpr size_t q_bytes = 2ull * 16 * STRIDE;
+  static constexpr size_t kv_bytes = 2ull * kWarpsA * kWarpKeys * STRIDE;   // per plane
+  static constexpr size_t o_bytes = sizeof(float) * kWarpsA * kRows * D;   // aliases the K tiles
+  static constexpr size_t ml_bytes = sizeof(float2) * kWarpsA * kRows;
+  static constexpr size_t total = q_bytes + 2 * kv_bytes + ml_bytes + 128;
+  static_assert(o_bytes <= kv_bytes, "warp outputs must fit in the K tiles");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+paged_attention_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ pages, int num_layers,
+                          int num_blocks, int block_size, int hkv, int layer, const int32_t* __restrict__ block_tables,
+                          int max_blocks, const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ q_lens,
+                          bf16* __restrict__ out, float scale, int T, int hq, int row_groups, int nsplit,
+                          float* __restrict__ ws_o, float2* __restrict__ ws_ml, unsigned int* __restrict__ counters) {
+  using S = TcSmem<D>;
+  constexpr int ST = S::STRIDE;
+  constexpr int KSTEPS = D / 16;
+  constexpr int NT = D / 8;              // n-tiles of P.V
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* qs = reinterpret_cast<bf16*>(smem);                                // [16][ST]
+  bf16* ks = reinterpret_cast<bf16*>(smem + S::q_bytes);                   // [warp][16][ST]
+  bf16* vs = reinterpret_cast<bf16*>(smem + S::q_bytes + S::kv_bytes);     // [warp][16][ST]
+  float* os = reinterpret_cast<float*>(ks);                                // [warp][kRows][D] after P.V
+  float2* mls = reinterpret_cast<float2*>(smem + S::q_bytes + 2 * S::kv_bytes);
+  __shared__ RowInfo ri;
+  __shared__ bool is_last;
+
+  pdl_wait();
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / row_groups, rg = blockIdx.y % row_groups;
+  const int b = blockIdx.z;
+  const int G = hq / hkv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seq_len = seq_lens[b];
+  const int ql = q_lens ? q_lens[b] : T;
+  const int total_rows = G * T;
+  const int row0 = rg * kRows;
+  if (tid == 0) {
+    ri.nrows = min(kRows, total_rows - row0);
+    for (int r = 0; r < kRows; ++r) {
+      const int gr = row0 + r;
+      const int t = gr / G;
+      ri.pos[r] = (r < ri.nrows && t < ql) ? seq_len - ql + t : -1;
+    }
+  }
+  __syncthreads();
+  const int nrows = ri.nrows;
+  int kmax = 0;
+  for (int r = 0; r < nrows; ++r) kmax = max(kmax, ri.pos[r] + 1);
+  const int k_begin = split * kChunk;
+  const int k_end = min(min(min(k_begin + kChunk, kmax), seq_len), max_blocks * block_size);
+  const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
+  if (k_end <= k_begin) {
+    if (tid < nrows) ws_ml[(grp_id * nsplit + split) * kRows + tid] = make_float2(-INFINITY, 0.f);
+    pdl_trigger();
+    if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+    attention_fold<bf16, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b,
+                            reinterpret_cast<float*>(ks));
+    return;
+  }
+
+  const int64_t plane = (int64_t)num_layers * num_blocks * block_size * hkv * D;
+  const bf16* kbase = pages + (int64_t)layer * num_blocks * block_size * hkv * D;
+  const int32_t* table = block_tables + (int64_t)b * max_blocks;
+  const int t0 = k_begin + warp * kWarpKeys;
+  const int jn = max(0, min(kWarpKeys, k_end - t0));
+
+  // ---- stage this warp's K and V rows (16 B pieces, zero-fill past the end)
+  {
+    int64_t my_off = 0;
+    if (lane < jn) {
+      const int key = t0 + lane;
+      int blk = table[key / block_size];
+      if ((unsigned)blk >= (unsigned)num_blocks) blk = 0;
+      my_off = (((int64_t)blk * block_size + key % block_size) * hkv + kvh) * D;
+    }
+    constexpr int PIECES = D / 8;                 // 16-byte pieces per row
+    const uint32_t kw = (uint32_t)__cvta_generic_to_shared(ks + warp * kWarpKeys * ST);
+    const uint32_t vw = (uint32_t)__cvta_generic_to_shared(vs + warp * kWarpKeys * ST);
+#pragma unroll 4
+    for (int i = lane; i < kWarpKeys * PIECES; i += 32) {
+      const int j = i / PIECES, c = i % PIECES;
+      const int64_t off = __shfl_sync(0xffffffffu, my_off, j);
+      const bool valid = j < jn;
+      const bf16* src = kbase + (valid ? off : 0) + c * 8;
+      cp_async16_zfill(kw + (uint32_t)(j * ST + c * 8) * 2, src, valid);
+      cp_async16_zfill(vw + (uint32_t)(j * ST + c * 8) * 2, src + plane, valid);
+    }
+    asm volatile("cp.async.commit_group;");
+  }
+  // ---- Q rows (bf16, zero padding rows) while the K/V copies are in flight
+  for (int i = tid; i < 16 * (D / 8); i += kAttnThreads) {
+    const int r = i / (D / 8), c = i % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nrows && ri.pos[r] >= 0) {
+      const int gr = row0 + r, t = gr / G, g = gr % G;
+      v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * T + t) * hq + kvh * G + g) * D + c * 8);
+    }
+    *reinterpret_cast<uint4*>(qs + r * ST + c * 8) = v;
+  }
+  asm volatile("cp.async.wait_group 0;");
+  __syncthreads();
+
+  // ---- S = Q K^T for the warp's 16 positions (2 n-tiles of 8)
+  float sacc[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
+  const uint32_t qaddr0 = (uint32_t)__cvta_generic_to_shared(qs);
+  const uint32_t kaddr0 = (uint32_t)__cvta_generic_to_shared(ks + warp * kWarpKeys * ST);
+  const uint32_t vaddr0 = (uint32_t)__cvta_generic_to_shared(vs + warp * kWarpKeys * ST);
+  const int lr = lane & 7, lm = lane >> 3;     // ldmatrix: row within matrix, matrix index
+#pragma unroll
+  for (int ks_ = 0; ks_ < KSTEPS; ++ks_) {
+    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+    // A: rows lr + 8*(lm&1), dims 16ks + 8*(lm>>1)
+    ldsm_x4(qaddr0 + (uint32_t)((lr + 8 * (lm & 1)) * ST + 16 * ks_ + 8 * (lm >> 1)) * 2, a0, a1, a2, a3);
+    // B: positions 8*(lm>>1) + lr, dims 16ks + 8*(lm&1)
+    ldsm_x4(kaddr0 + (uint32_t)((8 * (lm >> 1) + lr) * ST + 16 * ks_ + 8 * (lm & 1)) * 2, b0, b1, b2, b3);
+    mma_bf16_16816(sacc[0], a0, a1, a2, a3, b0, b1);
+    mma_bf16_16816(sacc[1], a0, a1, a2, a3, b2, b3);
+  }
+  // ---- softmax of the warp's positions per row (rows lane/4 and lane/4 + 8;
+  // only rows < kRows = 8 are real, the upper half of the tile stays empty)
+  const int rA = lane >> 2;
+  const int prow = (rA < nrows) ? ri.pos[rA] : -1;
+  float pa[2][2];
+  float m = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = t0 + nt * 8 + (lane & 3) * 2 + e;
+      const bool ok = (key < k_end) && (key <= prow);
+      pa[nt][e] = ok ? sacc[nt][e] * scale : -INFINITY;
+      m = fmaxf(m, pa[nt][e]);
+    }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  float l = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float pv = (m == -INFINITY || pa[nt][e] == -INFINITY) ? 0.f : expf(pa[nt][e] - m);
+      pa[nt][e] = pv;
+      l += pv;
+    }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if ((lane & 3) == 0 && rA < kRows) mls[warp * kRows + rA] = make_float2(m, l);
+  // P as the A operand (rows 8-15 are zero)
+  const uint32_t pa0 = pack_bf16(pa[0][0], pa[0][1]), pa1 = 0u;
+  const uint32_t pa2 = pack_bf16(pa[1][0], pa[1][1]), pa3 = 0u;
+
+  // ---- O = P V: n-tiles of 8 dims, two per ldmatrix.trans
+  float oacc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) oacc[nt][e] = 0.f;
+#pragma unroll
+  for (int np = 0; np < NT / 2; ++np) {
+    uint32_t b0, b1, b2, b3;
+    // matrices: (dims 16np + 8*(lm>>1), positions 8*(lm&1) + lr)
+    ldsm_x4_t(vaddr0 + (uint32_t)((8 * (lm & 1) + lr) * ST + 16 * np + 8 * (lm >> 1)) * 2, b0, b1, b2, b3);
+    mma_bf16_16816(oacc[2 * np], pa0, pa1, pa2, pa3, b0, b1);
+    mma_bf16_16816(oacc[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+  }
+  __syncthreads();  // every warp is done reading its K tile: the outputs may overwrite it
+  float* ow = os + warp * kRows * D;
+  if (rA < nrows) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      ow[rA * D + nt * 8 + (lane & 3) * 2] = oacc[nt][0];
+      ow[rA * D + nt * 8 + (lane & 3) * 2 + 1] = oacc[nt][1];
+    }
+  }
+  __syncthreads();
+
+  // ---- combine the warps in warp order -> this split's partial per row
+  const int64_t base = (grp_id * nsplit + split) * kRows;
+  for (int i = tid; i < nrows * D; i += kAttnThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsA; ++w) M = fmaxf(M, mls[w * kRows + r].x);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarpsA; ++w) {
+        const float2 ml = mls[w * kRows + r];
+        const float wt = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
+        L += ml.y * wt;
+        O += os[(w * kRows + r) * D + d] * wt;
+      }
+    }
+    ws_o[(base + r) * D + d] = O;
+    if (d == 0) ws_ml[base + r] = make_float2(M, L);
+  }
+  pdl_trigger();
+  if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+  attention_fold<bf16, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, os);
 }
 
 // ---------------------------------------------------------------- K2
@@ -330,6 +589,8 @@ __global__ void kv_write_kernel(KV* __restrict__ pages, int num_layers, int num_
                                 int D, int layer, const int32_t* __restrict__ block_tables, int max_blocks,
                                 const int32_t* __restrict__ positions, const KV* __restrict__ k,
                                 const KV* __restrict__ v, int T) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y, t = blockIdx.x;
   const int p = positions[(int64_t)b * T + t];
   if (p < 0 || p / block_size >= max_blocks) return;
@@ -353,6 +614,8 @@ __global__ void rope_kv_write_kernel(const KV* __restrict__ qkv, KV* __restrict_
                                      int layer, const int32_t* __restrict__ block_tables, int max_blocks,
                                      const int32_t* __restrict__ positions, const float* __restrict__ cos_t,
                                      const float* __restrict__ sin_t, int rope_max_pos, int T) {
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, t = blockIdx.y, b = blockIdx.z;
   const int64_t m = (int64_t)b * T + t;
   const int p = positions[m];
@@ -416,6 +679,25 @@ inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_
   return L;
 }
 
+template <int D>
+int launch_attention_tc(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks,
+                        int block_size, int hkv, int layer, const int32_t* tables, int max_blocks,
+                        const int32_t* seq_lens, const int32_t* q_lens, void* out, float scale, int B, int T, int hq,
+                        const AttnLayout& L, void* ws) {
+  using S = TcSmem<D>;
+  auto kern = paged_attention_tc_kernel<D>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total) != cudaSuccess)
+    return SSD_ERR_LAUNCH;
+  char* w = reinterpret_cast<char*>(ws);
+  dim3 grid(L.nsplit, hkv * L.row_groups, B);
+  SSD_PDL(kern, grid, kAttnThreads, S::total, st, reinterpret_cast<const bf16*>(q),
+          reinterpret_cast<const bf16*>(pages), num_layers, num_blocks, block_size, hkv, layer, tables, max_blocks,
+          seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups, L.nsplit,
+          reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
+          reinterpret_cast<unsigned int*>(w + L.off_cnt));
+  return SSD_OK;
+}
+
 template <typename KV, int D>
 int launch_attention(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks,
                      int block_size, int hkv, int layer, const int32_t* tables, int max_blocks,
@@ -427,7 +709,7 @@ int launch_attention(cudaStream_t st, const void* q, const void* pages, int num_
     return SSD_ERR_LAUNCH;
   char* w = reinterpret_cast<char*>(ws);
   dim3 grid(L.nsplit, hkv * L.row_groups, B);
-  kern<<<grid, kAttnThreads, S::total, st>>>(
+  SSD_PDL(kern, grid, kAttnThreads, S::total, st, 
       reinterpret_cast<const KV*>(q), reinterpret_cast<const KV*>(pages), num_layers, num_blocks, block_size, hkv,
       layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<KV*>(out), scale, T, hq, L.row_groups,
       L.nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
@@ -470,6 +752,16 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
   return launch_attention<KVT, DD>(st, q, pages, num_layers, num_blocks, block_size, num_kv_heads, layer,       \
                                    block_tables, max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, L, \
                                    workspace)
+#define SSD_ATTN_TC(DD)                                                                                       \
+  return launch_attention_tc<DD>(st, q, pages, num_layers, num_blocks, block_size, num_kv_heads, layer,        \
+                                 block_tables, max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, L,  \
+                                 workspace)
+  const bool aligned16 = !(reinterpret_cast<uintptr_t>(q) & 15) && !(reinterpret_cast<uintptr_t>(pages) & 15);
+  if (dtype == SSD_DTYPE_BF16 && aligned16) {
+    if (head_dim == 256) SSD_ATTN_TC(256);
+    if (head_dim == 128) SSD_ATTN_TC(128);
+    if (head_dim == 64) SSD_ATTN_TC(64);
+  }
   if (dtype == SSD_DTYPE_BF16) {
     if (head_dim == 256) SSD_ATTN_CASE(bf16, 256);
     if (head_dim == 128) SSD_ATTN_CASE(bf16, 128);
@@ -480,6 +772,7 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
     if (head_dim == 64) SSD_ATTN_CASE(float, 64);
   }
 #undef SSD_ATTN_CASE
+#undef SSD_ATTN_TC
   return SSD_ERR_UNSUPPORTED;
 }
 
@@ -492,11 +785,11 @@ extern "C" int ssd_kv_write(ssd_stream_t stream, void* pages, int dtype, int num
   dim3 grid(T, B);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == SSD_DTYPE_BF16)
-    kv_write_kernel<bf16><<<grid, 256, 0, st>>>(reinterpret_cast<bf16*>(pages), num_layers, num_blocks, block_size,
+    SSD_PDL(kv_write_kernel<bf16>, grid, 256, 0, st, reinterpret_cast<bf16*>(pages), num_layers, num_blocks, block_size,
                                                 num_kv_heads, head_dim, layer, block_tables, max_blocks, positions,
                                                 reinterpret_cast<const bf16*>(k), reinterpret_cast<const bf16*>(v), T);
   else if (dtype == SSD_DTYPE_F32)
-    kv_write_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<float*>(pages), num_layers, num_blocks,
+    SSD_PDL(kv_write_kernel<float>, grid, 256, 0, st, reinterpret_cast<float*>(pages), num_layers, num_blocks,
                                                  block_size, num_kv_heads, head_dim, layer, block_tables, max_blocks,
                                                  positions, reinterpret_cast<const float*>(k),
                                                  reinterpret_cast<const float*>(v), T);
@@ -519,12 +812,12 @@ extern "C" int ssd_rope_kv_write(ssd_stream_t stream, const void* qkv, void* q_o
   const int threads = head_dim / 2 < 32 ? 32 : (head_dim / 2 > 256 ? 256 : head_dim / 2);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == SSD_DTYPE_BF16)
-    rope_kv_write_kernel<bf16><<<grid, threads, 0, st>>>(
+    SSD_PDL(rope_kv_write_kernel<bf16>, grid, threads, 0, st, 
         reinterpret_cast<const bf16*>(qkv), reinterpret_cast<bf16*>(q_out), reinterpret_cast<bf16*>(pages),
         num_layers, num_blocks, block_size, num_heads, num_kv_heads, head_dim, layer, block_tables, max_blocks,
         positions, rope_cos, rope_sin, rope_max_pos, T);
   else if (dtype == SSD_DTYPE_F32)
-    rope_kv_write_kernel<float><<<grid, threads, 0, st>>>(
+    SSD_PDL(rope_kv_write_kernel<float>, grid, threads, 0, st, 
         reinterpret_cast<const float*>(qkv), reinterpret_cast<float*>(q_out), reinterpret_cast<float*>(pages),
         num_layers, num_blocks, block_size, num_heads, num_kv_heads, head_dim, layer, block_tables, max_blocks,
         positions, rope_cos, rope_sin, rope_max_pos, T);

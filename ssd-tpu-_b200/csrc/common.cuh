@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/ssd_verify.h"
 
 namespace ssd {
@@ -133,7 +135,42 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
+// Programmatic dependent launch.  Every kernel of the verify path is launched
+// with launch_pdl, so it may start while its predecessor in the stream is still
+// draining.  pdl_wait() blocks until the predecessor grid has completed and its
+// writes are visible: call it before reading anything an earlier kernel wrote
+// (a no-op when the launch had no programmatic dependency).  pdl_trigger() lets
+// the next kernel launch; kernels call it once their CTA's main work is issued.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 }  // namespace ssd
+
+// Launch through launch_pdl and turn a launch failure into SSD_ERR_LAUNCH.
+#define SSD_PDL(kern, grid, block, smem, st, ...)                                        \
+  do {                                                                                   \
+    if (::ssd::launch_pdl(kern, dim3(grid), dim3(block), (size_t)(smem), (cudaStream_t)(st), \
+                          __VA_ARGS__) != cudaSuccess) {                                 \
+      (void)cudaGetLastError();                                                          \
+      return SSD_ERR_LAUNCH;                                                             \
+    }                                                                                    \
+  } while (0)
 
 #define SSD_CHECK_LAUNCH()                               \
   do {                                                   \

@@ -52,6 +52,7 @@ linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restr
   T* xs = reinterpret_cast<T*>(smem_raw);  // [M][kc]
   __shared__ bool is_last;
 
+  pdl_wait();
   const int tile = blockIdx.x, split = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k0 = split * kc;
@@ -101,6 +102,7 @@ linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restr
   for (int r = 0; r < ROWS; ++r)
 #pragma unroll
     for (int m = 0; m < MMAX; ++m) acc[r][m] = warp_sum(acc[r][m]);
+  pdl_trigger();
 
   if (splits == 1) {
     if (lane == 0) {
@@ -180,7 +182,7 @@ static int launch_cc(cudaStream_t st, const void* x, const void* w, void* y, int
     return SSD_ERR_LAUNCH;
   unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
   float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
-  kern<<<dim3(tiles, p.splits), kLinThreads, smem, st>>>(reinterpret_cast<const T*>(x), reinterpret_cast<const T*>(w),
+  SSD_PDL(kern, dim3(tiles, p.splits), kLinThreads, smem, st, reinterpret_cast<const T*>(x), reinterpret_cast<const T*>(w),
                                                          y, epi, M, N, K, p.splits, p.kc, part, counters);
   SSD_CHECK_LAUNCH();
   return SSD_OK;

@@ -143,7 +143,9 @@ struct Cfg {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = MP * BK * 2;
   static constexpr uint32_t STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = MP <= 16 ? 10 : MP <= 32 ? 9 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
+  // MP <= 32: a ring small enough (<= 113 KB) that the next projection's CTA can
+  // share the SM and prefetch its weights while this one drains (PDL).
+  static constexpr int STAGES = MP <= 16 ? 6 : MP <= 32 ? 5 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
   static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;
   static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
@@ -152,7 +154,7 @@ struct Cfg {
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <int MP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads)
 linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const Params p) {
   using C = Cfg<MP>;
@@ -207,7 +209,24 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int u = u0; u < u1; ++u) {
+      // Weights never depend on the previous kernel: start streaming the first
+      // ring's worth of weight blocks before waiting for it (PDL), then add the
+      // token blocks of those stages once its outputs are visible.
+      const int pre = min(S, u1 - u0);
+      for (int i = 0; i < pre; ++i) {
+        const int u = u0 + i, tile = u / p.KB, kb = u - tile * p.KB;
+        mbar_expect_tx(full(i), C::STAGE);
+        tma_load_2d(base + i * C::STAGE, &wmap, full(i), kb * BK, tile * BM);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const int u = u0 + i, kb = u - (u / p.KB) * p.KB;
+        tma_load_2d(base + i * C::STAGE + C::A_BYTES, &xmap, full(i), kb * BK, 0);
+      }
+      issued = pre;
+      stage = pre % S;
+      phase = (pre == S) ? 1u : 0u;
+      for (int u = u0 + pre; u < u1; ++u) {
         const int tile = u / p.KB, kb = u - tile * p.KB;
         if (!wait_bounded(empty(stage), phase ^ 1u, abort_flag, p.err, 1)) break;
         mbar_expect_tx(full(stage), C::STAGE);
@@ -217,6 +236,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         ++issued;
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
+      pdl_trigger();  // all loads issued: the next kernel may start its prologue
       if (*abort_flag) {
         // drain: wait (bounded, ignoring the abort flag) for the loads still in flight
         for (int i = 0; i < S && i < issued; ++i) {
@@ -270,6 +290,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // outputs, residual inputs and the workspace belong to the previous kernel until it ends
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const int row = q * 32 + lane;
     int seg = 0;
@@ -472,7 +493,7 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   auto kern = linear_tc_kernel<MP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
     return SSD_ERR_LAUNCH;
-  kern<<<grid, kThreads, C::SMEM, st>>>(wm, xm, p);
+  SSD_PDL(kern, grid, kThreads, C::SMEM, st, wm, xm, p);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }

@@ -21,6 +21,8 @@ namespace {
 template <typename T>
 __global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __restrict__ E, T* __restrict__ x, int d,
                              int vocab, float scale) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   int tok = tokens[m];
   tok = tok < 0 ? 0 : (tok >= vocab ? vocab - 1 : tok);
@@ -33,6 +35,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __rest
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int d, float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const T* xr = x + (int64_t)m * d;
   float s = 0.f;
@@ -50,6 +54,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
 __global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                               bf16* __restrict__ y, int d, float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const int nv = d / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)m * d);
@@ -92,6 +98,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __res
 __global__ void positions_kernel(const int32_t* __restrict__ slb, const int32_t* __restrict__ ql, int B, int T,
                                  int32_t* __restrict__ pos, int32_t* __restrict__ seq_after,
                                  int32_t* __restrict__ qlen_out) {
+  pdl_wait();
+  pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * T; i += gridDim.x * blockDim.x) {
     const int b = i / T, t = i % T;
     const int q = ql ? ql[b] : T;
@@ -107,6 +115,8 @@ __global__ void positions_kernel(const int32_t* __restrict__ slb, const int32_t*
 template <typename T>
 __global__ void gather_last_kernel(const T* __restrict__ h, const int32_t* __restrict__ qlen, int tq, int d,
                                    T* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int t = min(max(qlen[b] - 1, 0), tq - 1);
   for (int i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)b * d + i] = h[((int64_t)b * tq + t) * d + i];
@@ -220,9 +230,9 @@ extern "C" int ssd_embed(ssd_stream_t stream, const int32_t* tokens, const void*
   float scale = sqrtf((float)d);
   if (dtype == SSD_DTYPE_BF16) {
     scale = __bfloat162float(__float2bfloat16_rn(scale));
-    embed_kernel<bf16><<<M, 256, 0, st>>>(tokens, (const bf16*)embed, (bf16*)x, d, vocab, scale);
+    SSD_PDL(embed_kernel<bf16>, M, 256, 0, st, tokens, (const bf16*)embed, (bf16*)x, d, vocab, scale);
   } else if (dtype == SSD_DTYPE_F32) {
-    embed_kernel<float><<<M, 256, 0, st>>>(tokens, (const float*)embed, (float*)x, d, vocab, scale);
+    SSD_PDL(embed_kernel<float>, M, 256, 0, st, tokens, (const float*)embed, (float*)x, d, vocab, scale);
   } else {
     return SSD_ERR_INVALID;
   }
@@ -237,11 +247,11 @@ extern "C" int ssd_rmsnorm(ssd_stream_t stream, const void* x, const void* w, in
   const bool vec = (d % 8 == 0) && d <= 8 * 256 * 4 && !(reinterpret_cast<uintptr_t>(x) & 15) &&
                    !(reinterpret_cast<uintptr_t>(w) & 15) && !(reinterpret_cast<uintptr_t>(y) & 15);
   if (dtype == SSD_DTYPE_BF16 && vec)
-    rmsnorm_bf16_vec_kernel<<<M, 256, 0, st>>>((const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
+    SSD_PDL(rmsnorm_bf16_vec_kernel, M, 256, 0, st, (const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
   else if (dtype == SSD_DTYPE_BF16)
-    rmsnorm_kernel<bf16><<<M, 256, 0, st>>>((const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
+    SSD_PDL(rmsnorm_kernel<bf16>, M, 256, 0, st, (const bf16*)x, (const bf16*)w, (bf16*)y, d, eps);
   else if (dtype == SSD_DTYPE_F32)
-    rmsnorm_kernel<float><<<M, 256, 0, st>>>((const float*)x, (const float*)w, (float*)y, d, eps);
+    SSD_PDL(rmsnorm_kernel<float>, M, 256, 0, st, (const float*)x, (const float*)w, (float*)y, d, eps);
   else
     return SSD_ERR_INVALID;
   SSD_CHECK_LAUNCH();
@@ -313,7 +323,7 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
   };
   if (bt->prof_count) *bt->prof_count = 0;
 
-  positions_kernel<<<(M + 255) / 256, 256, 0, st>>>(bt->seq_lens_before, bt->q_lens, B, T, s.pos, s.seq_after,
+  SSD_PDL(positions_kernel, (M + 255) / 256, 256, 0, st, bt->seq_lens_before, bt->q_lens, B, T, s.pos, s.seq_after,
                                                      s.qlen);
   SSD_CHECK_LAUNCH();
   SSD_TRY(ssd_embed(stream, bt->tokens, w->embed, dt, s.x, M, d, w->vocab));
@@ -335,9 +345,9 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
   SSD_TRY(ssd_rmsnorm(stream, s.x, w->final_norm, dt, s.h, M, d, w->eps));
   if (bt->logits_last_only) {
     if (dt == SSD_DTYPE_BF16)
-      gather_last_kernel<bf16><<<B, 256, 0, st>>>((const bf16*)s.h, s.qlen, T, d, (bf16*)s.hl);
+      SSD_PDL(gather_last_kernel<bf16>, B, 256, 0, st, (const bf16*)s.h, s.qlen, T, d, (bf16*)s.hl);
     else
-      gather_last_kernel<float><<<B, 256, 0, st>>>((const float*)s.h, s.qlen, T, d, (float*)s.hl);
+      SSD_PDL(gather_last_kernel<float>, B, 256, 0, st, (const float*)s.h, s.qlen, T, d, (float*)s.hl);
     SSD_CHECK_LAUNCH();
     SSD_TRY(proj(4, s.hl, w->embed, bt->logits, SSD_EPI_STORE_F32, B, w->vocab, d));
   } else {

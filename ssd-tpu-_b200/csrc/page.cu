@@ -44,6 +44,7 @@ page_allocate_kernel(int32_t* tables, int32_t* lens, int max_blocks, int32_t* fr
   __shared__ int s_extra[kPageThreads];
   __shared__ int s_start[kPageThreads];  // free-list top seen by the sequence
   __shared__ int s_top;
+  pdl_wait();
   if (threadIdx.x == 0) s_top = *free_top;
   __syncthreads();
   for (int base = 0; base < B; base += kPageThreads) {
@@ -90,6 +91,7 @@ page_allocate_kernel(int32_t* tables, int32_t* lens, int max_blocks, int32_t* fr
     __syncthreads();
   }
   if (threadIdx.x == 0) *free_top = s_top;
+  pdl_trigger();
 }
 
 // Release events in sequence order.  mode 0 = rollback (pop from the end while
@@ -103,6 +105,7 @@ page_release_kernel(int mode, int32_t* tables, int32_t* lens, int max_blocks, in
   __shared__ int s_blk[kEventCap];
   __shared__ int s_off[kPageThreads];
   __shared__ int s_top;
+  pdl_wait();
   if (threadIdx.x == 0) s_top = *free_top;
   __syncthreads();
 
@@ -188,6 +191,7 @@ page_release_kernel(int mode, int32_t* tables, int32_t* lens, int max_blocks, in
     __syncthreads();
   }
   if (threadIdx.x == 0) *free_top = s_top;
+  pdl_trigger();
 }
 
 }  // namespace
@@ -203,7 +207,7 @@ extern "C" int ssd_page_allocate(ssd_stream_t stream, int32_t* block_tables, int
   if (B == 0) return SSD_OK;
   if (!block_tables || !table_lens || !free_list || !free_top || !ref_counts || !num_tokens || !num_new)
     return SSD_ERR_INVALID;
-  page_allocate_kernel<<<1, kPageThreads, 0, (cudaStream_t)stream>>>(block_tables, table_lens, max_blocks,
+  SSD_PDL(page_allocate_kernel, 1, kPageThreads, 0, (cudaStream_t)stream, block_tables, table_lens, max_blocks,
                                                                      free_list, free_top, ref_counts, num_blocks,
                                                                      num_tokens, num_new, ok, block_size, B);
   SSD_CHECK_LAUNCH();
@@ -218,7 +222,7 @@ extern "C" int ssd_page_rollback(ssd_stream_t stream, int32_t* block_tables, int
   if (B == 0) return SSD_OK;
   if (!block_tables || !table_lens || !free_list || !free_top || !ref_counts || !num_tokens || !accepted)
     return SSD_ERR_INVALID;
-  page_release_kernel<<<1, kPageThreads, 0, (cudaStream_t)stream>>>(
+  SSD_PDL(page_release_kernel, 1, kPageThreads, 0, (cudaStream_t)stream, 
       0, block_tables, table_lens, max_blocks, nullptr, nullptr, 0, free_list, free_top, ref_counts, num_blocks,
       num_tokens, accepted, kv_lens, nullptr, block_size, B);
   SSD_CHECK_LAUNCH();
@@ -232,7 +236,7 @@ extern "C" int ssd_page_free(ssd_stream_t stream, int32_t* block_tables, int32_t
   if (B == 0) return SSD_OK;
   if (!block_tables || !table_lens || !free_list || !free_top || !ref_counts || !release) return SSD_ERR_INVALID;
   if (draft_tables && (!draft_lens || draft_max_blocks <= 0)) return SSD_ERR_INVALID;
-  page_release_kernel<<<1, kPageThreads, 0, (cudaStream_t)stream>>>(
+  SSD_PDL(page_release_kernel, 1, kPageThreads, 0, (cudaStream_t)stream, 
       1, block_tables, table_lens, max_blocks, draft_tables, draft_lens, draft_max_blocks, free_list, free_top,
       ref_counts, num_blocks, nullptr, nullptr, nullptr, release, 1, B);
   SSD_CHECK_LAUNCH();

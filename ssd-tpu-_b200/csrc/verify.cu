@@ -99,6 +99,7 @@ greedy_scan_kernel(const float* __restrict__ x, int64_t ld, int V, int kp1, int 
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
   __shared__ int tt[64];
+  pdl_wait();
   const int row = blockIdx.y, c = blockIdx.x;
   int lo, hi;
   chunk_bounds(V, nchunks, c, lo, hi);
@@ -107,6 +108,7 @@ greedy_scan_kernel(const float* __restrict__ x, int64_t ld, int V, int kp1, int 
   scan_argmax(x + (int64_t)row * ld, lo, hi, vec_ok, best, bidx);
   unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
   if (threadIdx.x == 0) partial[(int64_t)row * nchunks + c] = key;
+  pdl_trigger();
 
   const int group = row / kp1;
   if (!last_block_of(&counters[group], (unsigned)(kp1 * nchunks), &is_last)) return;
@@ -169,6 +171,7 @@ sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, 
   __shared__ float redf[32];
   __shared__ bool is_last;
   __shared__ float2 stats[130];
+  pdl_wait();
   const int nP = K + 1 - off, nR = nP + K;
   const int b = blockIdx.y / nR, r = blockIdx.y % nR;
   const bool is_p = r < nP;
@@ -201,6 +204,7 @@ sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, 
   m = M;
   s = sc;
   if (threadIdx.x == 0) part[(int64_t)blockIdx.y * nchunks + blockIdx.x] = make_float2(m, s);
+  pdl_trigger();
 
   if (!last_block_of(&counters[b], (unsigned)(nR * nchunks), &is_last)) return;
   // Fold chunk partials per row: M = max m_i, S = sum s_i * exp(m_i - M), chunk order.
@@ -247,8 +251,10 @@ sample_residual_kernel(const float* __restrict__ lp, const float* __restrict__ l
                        float* __restrict__ part, SampleDecision* __restrict__ dec) {
   __shared__ float redf[32];
   __shared__ bool is_last;
+  pdl_wait();
   const int b = blockIdx.y;
   const SampleDecision d = dec[b];
+  pdl_trigger();
   if (d.bonus) return;  // uniform over the group: no CTA touches the counter
   const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
   const float* qrow = lq + ((int64_t)b * K + d.qrow) * V;
@@ -279,6 +285,7 @@ sample_draw_kernel(const float* __restrict__ lp, const float* __restrict__ lq,
                    int32_t* __restrict__ recovery, uint8_t* __restrict__ mask) {
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
+  pdl_wait();
   const int b = blockIdx.y;
   const SampleDecision d = dec[b];
   const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
@@ -303,6 +310,7 @@ sample_draw_kernel(const float* __restrict__ lp, const float* __restrict__ lq,
   }
   unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
   if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = key;
+  pdl_trigger();
   if (!last_block_of(&counters[b], (unsigned)nchunks, &is_last)) return;
   if (threadIdx.x == 0) {
     unsigned long long k = 0ull;
@@ -333,12 +341,16 @@ __device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t i) {
 }
 
 __global__ void uniform_fill_kernel(float* out, int64_t n, uint64_t seed, uint64_t offset) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = hash_uniform(seed, offset + (uint64_t)i);
 }
 
 template <typename T>
 __global__ void normal_fill_kernel(T* out, int64_t n, float std, uint64_t seed) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float u1 = hash_uniform(seed, 2 * (uint64_t)i);
     const float u2 = hash_uniform(seed, 2 * (uint64_t)i + 1);
@@ -371,7 +383,7 @@ static int launch_greedy(cudaStream_t st, const float* x, int64_t ld, int rows, 
   unsigned long long* part = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ws) + kCounterBytes);
   const bool vec_ok = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   dim3 grid(nch, rows);
-  greedy_scan_kernel<<<grid, kScanThreads, 0, st>>>(x, ld, V, kp1, nch, vec_ok, counters, part, spec, acc,
+  SSD_PDL(greedy_scan_kernel, grid, kScanThreads, 0, st, x, ld, V, kp1, nch, vec_ok, counters, part, spec, acc,
                                                      rec, mask, tt, amax);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
@@ -440,7 +452,7 @@ extern "C" int ssd_verify_greedy_noalloc(ssd_stream_t stream, const float* logit
   unsigned long long* part =
       reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(base) + kNoAllocCounterBytes);
   const bool vec_ok = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits_p) & 15) == 0);
-  greedy_scan_kernel<<<dim3(nch, (unsigned)rows), kScanThreads, 0, st>>>(logits_p, V, V, K + 1, nch, vec_ok, counters,
+  SSD_PDL(greedy_scan_kernel, dim3(nch, (unsigned)rows), kScanThreads, 0, st, logits_p, V, V, K + 1, nch, vec_ok, counters,
                                                                          part, speculations, accept_until, recovery,
                                                                          accepted_mask, target_tokens, nullptr);
   SSD_CHECK_LAUNCH();
@@ -500,16 +512,16 @@ extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, con
   cudaStream_t st = (cudaStream_t)stream;
   const bool vec_ok = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits_p) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(logits_q) & 15) == 0);
-  sample_stats_kernel<<<dim3(nch, rows), kScanThreads, 0, st>>>(logits_p, logits_q, K, V, off, nch, vec_ok,
+  SSD_PDL(sample_stats_kernel, dim3(nch, rows), kScanThreads, 0, st, logits_p, logits_q, K, V, off, nch, vec_ok,
                                                                 temperature_p, temperature_q, c0, part,
                                                                 speculations, u_accept, dec);
   SSD_CHECK_LAUNCH();
   const int nch_b = scan_chunks(B, V);
-  sample_residual_kernel<<<dim3(nch_b, B), kScanThreads, 0, st>>>(logits_p, logits_q, K, V, nch_b, temperature_p,
+  SSD_PDL(sample_residual_kernel, dim3(nch_b, B), kScanThreads, 0, st, logits_p, logits_q, K, V, nch_b, temperature_p,
                                                                   temperature_q, sampler_x, c1,
                                                                   reinterpret_cast<float*>(part), dec);
   SSD_CHECK_LAUNCH();
-  sample_draw_kernel<<<dim3(nch_b, B), kScanThreads, 0, st>>>(
+  SSD_PDL(sample_draw_kernel, dim3(nch_b, B), kScanThreads, 0, st, 
       logits_p, logits_q, u_gumbel, K, V, nch_b, temperature_p, temperature_q, sampler_x, c2,
       reinterpret_cast<unsigned long long*>(part), dec, accept_until, recovery, accepted_mask);
   SSD_CHECK_LAUNCH();
@@ -521,7 +533,7 @@ extern "C" int ssd_uniform_fill(ssd_stream_t stream, float* out, int64_t n, uint
   if (n == 0) return SSD_OK;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  uniform_fill_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(out, n, seed, offset);
+  SSD_PDL(uniform_fill_kernel, (unsigned)blocks, 256, 0, (cudaStream_t)stream, out, n, seed, offset);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }
@@ -533,9 +545,9 @@ extern "C" int ssd_normal_fill(ssd_stream_t stream, void* out, int dtype, int64_
   if (blocks > 148 * 32) blocks = 148 * 32;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == SSD_DTYPE_BF16)
-    normal_fill_kernel<bf16><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<bf16*>(out), n, std, seed);
+    SSD_PDL(normal_fill_kernel<bf16>, (unsigned)blocks, 256, 0, st, reinterpret_cast<bf16*>(out), n, std, seed);
   else if (dtype == SSD_DTYPE_F32)
-    normal_fill_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<float*>(out), n, std, seed);
+    SSD_PDL(normal_fill_kernel<float>, (unsigned)blocks, 256, 0, st, reinterpret_cast<float*>(out), n, std, seed);
   else
     return SSD_ERR_INVALID;
   SSD_CHECK_LAUNCH();

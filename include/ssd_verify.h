@@ -220,6 +220,18 @@ int ssd_linear_max_m(void);
 int ssd_linear(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y,
                int epilogue, int M, int N, int K, void* workspace, size_t workspace_bytes);
 
+/*
+ * Projection of RMS-normalised token rows with the norm weight folded into w:
+ * y = epilogue(rsqrt(mean(x[m]^2) + eps) * (x[m] w^T)), where w = W * (1 + g)
+ * column-wise for the Gemma RMSNorm weight g.  Fuses the input / MLP RMSNorm of
+ * jax_ssd/models/gemma_adapter.py:81-102 (HF Gemma) into the QKV and gate/up
+ * projections.  Epilogues: SSD_EPI_STORE, SSD_EPI_STORE_F32, SSD_EPI_GEGLU.
+ * Uses the ssd_linear_workspace_size workspace.
+ */
+int ssd_linear_rownorm(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y,
+                       int epilogue, int M, int N, int K, float eps, void* workspace,
+                       size_t workspace_bytes);
+
 /* ------------------------------------------------ fused small ops of the forward */
 
 /* x[m] = round(embed[tokens[m]] * round(sqrt(d))) ; tokens [M] int32 */
@@ -247,10 +259,11 @@ typedef struct {
   int dtype;                       /* storage dtype of weights, activations and KV */
   const void* embed;               /* [vocab, d] (tied LM head) */
   const void* final_norm;          /* [d] */
-  const void* const* attn_norm;    /* host array [L] of device [d] */
+  /* The input and MLP RMSNorm weights are folded into the projections that
+   * consume them: w_qkv = W_qkv * (1 + attn_norm) and w_gate_up = W_gu *
+   * (1 + mlp_norm), column-wise, rounded to the storage dtype. */
   const void* const* w_qkv;        /* host array [L] of device [(Hq+2Hkv)*D, d] */
   const void* const* w_o;          /* host array [L] of device [d, Hq*D] */
-  const void* const* mlp_norm;     /* host array [L] of device [d] */
   const void* const* w_gate_up;    /* host array [L] of device [2F, d], rows (gate_i, up_i) */
   const void* const* w_down;       /* host array [L] of device [d, F] */
   const float* rope_cos;           /* [rope_max_pos, D/2] */

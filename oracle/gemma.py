@@ -13,6 +13,13 @@ This module restates the published Gemma-1 architecture:
 * GeGLU MLP ``down(gelu_tanh(gate(x)) * up(x))``;
 * final RMSNorm and the tied LM head ``logits = h E^T``.
 
+Weights may come "folded" (``weights["folded"]``): the q/k/v and gate/up
+matrices then already carry the RMSNorm weights, ``W' = W * (1 + g)``
+column-wise, and those projections compute ``round(inv(x) * (x @ W'^T))`` with
+``inv(x) = 1/sqrt(mean(x^2) + eps)`` -- the formulation the CUDA path uses.
+Unfolded weights use the textbook ``round(round(norm(x)) @ W^T)``; in fp32 the
+two agree to rounding.
+
 ``precision="fp32"`` computes everything in float32 (the toy pair, and the
 cross-check against the installed torch ``GemmaForCausalLM``).
 ``precision="bf16"`` rounds to bfloat16 at exactly the points where the CUDA
@@ -113,6 +120,7 @@ class OracleGemma:
             "layers": [{k: r(v) for k, v in lw.items()} for lw in weights["layers"]],
         }
         self.cos, self.sin = rope_table(max_pos, shape.head_dim, shape.rope_theta)
+        self.folded = bool(weights.get("folded", False))
 
     # ---- pieces (each rounds where the CUDA path stores bf16)
     def embed(self, tokens):
@@ -129,6 +137,15 @@ class OracleGemma:
 
     def linear(self, x, w):
         return self.r(x.astype(np.float32) @ w.T)
+
+    def inv_rms(self, x):
+        xf = x.astype(np.float32)
+        ms = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+        return (np.float32(1.0) / np.sqrt(ms + np.float32(self.s.eps))).astype(np.float32)
+
+    def linear_rownorm(self, x, w):
+        """round(inv(x) * (x @ w^T)) for folded weights."""
+        return self.r((x.astype(np.float32) @ w.T) * self.inv_rms(x))
 
     def rope(self, x, pos):
         """x[..., H, D] at positions pos[...] (same leading shape)."""
@@ -160,10 +177,13 @@ class OracleGemma:
         nl = s.num_layers if stop_layer is None else stop_layer
         for li in range(nl):
             lw = self.w["layers"][li]
-            h = self.rmsnorm(x, lw["attn_norm"])
-            q = self.linear(h, lw["wq"]).reshape(bsz, t, s.num_heads, s.head_dim)
-            k = self.linear(h, lw["wk"]).reshape(bsz, t, s.num_kv_heads, s.head_dim)
-            v = self.linear(h, lw["wv"]).reshape(bsz, t, s.num_kv_heads, s.head_dim)
+            if self.folded:
+                proj, h = self.linear_rownorm, x
+            else:
+                proj, h = self.linear, self.rmsnorm(x, lw["attn_norm"])
+            q = proj(h, lw["wq"]).reshape(bsz, t, s.num_heads, s.head_dim)
+            k = proj(h, lw["wk"]).reshape(bsz, t, s.num_kv_heads, s.head_dim)
+            v = proj(h, lw["wv"]).reshape(bsz, t, s.num_kv_heads, s.head_dim)
             pc = np.where(valid, pos, 0)
             q = self.rope(q, pc)
             k = self.rope(k, pc)
@@ -171,9 +191,13 @@ class OracleGemma:
             a = paged_kv.paged_verify_attention(q, pages, li, block_tables, seq_after, ql)
             a = self.r(a.astype(np.float32)).reshape(bsz, t, s.num_heads * s.head_dim)
             x = self.r(x + self.linear(a, lw["wo"]))
-            h = self.rmsnorm(x, lw["mlp_norm"])
-            g = self.linear(h, lw["wg"])
-            u = self.linear(h, lw["wu"])
+            if self.folded:
+                g = self.linear_rownorm(x, lw["wg"])
+                u = self.linear_rownorm(x, lw["wu"])
+            else:
+                h = self.rmsnorm(x, lw["mlp_norm"])
+                g = self.linear(h, lw["wg"])
+                u = self.linear(h, lw["wu"])
             m = self.r(self.r(gelu_tanh(g)) * u)
             x = self.r(x + self.linear(m, lw["wd"]))
         t_layers = _time.perf_counter()
@@ -185,6 +209,17 @@ class OracleGemma:
             timings["layers_s"] = t_layers - t_start
             timings["head_s"] = _time.perf_counter() - t_layers
         return out
+
+
+def fold_norms(weights: dict) -> dict:
+    """Fold the RMSNorm weights into q/k/v and gate/up (fp32): W' = W * (1 + g) column-wise."""
+    out = {"embed": weights["embed"], "final_norm": weights["final_norm"], "layers": [], "folded": True}
+    for lw in weights["layers"]:
+        a = (np.float32(1.0) + lw["attn_norm"].astype(np.float32))[None, :]
+        m = (np.float32(1.0) + lw["mlp_norm"].astype(np.float32))[None, :]
+        out["layers"].append({**lw, "wq": lw["wq"] * a, "wk": lw["wk"] * a, "wv": lw["wv"] * a,
+                              "wg": lw["wg"] * m, "wu": lw["wu"] * m})
+    return out
 
 
 def new_pages(shape: GemmaShape, num_blocks: int, block_size: int) -> np.ndarray:

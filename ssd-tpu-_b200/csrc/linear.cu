@@ -45,18 +45,33 @@ template <> struct WVec<float> {
 template <typename T, int MMAX, int ROWS>
 __global__ void __launch_bounds__(kLinThreads)
 linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restrict__ y, int epi, int M, int N,
-                 int K, int splits, int kc, float* __restrict__ ws, unsigned int* __restrict__ counters) {
+                 int K, int splits, int kc, float* __restrict__ ws, unsigned int* __restrict__ counters,
+                 int rowscale, float eps) {
   constexpr int VN = WVec<T>::N;
   constexpr int STEP = 32 * VN;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* xs = reinterpret_cast<T*>(smem_raw);  // [M][kc]
   __shared__ bool is_last;
+  __shared__ float inv_s[16];
 
   pdl_wait();
   const int tile = blockIdx.x, split = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k0 = split * kc;
   const int klen = min(kc, K - k0);
+  if (rowscale) {
+    // RMS of each full token row (the (1 + w) factor is folded into the weights);
+    // warp w takes rows w, w + 8; lane-strided sums and an xor tree: fixed order.
+    for (int m = warp; m < M; m += kWarps) {
+      float a = 0.f;
+      for (int k = lane; k < K; k += 32) {
+        const float v = to_f(x[(int64_t)m * K + k]);
+        a = fmaf(v, v, a);
+      }
+      a = warp_sum(a);
+      if (lane == 0) inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(a, (float)K), eps)));
+    }
+  }
   // stage x[:, k0:k0+klen]
   {
     const int pieces = klen / VN;
@@ -113,7 +128,12 @@ linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restr
         if (epi == SSD_EPI_GEGLU && (r & 1)) continue;
 #pragma unroll
         for (int m = 0; m < MMAX; ++m)
-          if (m < M) epilogue_store<T>(epi, y, N, m, n, acc[r][m], (r + 1 < ROWS) ? acc[r + 1][m] : 0.f);
+          if (m < M) {
+            const float sc = rowscale ? inv_s[m] : 1.f;
+            const float a0 = rowscale ? __fmul_rn(acc[r][m], sc) : acc[r][m];
+            const float a1 = (r + 1 < ROWS) ? (rowscale ? __fmul_rn(acc[r + 1][m], sc) : acc[r + 1][m]) : 0.f;
+            epilogue_store<T>(epi, y, N, m, n, a0, a1);
+          }
       }
     }
     return;
@@ -139,6 +159,10 @@ linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restr
     for (int sp = 0; sp < splits; ++sp) {
       s += __ldcg(&ws[((int64_t)sp * M + m) * N + n]);
       if (epi == SSD_EPI_GEGLU) s2 += __ldcg(&ws[((int64_t)sp * M + m) * N + n + 1]);
+    }
+    if (rowscale) {
+      s = __fmul_rn(s, inv_s[m]);
+      s2 = __fmul_rn(s2, inv_s[m]);
     }
     epilogue_store<T>(epi, y, N, m, n, s, s2);
   }
@@ -172,7 +196,7 @@ size_t linear_cc_workspace(int M, int N, int K, int elem_bytes) {
 
 template <typename T, int MMAX, int ROWS>
 static int launch_cc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K,
-                     const LinearPlan& p, void* ws) {
+                     const LinearPlan& p, void* ws, int rowscale, float eps) {
   const int tiles = (N + kWarps * ROWS - 1) / (kWarps * ROWS);
   const size_t smem = sizeof(T) * (size_t)M * p.kc;
   auto kern = linear_cc_kernel<T, MMAX, ROWS>;
@@ -183,27 +207,29 @@ static int launch_cc(cudaStream_t st, const void* x, const void* w, void* y, int
   unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
   float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
   SSD_PDL(kern, dim3(tiles, p.splits), kLinThreads, smem, st, reinterpret_cast<const T*>(x), reinterpret_cast<const T*>(w),
-                                                         y, epi, M, N, K, p.splits, p.kc, part, counters);
+                                                         y, epi, M, N, K, p.splits, p.kc, part, counters, rowscale, eps);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }
 
 template <typename T>
 int linear_cc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-              size_t ws_bytes) {
+              size_t ws_bytes, int rowscale, float eps) {
   if (M > 16) return SSD_ERR_UNSUPPORTED;
   const LinearPlan p = plan_linear_cc(N, K, sizeof(T));
   if (p.splits > 1 && (!ws || ws_bytes < linear_cc_workspace(M, N, K, sizeof(T)))) return SSD_ERR_WORKSPACE;
   if (sizeof(T) * (size_t)M * p.kc > 200 * 1024) return SSD_ERR_UNSUPPORTED;
   if (p.splits > 1 && p.tiles_max > kCounterCap) return SSD_ERR_UNSUPPORTED;
-  if (M <= 1) return launch_cc<T, 1, 8>(st, x, w, y, epi, M, N, K, p, ws);
-  if (M <= 2) return launch_cc<T, 2, 8>(st, x, w, y, epi, M, N, K, p, ws);
-  if (M <= 4) return launch_cc<T, 4, 8>(st, x, w, y, epi, M, N, K, p, ws);
-  if (M <= 8) return launch_cc<T, 8, 8>(st, x, w, y, epi, M, N, K, p, ws);
-  return launch_cc<T, 16, 4>(st, x, w, y, epi, M, N, K, p, ws);
+  if (M <= 1) return launch_cc<T, 1, 8>(st, x, w, y, epi, M, N, K, p, ws, rowscale, eps);
+  if (M <= 2) return launch_cc<T, 2, 8>(st, x, w, y, epi, M, N, K, p, ws, rowscale, eps);
+  if (M <= 4) return launch_cc<T, 4, 8>(st, x, w, y, epi, M, N, K, p, ws, rowscale, eps);
+  if (M <= 8) return launch_cc<T, 8, 8>(st, x, w, y, epi, M, N, K, p, ws, rowscale, eps);
+  return launch_cc<T, 16, 4>(st, x, w, y, epi, M, N, K, p, ws, rowscale, eps);
 }
 
-template int linear_cc<bf16>(cudaStream_t, const void*, const void*, void*, int, int, int, int, void*, size_t);
-template int linear_cc<float>(cudaStream_t, const void*, const void*, void*, int, int, int, int, void*, size_t);
+template int linear_cc<bf16>(cudaStream_t, const void*, const void*, void*, int, int, int, int, void*, size_t, int,
+                             float);
+template int linear_cc<float>(cudaStream_t, const void*, const void*, void*, int, int, int, int, void*, size_t, int,
+                              float);
 
 }  // namespace ssd

@@ -49,12 +49,12 @@ LinearPlan plan_linear_cc(int N, int K, int elem_bytes);
 size_t linear_cc_workspace(int M, int N, int K, int elem_bytes);
 template <typename T>
 int linear_cc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-              size_t ws_bytes);
+              size_t ws_bytes, int rowscale = 0, float eps = 0.f);
 
 // tcgen05 weight-streaming path (bf16)
 size_t linear_tc_workspace(int M, int N, int K);
 int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-              size_t ws_bytes);
+              size_t ws_bytes, int rowscale = 0, float eps = 0.f);
 bool linear_tc_supported(int M, int N, int K);
 
 }  // namespace ssd

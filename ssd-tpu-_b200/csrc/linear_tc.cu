@@ -39,6 +39,9 @@ constexpr uint32_t kWaitLimit = 1u << 24;  // polls before a wait gives up (~sec
 
 struct Params {
   void* y;
+  const bf16* x;  // token rows (read directly only for the row norms)
+  int rowscale;   // 1: scale row m of the result by rsqrt(mean(x[m]^2) + eps)
+  float eps;
   int epi, M, N, K;
   int KB;        // k-blocks per tile
   int U;         // total units = tiles * KB
@@ -147,7 +150,7 @@ struct Cfg {
   // share the SM and prefetch its weights while this one drains (PDL).
   static constexpr int STAGES = MP <= 16 ? 6 : MP <= 32 ? 5 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
   static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;
-  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4) + 16 + 4 * 256;  // + row scales
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
 };
 
@@ -171,6 +174,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * C::STAGE + 8 * (2 * S + 4));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  float* inv_s = reinterpret_cast<float*>(tmem_slot + 4);  // [M] row scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -293,6 +297,27 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     pdl_wait();  // outputs, residual inputs and the workspace belong to the previous kernel until it ends
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const int row = q * 32 + lane;
+    if (p.rowscale) {
+      // RMS of each token row (the (1 + w) factor is folded into the weights):
+      // warp (q) takes rows m = q, q+4, ...; lanes stride K in 8-element vectors,
+      // xor-tree sum -- a fixed order, identical in every CTA and for any M.
+      for (int m = q; m < p.M; m += 4) {
+        const bf16* xr = p.x + (size_t)m * p.K;
+        float acc = 0.f;
+        for (int k0 = lane * 8; k0 < p.K; k0 += 32 * 8) {
+          float f[8];
+          unpack8(ldg_nc_v4(xr + k0), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) {
+          const float ms = __fdiv_rn(acc, (float)p.K);
+          inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+        }
+      }
+      epi_bar();
+    }
     int seg = 0;
     int u = u0;
     const int first_tile = u0 / p.KB;
@@ -320,6 +345,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = c0 + j;
+          if (whole && p.rowscale && m < p.M) v[j] = __fmul_rn(v[j], inv_s[m]);
           const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
           if (m >= p.M) continue;
           if (whole) {
@@ -374,6 +400,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
+          if (p.rowscale && i < mn) s[i] = __fmul_rn(s[i], inv_s[m0 + i]);
           const float up = __shfl_down_sync(0xffffffffu, s[i], 1);
           if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1)))
             epilogue_store<bf16>(p.epi, p.y, p.N, m0 + i, n, s[i], up);
@@ -473,7 +500,8 @@ size_t workspace_bytes(int M, int N, int K) {
 }
 
 template <int MP>
-int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws) {
+int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
+           int rowscale, float eps) {
   using C = Cfg<MP>;
   CUtensorMap wm, xm;
   if (!weight_map(&wm, w, N, K)) return SSD_ERR_LAUNCH;
@@ -482,6 +510,9 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   int grid;
   plan(M, N, K, num_sms(), p, grid);
   p.y = y;
+  p.x = reinterpret_cast<const bf16*>(x);
+  p.rowscale = rowscale;
+  p.eps = eps;
   p.epi = epi;
   p.M = M;
   p.N = N;
@@ -508,14 +539,14 @@ bool linear_tc_supported(int M, int N, int K) {
 size_t linear_tc_workspace(int M, int N, int K) { return tc::workspace_bytes(M, N, K); }
 
 int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-              size_t ws_bytes) {
+              size_t ws_bytes, int rowscale, float eps) {
   if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
-  if (M <= 16) return tc::launch<16>(st, x, w, y, epi, M, N, K, ws);
-  if (M <= 32) return tc::launch<32>(st, x, w, y, epi, M, N, K, ws);
-  if (M <= 64) return tc::launch<64>(st, x, w, y, epi, M, N, K, ws);
-  if (M <= 128) return tc::launch<128>(st, x, w, y, epi, M, N, K, ws);
-  return tc::launch<256>(st, x, w, y, epi, M, N, K, ws);
+  if (M <= 16) return tc::launch<16>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
+  if (M <= 32) return tc::launch<32>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
+  if (M <= 64) return tc::launch<64>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
+  if (M <= 128) return tc::launch<128>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
+  return tc::launch<256>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
 }
 
 }  // namespace ssd

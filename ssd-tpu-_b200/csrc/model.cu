@@ -4,10 +4,12 @@
 // (jax_ssd/models/base.py:34-58) as implemented by GemmaAdapter
 // (jax_ssd/models/gemma_adapter.py:81-143): one host call issues the whole
 // layer stack on one stream, so it can be captured into a CUDA graph.  Per
-// layer: RMSNorm -> QKV projection -> RoPE + K/V page write (fused) -> paged
-// attention -> O projection with the residual add fused -> RMSNorm -> gate/up
-// projection with GeGLU fused -> down projection with the residual add fused.
-// Numerics: bf16 storage between these ops, fp32 math inside them.
+// layer (5 launches): QKV projection with the input RMSNorm fused (norm weight
+// folded into the weight columns, row rsqrt applied in the epilogue) -> RoPE +
+// K/V page write -> paged attention -> O projection with the residual add fused
+// -> gate/up projection with the MLP RMSNorm and GeGLU fused -> down projection
+// with the residual add fused.  Numerics: bf16 storage between these ops, fp32
+// math inside them.
 #include <math.h>
 
 #include <algorithm>
@@ -177,12 +179,12 @@ Scratch carve(const ssd_gemma_weights* w, int B, int T, int max_seq_len, char* b
 }  // namespace
 
 int linear_dispatch(cudaStream_t st, const void* x, const void* w, int dtype, void* y, int epi, int M, int N, int K,
-                    void* ws, size_t ws_bytes) {
+                    void* ws, size_t ws_bytes, int rowscale = 0, float eps = 0.f) {
   if (dtype == SSD_DTYPE_BF16) {
-    if (linear_tc_supported(M, N, K)) return linear_tc(st, x, w, y, epi, M, N, K, ws, ws_bytes);
-    return linear_cc<bf16>(st, x, w, y, epi, M, N, K, ws, ws_bytes);
+    if (linear_tc_supported(M, N, K)) return linear_tc(st, x, w, y, epi, M, N, K, ws, ws_bytes, rowscale, eps);
+    return linear_cc<bf16>(st, x, w, y, epi, M, N, K, ws, ws_bytes, rowscale, eps);
   }
-  return linear_cc<float>(st, x, w, y, epi, M, N, K, ws, ws_bytes);
+  return linear_cc<float>(st, x, w, y, epi, M, N, K, ws, ws_bytes, rowscale, eps);
 }
 
 }  // namespace ssd
@@ -221,6 +223,18 @@ extern "C" int ssd_linear(ssd_stream_t stream, const void* x, const void* w, int
   const int vn = dtype == SSD_DTYPE_BF16 ? 8 : 4;
   if (K % vn) return SSD_ERR_UNSUPPORTED;
   return linear_dispatch((cudaStream_t)stream, x, w, dtype, y, epilogue, M, N, K, workspace, workspace_bytes);
+}
+
+extern "C" int ssd_linear_rownorm(ssd_stream_t stream, const void* x, const void* w, int dtype, void* y, int epilogue,
+                                  int M, int N, int K, float eps, void* workspace, size_t workspace_bytes) {
+  if (M <= 0 || N <= 0 || K <= 0 || !x || !w || !y || !(eps >= 0.f)) return SSD_ERR_INVALID;
+  if (M > max_m()) return SSD_ERR_UNSUPPORTED;
+  if (epilogue != SSD_EPI_STORE && epilogue != SSD_EPI_STORE_F32 && epilogue != SSD_EPI_GEGLU) return SSD_ERR_INVALID;
+  if (epilogue == SSD_EPI_GEGLU && (N & 1)) return SSD_ERR_INVALID;
+  if (dtype != SSD_DTYPE_BF16 && dtype != SSD_DTYPE_F32) return SSD_ERR_INVALID;
+  const int vn = dtype == SSD_DTYPE_BF16 ? 8 : 4;
+  if (K % vn) return SSD_ERR_UNSUPPORTED;
+  return linear_dispatch((cudaStream_t)stream, x, w, dtype, y, epilogue, M, N, K, workspace, workspace_bytes, 1, eps);
 }
 
 extern "C" int ssd_embed(ssd_stream_t stream, const int32_t* tokens, const void* embed, int dtype, void* x, int M,
@@ -263,12 +277,11 @@ static bool weights_ok(const ssd_gemma_weights* w) {
       w->num_heads % w->num_kv_heads || w->head_dim <= 0 || w->ffn <= 0 || w->vocab <= 0)
     return false;
   if (w->dtype != SSD_DTYPE_BF16 && w->dtype != SSD_DTYPE_F32) return false;
-  if (!w->embed || !w->final_norm || !w->attn_norm || !w->w_qkv || !w->w_o || !w->mlp_norm || !w->w_gate_up ||
-      !w->w_down || !w->rope_cos || !w->rope_sin || w->rope_max_pos <= 0)
+  if (!w->embed || !w->final_norm || !w->w_qkv || !w->w_o || !w->w_gate_up || !w->w_down || !w->rope_cos ||
+      !w->rope_sin || w->rope_max_pos <= 0)
     return false;
   for (int l = 0; l < w->num_layers; ++l)
-    if (!w->attn_norm[l] || !w->w_qkv[l] || !w->w_o[l] || !w->mlp_norm[l] || !w->w_gate_up[l] || !w->w_down[l])
-      return false;
+    if (!w->w_qkv[l] || !w->w_o[l] || !w->w_gate_up[l] || !w->w_down[l]) return false;
   return true;
 }
 
@@ -309,10 +322,10 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     if (capturing) cudaEventRecordWithFlags((cudaEvent_t)ev, st, cudaEventRecordExternal);
     else cudaEventRecord((cudaEvent_t)ev, st);
   };
-  auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k) {
+  auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k, int rowscale) {
     const bool rec = bt->prof_events && nprof < bt->prof_capacity;
     if (rec) rec_event(bt->prof_events[2 * nprof]);
-    const int r = linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes);
+    const int r = linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes, rowscale, w->eps);
     if (rec) {
       rec_event(bt->prof_events[2 * nprof + 1]);
       if (bt->prof_kind) bt->prof_kind[nprof] = kind;
@@ -328,18 +341,18 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
   SSD_CHECK_LAUNCH();
   SSD_TRY(ssd_embed(stream, bt->tokens, w->embed, dt, s.x, M, d, w->vocab));
   for (int l = 0; l < L; ++l) {
-    SSD_TRY(ssd_rmsnorm(stream, s.x, w->attn_norm[l], dt, s.h, M, d, w->eps));
-    SSD_TRY(proj(0, s.h, w->w_qkv[l], s.qkv, SSD_EPI_STORE, M, (hq + 2 * hkv) * D, d));
+    // RMSNorm folded: w_qkv carries (1 + attn_norm) in its columns, the projection
+    // scales each token row by its rsqrt(mean(x^2) + eps)
+    SSD_TRY(proj(0, s.x, w->w_qkv[l], s.qkv, SSD_EPI_STORE, M, (hq + 2 * hkv) * D, d, 1));
     SSD_TRY(ssd_rope_kv_write(stream, s.qkv, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hq, hkv, D, l,
                               bt->block_tables, bt->max_blocks, s.pos, w->rope_cos, w->rope_sin, w->rope_max_pos, B,
                               T));
     SSD_TRY(ssd_paged_verify_attention(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
                                        bt->block_tables, bt->max_blocks, s.seq_after, s.qlen, s.attn, scale, B, T,
                                        hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes));
-    SSD_TRY(proj(1, s.attn, w->w_o[l], s.x, SSD_EPI_RESIDUAL, M, d, hq * D));
-    SSD_TRY(ssd_rmsnorm(stream, s.x, w->mlp_norm[l], dt, s.h, M, d, w->eps));
-    SSD_TRY(proj(2, s.h, w->w_gate_up[l], s.act, SSD_EPI_GEGLU, M, 2 * F, d));
-    SSD_TRY(proj(3, s.act, w->w_down[l], s.x, SSD_EPI_RESIDUAL, M, d, F));
+    SSD_TRY(proj(1, s.attn, w->w_o[l], s.x, SSD_EPI_RESIDUAL, M, d, hq * D, 0));
+    SSD_TRY(proj(2, s.x, w->w_gate_up[l], s.act, SSD_EPI_GEGLU, M, 2 * F, d, 1));  // mlp_norm folded likewise
+    SSD_TRY(proj(3, s.act, w->w_down[l], s.x, SSD_EPI_RESIDUAL, M, d, F, 0));
   }
   if (!bt->logits) return SSD_OK;  // prompt chunk: only the K/V rows were needed
   SSD_TRY(ssd_rmsnorm(stream, s.x, w->final_norm, dt, s.h, M, d, w->eps));
@@ -349,9 +362,9 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     else
       SSD_PDL(gather_last_kernel<float>, B, 256, 0, st, (const float*)s.h, s.qlen, T, d, (float*)s.hl);
     SSD_CHECK_LAUNCH();
-    SSD_TRY(proj(4, s.hl, w->embed, bt->logits, SSD_EPI_STORE_F32, B, w->vocab, d));
+    SSD_TRY(proj(4, s.hl, w->embed, bt->logits, SSD_EPI_STORE_F32, B, w->vocab, d, 0));
   } else {
-    SSD_TRY(proj(4, s.h, w->embed, bt->logits, SSD_EPI_STORE_F32, M, w->vocab, d));
+    SSD_TRY(proj(4, s.h, w->embed, bt->logits, SSD_EPI_STORE_F32, M, w->vocab, d, 0));
   }
 #undef SSD_TRY
   return SSD_OK;

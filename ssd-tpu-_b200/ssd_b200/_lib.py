@@ -49,6 +49,7 @@ SIGNATURES = {
     "ssd_linear_workspace_size": (_sz, [_i, _i, _i]),
     "ssd_linear_max_m": (_i, []),
     "ssd_linear": (_i, [_p, _p, _p, _i, _p, _i, _i, _i, _i, _p, _sz]),
+    "ssd_linear_rownorm": (_i, [_p, _p, _p, _i, _p, _i, _i, _i, _i, _f, _p, _sz]),
     "ssd_embed": (_i, [_p, _p, _p, _i, _p, _i, _i, _i]),
     "ssd_rmsnorm": (_i, [_p, _p, _p, _i, _p, _i, _i, _f]),
     "ssd_rope_kv_write": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p, _p, _p, _i,
@@ -66,8 +67,7 @@ class GemmaWeightsC(C.Structure):
         ("num_layers", _i), ("d_model", _i), ("num_heads", _i), ("num_kv_heads", _i),
         ("head_dim", _i), ("ffn", _i), ("vocab", _i), ("eps", _f), ("dtype", _i),
         ("embed", _p), ("final_norm", _p),
-        ("attn_norm", C.POINTER(_p)), ("w_qkv", C.POINTER(_p)), ("w_o", C.POINTER(_p)),
-        ("mlp_norm", C.POINTER(_p)), ("w_gate_up", C.POINTER(_p)), ("w_down", C.POINTER(_p)),
+        ("w_qkv", C.POINTER(_p)), ("w_o", C.POINTER(_p)), ("w_gate_up", C.POINTER(_p)), ("w_down", C.POINTER(_p)),
         ("rope_cos", _p), ("rope_sin", _p), ("rope_max_pos", _i),
     ]
 

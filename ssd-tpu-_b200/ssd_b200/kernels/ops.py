@@ -13,8 +13,12 @@ EPILOGUES = {"store": SSD_EPI_STORE, "store_f32": SSD_EPI_STORE_F32, "residual":
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, epilogue: str = "store", out: torch.Tensor | None = None,
-           ws_key: str = "linear") -> torch.Tensor:
-    """epilogue(x[M,K] w[N,K]^T); ``residual`` accumulates into ``out`` in place."""
+           ws_key: str = "linear", rownorm_eps: float | None = None) -> torch.Tensor:
+    """epilogue(x[M,K] w[N,K]^T); ``residual`` accumulates into ``out`` in place.
+
+    With ``rownorm_eps`` the result rows are scaled by rsqrt(mean(x^2) + eps)
+    (``ssd_linear_rownorm``: an RMSNorm whose weight is folded into ``w``).
+    """
     m, k = x.shape
     n = w.shape[0]
     epi = EPILOGUES[epilogue]
@@ -24,6 +28,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, epilogue: str = "store", out: torch
         cols = n // 2 if epi == SSD_EPI_GEGLU else n
         out = torch.empty((m, cols), dtype=torch.float32 if epi == SSD_EPI_STORE_F32 else x.dtype, device=x.device)
     ws = workspace(x.device, ws_key, lib().ssd_linear_workspace_size(m, n, k))
+    if rownorm_eps is not None:
+        check(lib().ssd_linear_rownorm(stream_ptr(), ptr(x), ptr(w), dtype_code(w.dtype), ptr(out), epi, m, n, k,
+                                       float(rownorm_eps), ptr(ws), ws.numel()), "ssd_linear_rownorm")
+        return out
     check(lib().ssd_linear(stream_ptr(), ptr(x), ptr(w), dtype_code(w.dtype), ptr(out), epi, m, n, k, ptr(ws),
                            ws.numel()), "ssd_linear")
     return out

@@ -9,6 +9,12 @@ Weights live on the GPU in the layout the kernels stream:
 * ``w_down[l]``     [d, F]
 * ``embed``         [V, d]                  also the tied LM head
 
+The input and MLP RMSNorm weights g are folded into the projections that read
+the normalised rows: ``w_qkv = W_qkv * (1 + g_attn)`` and ``w_gate_up = W_gu *
+(1 + g_mlp)`` column-wise (fp32 product, rounded once to the storage dtype); the
+projection kernels scale each token row by its rsqrt(mean(x^2) + eps).  The
+norm vectors are kept for reference; the forward does not read them.
+
 Random init (the reference loads checkpoints; the benchmark configs use random
 weights from a seed) runs on the device with the counter-based
 ``ssd_normal_fill``: projections ~ N(0, (1.2/sqrt(fan_in))^2), embedding ~
@@ -137,7 +143,14 @@ class GemmaWeights:
             w._fill(w.mlp_norm[l], NORM_STD, nxt())
             w._fill(w.w_gate_up[l], init_std(s.d_model), nxt())
             w._fill(w.w_down[l], init_std(s.ffn), nxt())
+        w._fold_norms()
         return w
+
+    def _fold_norms(self) -> None:
+        """w_qkv *= (1 + attn_norm), w_gate_up *= (1 + mlp_norm) column-wise (fp32, rounded once)."""
+        for l in range(self.shape.num_layers):
+            for mat, g in ((self.w_qkv[l], self.attn_norm[l]), (self.w_gate_up[l], self.mlp_norm[l])):
+                mat.copy_((mat.float() * (1.0 + g.float())[None, :]).to(self.dtype))
 
     @classmethod
     def from_canonical(cls, shape: GemmaShape, host: dict, dtype=torch.bfloat16, device="cuda",
@@ -155,14 +168,20 @@ class GemmaWeights:
             gu = torch.stack([t(lw["wg"]), t(lw["wu"])], 1).reshape(2 * shape.ffn, shape.d_model)
             w.w_gate_up[l].copy_(gu)
             w.w_down[l].copy_(t(lw["wd"]))
+        if not host.get("folded", False):
+            w._fold_norms()
         return w
 
     def to_canonical(self, layers: int | None = None) -> dict:
-        """Unpack to canonical float32 numpy matrices (for the CPU oracle)."""
+        """Unpack to per-matrix float32 numpy arrays (for the CPU oracle).
+
+        The q/k/v and gate/up matrices are returned as stored, i.e. with the
+        RMSNorm weights folded in (``"folded": True``).
+        """
         s = self.shape
         f = lambda x: x.float().cpu().numpy()  # noqa: E731
         hq, hkv, hd = s.num_heads * s.head_dim, s.num_kv_heads * s.head_dim, s.head_dim
-        out = {"embed": f(self.embed), "final_norm": f(self.final_norm), "layers": []}
+        out = {"embed": f(self.embed), "final_norm": f(self.final_norm), "layers": [], "folded": True}
         for l in range(s.num_layers if layers is None else layers):
             qkv = f(self.w_qkv[l])
             gu = f(self.w_gate_up[l]).reshape(s.ffn, 2, s.d_model)
@@ -178,16 +197,14 @@ class GemmaWeights:
         if self._cstruct is None:
             s = self.shape
             arr = lambda ts: (C.c_void_p * len(ts))(*[ptr(t) for t in ts])  # noqa: E731
-            self._arrays = [arr(self.attn_norm), arr(self.w_qkv), arr(self.w_o), arr(self.mlp_norm),
-                            arr(self.w_gate_up), arr(self.w_down)]
+            self._arrays = [arr(self.w_qkv), arr(self.w_o), arr(self.w_gate_up), arr(self.w_down)]
             cs = GemmaWeightsC()
             cs.num_layers, cs.d_model, cs.num_heads, cs.num_kv_heads = s.num_layers, s.d_model, s.num_heads, s.num_kv_heads
             cs.head_dim, cs.ffn, cs.vocab, cs.eps = s.head_dim, s.ffn, s.vocab, s.eps
             cs.dtype = dtype_code(self.dtype)
             cs.embed, cs.final_norm = ptr(self.embed), ptr(self.final_norm)
             P = C.POINTER(C.c_void_p)
-            cs.attn_norm, cs.w_qkv, cs.w_o, cs.mlp_norm, cs.w_gate_up, cs.w_down = [
-                C.cast(a, P) for a in self._arrays]
+            cs.w_qkv, cs.w_o, cs.w_gate_up, cs.w_down = [C.cast(a, P) for a in self._arrays]
             cs.rope_cos, cs.rope_sin, cs.rope_max_pos = ptr(self.rope_cos), ptr(self.rope_sin), self.max_pos
             self._cstruct = cs
         return self._cstruct
@@ -240,7 +257,7 @@ class GemmaRunner:
 
     @staticmethod
     def launches_per_forward(shape: GemmaShape, with_logits: bool, last_only: bool) -> int:
-        """Kernel launches issued by one ssd_gemma_forward (positions, embed, 8 per layer, head)."""
+        """Kernel launches issued by one ssd_gemma_forward (positions, embed, 6 per layer, head)."""
         n = 2 + 8 * shape.num_layers
         if with_logits:
             n += 2 + (1 if last_only else 0)

@@ -124,3 +124,34 @@ def test_tcgen05_shapes_and_tails(cuda, m, n, k):
     head = ws[: 16384 * 4 + 4].view(torch.int32)
     assert int(head[:16384].abs().sum()) == 0      # ticket counters reset
     assert int(head[16384]) == 0                   # no device-side wait gave up
+
+
+@pytest.mark.parametrize("dtype_name,m,n,k,epi", [("bf16", 5, 12288, 3072, "store"), ("bf16", 5, 2 * 24576, 3072, "geglu"),
+                                                  ("bf16", 1, 2560, 2048, "store"), ("f32", 5, 1024, 256, "store"),
+                                                  ("f32", 3, 2048, 256, "geglu")])
+def test_rownorm_projection(cuda, dtype_name, m, n, k, epi):
+    """ssd_linear_rownorm = round(rsqrt(mean(x^2)+eps) * (x w^T)), the folded-norm projection."""
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+
+    dt = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    g = torch.Generator(device="cuda").manual_seed(m * n)
+    x = (3.0 * torch.randn((m, k), device="cuda", generator=g)).to(dt)
+    w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).to(dt)
+    y = linear(x, w, epi, rownorm_eps=1e-6)
+    xf = x.float()
+    inv = 1.0 / torch.sqrt((xf * xf).mean(-1, keepdim=True) + 1e-6)
+    acc = (xf @ w.float().T) * inv
+    if epi == "geglu":
+        gate, up = acc[:, 0::2], acc[:, 1::2]
+        if dt == torch.bfloat16:
+            gate, up = gate.bfloat16().float(), up.bfloat16().float()
+        ref = torch.nn.functional.gelu(gate, approximate="tanh")
+        if dt == torch.bfloat16:
+            ref = ref.bfloat16().float()
+        ref = ref * up
+    else:
+        ref = acc
+    tol = 2e-2 if dt == torch.bfloat16 else 1e-5
+    torch.testing.assert_close(y.float(), ref, rtol=tol, atol=tol)

@@ -253,3 +253,19 @@ def test_oracle_gemma_matches_transformers_fp32():
     b = om.forward(ids[None, 7:], pages, table, [7])
     got = np.concatenate([a[0], b[0]], 0)
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_folded_norm_formulation_matches_textbook_fp32():
+    """Folding the RMSNorm weights into q/k/v and gate/up is exact math: fp32 results agree to rounding."""
+    from oracle.gemma import fold_norms
+
+    w = init_weights(TOY_T, 4)
+    a = OracleGemma(TOY_T, w, "fp32")
+    b = OracleGemma(TOY_T, fold_norms(w), "fp32")
+    assert b.folded and not a.folded
+    ids = np.random.default_rng(1).integers(0, TOY_T.vocab, (1, 21))
+    pa, pb = new_pages(TOY_T, 4, 16), new_pages(TOY_T, 4, 16)
+    table = np.arange(4, dtype=np.int32)[None]
+    la = a.forward(ids, pa, table, [0])
+    lb = b.forward(ids, pb, table, [0])
+    np.testing.assert_allclose(la, lb, rtol=1e-4, atol=1e-5)

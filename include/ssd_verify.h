@@ -162,6 +162,20 @@ int ssd_page_free(ssd_stream_t stream, int32_t* block_tables, int32_t* table_len
                   int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks,
                   const uint8_t* release, int B);
 
+/* ------------------------------------------------------------ speculation cache */
+/*
+ * SpecCache.lookup (jax_ssd/algorithm/spec_cache.py:43-66) on the device.
+ *   keys [N,3] int32, valid [N] uint8, tokens [N,K] int32, logits [N,K,V] fp32 (may be
+ *   NULL when out_logits is NULL); request_keys [B,3].
+ *   hit [B] uint8, idx [B] int32 (-1 on a miss), out_tokens [B,K] (0 on a miss),
+ *   out_logits [B,K,V] (may be NULL; zeros on a miss).
+ * A request hits the first valid slot whose three key fields all match.
+ */
+int ssd_spec_cache_lookup(ssd_stream_t stream, const int32_t* keys, const uint8_t* valid,
+                          const int32_t* tokens, const float* logits, int N, int K, int V,
+                          const int32_t* request_keys, int B, uint8_t* hit, int32_t* idx,
+                          int32_t* out_tokens, float* out_logits);
+
 /* --------------------------------------------------------------- K2: KV write */
 /*
  * Write K/V rows of new tokens into the paged cache.

@@ -1,0 +1,153 @@
+"""Gemma adapter on the verify-path kernels (replaces jax_ssd/models/gemma_adapter.py).
+
+Implements the ``DecodeModelAdapter`` protocol (jax_ssd/models/base.py:34-60)
+and the duck-typed extras the reference engine calls (``allocate_kv``,
+``commit_tokens``, ``draft_speculate``, ``tokenize``, ``decode_tokens_to_str``),
+with a real paged KV cache instead of the reference's dummy one:
+
+* ``verify`` runs one ``ssd_gemma_forward`` over the k+1 tokens at their true
+  positions (the reference passes ``arange(k+1)``, engine.py:234, and its
+  adapter ignores it) and writes their K/V rows;
+* ``commit_tokens(accepted + [recovery])`` keeps the verified recovery token and
+  the accepted drafts in the cache and rolls the rest back (``ssd_page_rollback``)
+  -- the reference instead re-runs one forward per committed token
+  (gemma_adapter.py:145-152);
+* ``draft_speculate(prefix, k)`` reuses the draft cache up to the longest
+  common prefix with what it already holds, feeds the remaining tokens, then
+  drafts k greedy tokens (the reference re-prefills the whole prefix each time
+  and drops its first prediction, gemma_adapter.py:154-175).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..algorithm.verify import argmax_rows
+from ..kernels.kv_cache import KVCacheState
+from ..kernels.ops import max_tokens_per_forward
+from ..runtime.page_manager import PageManager
+from .base import DecodeResult, PrefillResult, VerifyResultModel
+from .gemma import GemmaRunner, GemmaWeights
+
+
+class GemmaAdapter:
+    def __init__(self, weights: GemmaWeights, max_model_len: int = 4096, block_size: int = 16,
+                 max_tokens: int = 64, name: str = "gemma") -> None:
+        s = weights.shape
+        self.w = weights
+        self.name = name
+        self.vocab_size = s.vocab
+        self.max_model_len = max_model_len
+        self.block_size = block_size
+        self.num_blocks = (max_model_len + block_size - 1) // block_size + 2
+        self.dev = weights.device
+        self.chunk = min(64, max_tokens_per_forward(weights.dtype))
+        self.runner = GemmaRunner(weights, 1, max(self.chunk, max_tokens), max_model_len)
+        self.cache = KVCacheState.allocate(s.num_layers, self.num_blocks, block_size, s.num_kv_heads, s.head_dim,
+                                           dtype=weights.dtype, device=self.dev)
+        self.pm = PageManager(block_size, self.num_blocks, max_seqs=1, device=self.dev)
+        self.cached: list[int] = []   # tokens whose K/V rows are valid in the cache
+        self.pending: list[int] = []  # tokens of the last verify (written, not yet committed)
+        self._lg1 = torch.empty((1, s.vocab), dtype=torch.float32, device=self.dev)
+
+    # ------------------------------------------------------------ cache state
+    def _i32(self, v) -> torch.Tensor:
+        return torch.tensor([int(v)], dtype=torch.int32, device=self.dev)
+
+    def _truncate(self, n: int) -> None:
+        """Keep the first n cached tokens; surplus pages go back to the free list."""
+        if n < len(self.cached) or self.pending:
+            self.pm.rollback_rows(0, 1, self._i32(n), self._i32(0))
+        self.cached = self.cached[:n]
+        self.pending = []
+
+    def _run(self, tokens: list[int], logits: torch.Tensor | None, last_only: bool) -> torch.Tensor | None:
+        """Append `tokens` to the cache (chunked); returns the logits of the last chunk."""
+        n0 = len(self.cached)
+        if n0 + len(tokens) > self.max_model_len:
+            raise ValueError("sequence exceeds max_model_len")
+        self.pm.allocate_rows(0, 1, self._i32(n0), self._i32(len(tokens)), None)
+        out = None
+        for c0 in range(0, len(tokens), self.chunk):
+            part = tokens[c0:c0 + self.chunk]
+            last = c0 + self.chunk >= len(tokens)
+            t = torch.tensor([part], dtype=torch.int32, device=self.dev)
+            lg = logits if last else None
+            self.runner.forward(t, self._i32(n0 + c0), self.cache.pages, self.pm.tables, lg, last_only=last_only)
+            out = lg
+        self.cached.extend(int(x) for x in tokens)
+        return out
+
+    def allocate_kv(self) -> KVCacheState:
+        self._truncate(0)
+        return self.cache
+
+    # ------------------------------------------------------------ protocol
+    def prefill(self, token_ids, kv_cache=None, page_table=None) -> PrefillResult:
+        self._truncate(0)
+        toks = [int(x) for x in torch.as_tensor(token_ids).reshape(-1).tolist()]
+        lg = self._run(toks, self._lg1, last_only=True)
+        return PrefillResult(logits=lg.clone(), kv_cache=self.cache)
+
+    def decode(self, token_id: int, position: int | None = None, kv_cache=None, page_table=None) -> DecodeResult:
+        if self.pending:
+            self._truncate(len(self.cached))
+        lg = self._run([int(token_id)], self._lg1, last_only=True)
+        nxt = torch.empty(1, dtype=torch.int32, device=self.dev)
+        argmax_rows(lg, nxt)
+        return DecodeResult(logits=lg.clone(), kv_cache=self.cache, next_token=int(nxt.item()))
+
+    def verify(self, token_ids_kp1, positions=None, kv_cache=None, page_table=None) -> VerifyResultModel:
+        if self.pending:
+            self._truncate(len(self.cached))
+        toks = [int(x) for x in torch.as_tensor(token_ids_kp1).reshape(-1).tolist()]
+        lg = torch.empty((1, len(toks), self.vocab_size), dtype=torch.float32, device=self.dev)
+        n0 = len(self.cached)
+        self.pm.allocate_rows(0, 1, self._i32(n0), self._i32(len(toks)), None)
+        self.runner.forward(torch.tensor([toks], dtype=torch.int32, device=self.dev), self._i32(n0),
+                            self.cache.pages, self.pm.tables, lg, last_only=False)
+        self.pending = toks
+        return VerifyResultModel(logits=lg, kv_cache=self.cache)
+
+    def commit_tokens(self, token_ids: list[int]) -> None:
+        """After verify([r] + draft): token_ids = accepted + [new recovery] keeps r + accepted."""
+        if self.pending:
+            keep = min(len(token_ids), len(self.pending))  # r and the len(token_ids) - 1 accepted drafts
+            n = len(self.cached) + keep
+            self.cached.extend(self.pending[:keep])
+            self.pending = []
+            self.pm.rollback_rows(0, 1, self._i32(n), self._i32(0))
+        # tokens that were never verified (e.g. a fresh recovery) enter with the next forward
+
+    def draft_speculate(self, prefix_tokens: list[int], k: int, *,
+                        with_bonus: bool = False) -> tuple[list[int], torch.Tensor]:
+        """k greedy draft tokens after `prefix_tokens` and the logits that chose them, [k, V]
+        (``with_bonus``: one more forward over the last draft, logits [k+1, V])."""
+        prefix = [int(t) for t in prefix_tokens]
+        common = 0
+        for a, b in zip(self.cached, prefix):
+            if a != b:
+                break
+            common += 1
+        common = min(common, len(prefix) - 1)  # always feed at least one token
+        self._truncate(common)
+        rows = k + 1 if with_bonus else k
+        logits = torch.empty((rows, self.vocab_size), dtype=torch.float32, device=self.dev)
+        feed = prefix[common:]
+        spec: list[int] = []
+        nxt = torch.empty(1, dtype=torch.int32, device=self.dev)
+        for i in range(rows):
+            lg = self._run(feed, self._lg1, last_only=True)
+            logits[i].copy_(lg[0])
+            if i == k:
+                break
+            argmax_rows(lg, nxt)
+            spec.append(int(nxt.item()))
+            feed = [spec[-1]]
+        return spec, logits
+
+    def tokenize(self, text: str) -> list[int]:
+        return [b % self.vocab_size for b in text.encode("utf-8")]
+
+    def decode_tokens_to_str(self, token_ids: list[int]) -> str:
+        return " ".join(f"t{int(t)}" for t in token_ids)

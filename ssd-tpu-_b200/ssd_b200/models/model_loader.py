@@ -1,0 +1,39 @@
+"""Load target/draft adapters (jax_ssd/models/model_loader.py:40-76).
+
+There are no checkpoints here: a model "path" names a random-init preset of
+``models.gemma.PRESETS`` (default: "gemma-7b" target, "gemma-2b" draft; the toy
+pair with ``use_toy``).  Weights are initialised on the device from the seed.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .gemma import PRESETS, GemmaWeights
+from .gemma_adapter import GemmaAdapter
+
+_SHARED: dict[tuple, GemmaWeights] = {}
+
+
+def default_preset(role: str, use_toy: bool) -> str:
+    if use_toy:
+        return "toy-target" if role == "target" else "toy-draft"
+    return "gemma-7b" if role == "target" else "gemma-2b"
+
+
+def load_weights(model_path: str | None, *, use_toy: bool = False, seed: int = 0, role: str = "target",
+                 device="cuda") -> GemmaWeights:
+    name = model_path if model_path in PRESETS else default_preset(role, use_toy)
+    dtype = torch.float32 if name.startswith("toy") else torch.bfloat16
+    key = (name, seed, str(device))
+    w = _SHARED.get(key)
+    if w is None:
+        w = GemmaWeights.random(PRESETS[name], seed=seed, dtype=dtype, device=device)
+        _SHARED[key] = w
+    return w
+
+
+def load_model_adapter(model_path: str | None, *, use_toy: bool = False, seed: int = 0, share_key=None,
+                       mesh=None, devices=None, role: str = "target", max_model_len: int = 4096) -> GemmaAdapter:
+    w = load_weights(model_path, use_toy=use_toy, seed=seed, role=role)
+    return GemmaAdapter(w, max_model_len=max_model_len, name=role)

@@ -1,0 +1,160 @@
+"""Draft worker with host queues for async SSD (jax_ssd/runtime/workers.py:32-145).
+
+The worker thread serves ``DraftRequest(SERVE)`` messages on its own CUDA
+stream:
+
+1. ``_handle`` looks the request keys ``[seq_id, accepted, recovery]`` up in its
+   ``SpecCache`` (``ssd_spec_cache_lookup``); on a miss it drafts k tokens from
+   the request's committed prefix (``draft_speculate``) -- the reference drafts
+   from ``[recovery]`` alone (workers.py:96-109).
+2. After the response is queued, ``_rebuild_cache`` resets the cache and
+   pre-drafts the branches the next request can name while the target
+   verifies: for each accepted length ``a`` in 0..k, ``fan_out_list[a]``
+   recovery candidates, the top tokens of the draft's own distribution at
+   position ``a`` with the drafted token removed (a rejected draft is never the
+   recovery token; at ``a = k`` the bonus distribution is used as is).  Each
+   branch is drafted from ``prefix + spec[:a] + [candidate]``, so a hit serves
+   exactly the tokens a miss would draft.  The rebuild finishes before the
+   next request is served (as in the reference, which rebuilds inside
+   ``_handle``); it overlaps the target's verify when the engine runs the draft
+   on another device or stream.  The reference builds the same keys
+   (workers.py:119-145) from top-F of all-zero glue logits, i.e. candidates
+   ``0..F-1``, and drafts them from the candidate alone.
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+
+import torch
+
+from ..algorithm.async_protocol import DraftCommand, DraftRequest, DraftResponse
+from ..algorithm.spec_cache import SpecCache
+from ..config import SSDConfig
+
+
+class DraftWorker:
+    def __init__(self, config: SSDConfig, draft_model) -> None:
+        self.config = config
+        self.model = draft_model
+        self.request_queue: queue.Queue = queue.Queue()
+        self.response_queue: queue.Queue = queue.Queue()
+        self.cache: SpecCache | None = None
+        self.stream: torch.cuda.Stream | None = None
+        self._thread: threading.Thread | None = None
+        self._running = False
+        self.error: BaseException | None = None
+        self.prefetch = True
+        self.branches_drafted = 0
+
+    def start(self) -> None:
+        self._running = True
+        dev = torch.device(self.model.dev)
+        self._device = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.stream = torch.cuda.Stream(device=self._device)
+        with torch.cuda.stream(self.stream):
+            self.cache = SpecCache.create(num_branches=max(1, self.config.mq_len), k=self.config.speculate_k,
+                                          vocab=self.model.vocab_size, device=self.model.dev, with_logits=False)
+        self.stream.synchronize()
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
+
+    def stop(self) -> None:
+        self._running = False
+        if self._thread:
+            self.request_queue.put(DraftRequest(DraftCommand.SHUTDOWN, torch.zeros((0, 3), dtype=torch.int32),
+                                                torch.zeros(0), torch.zeros(0), torch.zeros(0)))
+            self._thread.join(timeout=30)
+
+    def submit(self, req: DraftRequest) -> None:
+        self.request_queue.put(req)
+
+    def get_response(self, timeout: float = 120.0) -> DraftResponse:
+        resp = self.response_queue.get(timeout=timeout)
+        if isinstance(resp, BaseException):
+            raise resp
+        return resp
+
+    def _loop(self) -> None:
+        try:
+            torch.cuda.set_device(self._device)
+        except BaseException as exc:
+            self.error = exc
+            self.response_queue.put(exc)
+            return
+        with torch.cuda.stream(self.stream):
+            while self._running:
+                try:
+                    req = self.request_queue.get(timeout=0.1)
+                except queue.Empty:
+                    continue
+                if req.command == DraftCommand.SHUTDOWN:
+                    break
+                try:
+                    resp, plans = self._handle(req)
+                    self.response_queue.put(resp)
+                    if self.prefetch:
+                        self._rebuild_cache(plans)
+                except BaseException as exc:  # surface to the engine thread
+                    self.error = exc
+                    self.response_queue.put(exc)
+
+    def _handle(self, req: DraftRequest) -> tuple[DraftResponse, list]:
+        k = self.config.speculate_k
+        hit, _, tokens, _ = self.cache.lookup(req.cache_keys)
+        hit_h = hit.cpu()
+        keys_h = req.cache_keys.cpu()
+        rows, plans = [], []
+        for i in range(keys_h.shape[0]):
+            prefix = [int(t) for t in req.prefix_tokens[i]]
+            if bool(hit_h[i]):
+                spec = [int(t) for t in tokens[i].tolist()]
+                rows.append(tokens[i])
+                plans.append((keys_h[i], prefix, spec, None))
+                continue
+            spec, logits = self.model.draft_speculate(prefix, k, with_bonus=self.prefetch)
+            rows.append(torch.tensor(spec, dtype=torch.int32, device=self.model.dev))
+            plans.append((keys_h[i], prefix, spec, logits))
+        spec_tokens = torch.stack(rows)
+        self.stream.synchronize()
+        return DraftResponse(cache_hit=hit, spec_tokens=spec_tokens,
+                             draft_logits=torch.zeros((len(rows), k, 1), dtype=torch.float32)), plans
+
+    def _rebuild_cache(self, plans: list) -> None:
+        """Pre-draft the next request's branches (see the module docstring).
+
+        Branches are drafted most-likely first, scored with the draft's own
+        distribution q standing in for the target's: an accepted length ``a``
+        has weight prod_{j<a} q_j(s_j) * (1 - q_a(s_a)) (prod_{j<k} q_j(s_j) for
+        a = k) and candidate c at ``a`` the share q_a(c) / (1 - q_a(s_a)).
+        """
+        k = self.config.speculate_k
+        fan = tuple(self.config.fan_out_list)
+        if len(fan) < k + 1:
+            fan = fan + (fan[-1],) * (k + 1 - len(fan))
+        self.cache.reset()
+        branches = []
+        for key, prefix, spec, logits in plans:
+            if logits is None:  # served from the cache: draft once more for the glue logits
+                spec, logits = self.model.draft_speculate(prefix, k, with_bonus=True)
+            q = torch.softmax(logits.float(), dim=-1)
+            q_spec = q[torch.arange(k, device=q.device), torch.tensor(spec, device=q.device)].tolist()
+            reach = 1.0  # prod_{j<a} q_j(s_j)
+            for a in range(k + 1):
+                row = q[a].clone()
+                if a < k:
+                    row[spec[a]] = 0.0  # a rejected draft is never the recovery token
+                if fan[a] > 0:
+                    top = torch.topk(row, fan[a])
+                    for c, pc in zip(top.indices.tolist(), top.values.tolist()):
+                        # reach * (1 - q_a(s_a)) * q_a(c) / (1 - q_a(s_a)) = reach * q_a(c)
+                        branches.append((reach * pc, int(key[0]), a, int(c), prefix + spec[:a] + [int(c)]))
+                if a < k:
+                    reach *= q_spec[a]
+        branches.sort(key=lambda b: -b[0])
+        for slot, (_, sid, a, c, branch) in enumerate(branches[: self.cache.keys.shape[0]]):
+            s, _ = self.model.draft_speculate(branch, k)
+            self.cache.insert(slot, [sid, a, c], s)
+            self.branches_drafted += 1
+        self.stream.synchronize()

@@ -1,0 +1,13 @@
+"""Generation controls (jax_ssd/sampling_params.py:8-13)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+@dataclass
+class SamplingParams:
+    temperature: float = 0.0
+    draft_temperature: float = 0.0
+    max_new_tokens: int = 128
+    ignore_eos: bool = False

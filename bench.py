@@ -11,8 +11,11 @@ steps (all ranks, device-timed with CUDA events, max over ranks); ``e2e`` = the
 same metric for a whole ``SpeculativeDecoder.generate`` call from a host prompt
 list to host tokens (prefill included); ``verify_step_us`` / ``verify_hbm_gbs``
 describe the verify forward alone; ``roofline`` covers the dominant kernel (the
-weight-streaming projections).  With N > 1 (torchrun) each rank decodes its own
-sequence (replicas; no data-path collective).
+weight-streaming projections).  With N > 1 (torchrun) the pair is tensor-parallel
+over the N GPUs (``--parallel tp``, the default: heads / FFN / vocabulary split,
+the O / down all-reduces and the LM-head all-gather fused into the projection
+kernels over NVLink; one sequence, strong scaling), or each rank decodes its own
+sequence (``--parallel replicas``; no data-path collective, weak scaling).
 
 ``--impl reference`` times the CPU restatement of the same path (numpy oracle:
 the reference's own JAX code cannot run here) on a bounded layer sample.
@@ -49,11 +52,14 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--e2e-new-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=["linear", "attention", "verify", "sample"], default=None,
+    ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
+                    help="N > 1: tensor-parallel pair (one sequence) or independent replicas")
+    ap.add_argument("--op", choices=["linear", "attention", "verify", "sample", "allreduce", "allgather"],
+                    default=None,
                     help="time one kernel family on its op-level workload instead of the decode loop")
-    ap.add_argument("--m", type=int, default=5)
-    ap.add_argument("--n", type=int, default=49152)
-    ap.add_argument("--kdim", type=int, default=3072)
+    ap.add_argument("--rows", "--m", dest="m", type=int, default=5)
+    ap.add_argument("--cols", "--n", dest="n", type=int, default=49152)
+    ap.add_argument("--depth", "--kdim", dest="kdim", type=int, default=3072)
     ap.add_argument("--attn", choices=["2a", "decode7b", "decode2b"], default="2a",
                     help="--op attention shape: op config 2a (B=8, ctx U[512,4096]) or one decode step")
     return ap.parse_args()
@@ -212,15 +218,28 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local)
     k = args.k
+    tp = world > 1 and args.parallel == "tp"
     st_, sd_ = PRESETS["gemma-7b"], PRESETS["gemma-2b"]
-    target = GemmaWeights.random(st_, seed=1000 + rank)
-    draft = GemmaWeights.random(sd_, seed=2000 + rank)
-    rng = np.random.default_rng(rank)
+    comm = None
+    if tp:
+        from ssd_b200.runtime.tensor_parallel import TPComm, shard_weights
+
+        # every rank draws the same full weights from the seed and keeps its shard
+        target = shard_weights(GemmaWeights.random(st_, seed=1000), rank, world)
+        draft = shard_weights(GemmaWeights.random(sd_, seed=2000), rank, world)
+        torch.cuda.empty_cache()
+        comm = TPComm(heap_bytes=192 << 20, max_m=256, max_n=max(st_.d_model, sd_.d_model))
+        rng = np.random.default_rng(0)
+    else:
+        target = GemmaWeights.random(st_, seed=1000 + rank)
+        draft = GemmaWeights.random(sd_, seed=2000 + rank)
+        rng = np.random.default_rng(rank)
+    lt, ld = target.shape, draft.shape  # this rank's (sharded) shapes
     prompt = [int(x) for x in rng.integers(0, st_.vocab, args.prompt_len)]
     total_steps = args.warmup + args.steps
     max_seq = args.prompt_len + (total_steps + 2) * (k + 1) + 32
     max_seq = max(max_seq, args.prompt_len + args.e2e_new_tokens * (k + 1) + 32)
-    dec = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq)
+    dec = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq, comm=comm)
     dec.start(prompt)
     for _ in range(args.warmup):
         dec.step()
@@ -258,6 +277,8 @@ def run_ours(args):
         tsum = t[1:2].clone()
         dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
         ms_max, tok_all = float(tmax.item()), float(tsum.item())
+        if tp:
+            tok_all = float(tokens)  # one sequence decoded by all ranks together
     else:
         ms_max, tok_all = ms, float(tokens)
     value = tok_all / (ms_max / 1000.0)
@@ -265,18 +286,24 @@ def run_ours(args):
     # Projection launches timed with CUDA events in a second window of the same
     # decode (events between kernels add gaps, so they stay out of `value`).
     timer = ProjectionTimer(capacity=4 * st_.num_layers + 8)
-    dec_p = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq, timer=timer)
+    if comm is not None:
+        heap_top = comm._top
+    dec_p = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq, timer=timer, comm=comm)
     dec_p.start(prompt)
     for _ in range(args.warmup):
         dec_p.step()
     timer.reset()
     for _ in range(max(8, min(args.steps, 32))):
         dec_p.step()
+    torch.cuda.synchronize()
     del dec_p
+    if comm is not None:
+        comm._top = heap_top  # the profiled decoder's symmetric buffers are free again
 
-    # verify-step bytes: all target weights once + KV rows read (+ logits written)
-    wbytes = target.weight_bytes()
-    kv_tok = st_.kv_bytes_per_token()
+    # verify-step bytes (per rank): its target weight shard once + its KV rows read
+    # (+ the logits block it writes); the replicated embedding is read for k+1 rows only
+    wbytes = lt.layer_weight_bytes() * lt.num_layers + (st_.vocab // max(world if tp else 1, 1)) * st_.d_model * 2
+    kv_tok = lt.kv_bytes_per_token()
     mean_ctx = ctx_sum / args.steps
     verify_bytes = wbytes + kv_tok * mean_ctx + (k + 1) * st_.vocab * 4
     verify_us = 1000.0 * statistics.mean(verify_ms)
@@ -284,7 +311,8 @@ def run_ours(args):
 
     # dominant kernel: the weight-streaming projections inside the timed verify forwards
     M = k + 1
-    d, hq, hkv, D, F, V = st_.d_model, st_.num_heads, st_.num_kv_heads, st_.head_dim, st_.ffn, st_.vocab
+    d, hq, hkv, D, F = lt.d_model, lt.num_heads, lt.num_kv_heads, lt.head_dim, lt.ffn
+    V = st_.vocab // (world if tp else 1)
     shapes = {"qkv": ((hq + 2 * hkv) * D, d, 2), "o": (d, hq * D, 2), "gate_up": (2 * F, d, 2),
               "down": (d, F, 2), "lm_head": (V, d, 4)}
     proj_bytes = 0.0
@@ -302,12 +330,12 @@ def run_ours(args):
                           "gbs": b1 * nl / (timer.total_ms[kind] / 1000.0) / 1e9}
     n_launch = sum(timer.launches.values())
     achieved = proj_bytes / (proj_ms / 1000.0) / 1e9
-    lpf_t = GemmaRunner.launches_per_forward(st_, True, False)
-    lpf_d = GemmaRunner.launches_per_forward(sd_, True, True)
+    lpf_t = GemmaRunner.launches_per_forward(lt, True, False)
+    lpf_d = GemmaRunner.launches_per_forward(ld, True, True)
     launches_per_step = k * (lpf_d + 1) + 1 + (1 + lpf_t + 1) + 2
 
     # e2e: one whole generate() from a host prompt list to host tokens
-    dec2 = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq)
+    dec2 = SpeculativeDecoder(target, draft, k=k, max_seq_len=max_seq, comm=comm)
     torch.cuda.synchronize()
     w0 = time.perf_counter()
     out, info = dec2.generate(prompt, args.e2e_new_tokens)
@@ -319,7 +347,7 @@ def run_ours(args):
         dist.all_reduce(a, op=dist.ReduceOp.MAX)
         b = e2e_local[1:2].clone()
         dist.all_reduce(b, op=dist.ReduceOp.SUM)
-        e2e_val = float(b.item()) / float(a.item())
+        e2e_val = (len(out) if tp else float(b.item())) / float(a.item())
     else:
         e2e_val = len(out) / (w1 - w0)
 
@@ -338,10 +366,10 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
-            "random prompt ids)",
-            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": args.prompt_len, "k": k,
-                       "parallelism": "replicas" if world > 1 else "tp1",
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, random prompt ids)",
+            "config": {"workload": WORKLOAD, "global_batch": 1 if tp else world, "seq_len": args.prompt_len, "k": k,
+                       "parallelism": f"tp{world}" if tp else ("replicas" if world > 1 else "tp1"),
                        "l2": "inputs larger than L2: 17.1 GB of target weights + 5.0 GB of draft weights "
                              "streamed per step"},
             "verify_step_us": verify_us,
@@ -362,8 +390,14 @@ def run_ours(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        torch.cuda.synchronize()
+        if comm.status() != 0:
+            print(f"rank {rank}: tensor-parallel wait timed out", file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
 
 
@@ -380,7 +414,15 @@ def run_op(args):
     from ssd_b200.kernels.kv_cache import KVCacheState, paged_verify_attention
     from ssd_b200.kernels.ops import linear
 
-    torch.cuda.set_device(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     hbm, kind = peaks()
     g = torch.Generator(device="cuda").manual_seed(0)
     reps = max(args.steps, 1)
@@ -415,6 +457,44 @@ def run_op(args):
         nbytes = n * k * 2 + m * k * 2 + m * n * 2
         line = {"op": "linear", "m": m, "n": n, "k": k, "us": ms * 1000, "gbs": nbytes / ms / 1e6,
                 "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind, "weights_rotated": nrot}
+    elif args.op in ("allreduce", "allgather"):
+        # one tensor-parallel projection per rank (M x N outputs, this rank's K / N block),
+        # against the plain projection of the same local shape; --n / --kdim are the
+        # LOCAL sizes (7B O at TP2: --n 3072 --kdim 2048; LM head at TP2: --op allgather
+        # --n 128000 --kdim 3072)
+        from ssd_b200.kernels.ops import linear_allgather, linear_allreduce
+        from ssd_b200.runtime.tensor_parallel import TPComm
+
+        m, n, k = args.m, args.n, args.kdim
+        comm = TPComm(heap_bytes=(64 << 20) + 8 * m * n * world * 4, max_m=m, max_n=n if args.op == "allreduce" else 1)
+        nrot = max(1, int(np.ceil(512e6 / (n * k * 2))))
+        ws = [(torch.randn((n, k), device="cuda", generator=g) * 0.02).bfloat16() for _ in range(nrot)]
+        x = torch.randn((m, k), device="cuda", generator=g).bfloat16()
+        if args.op == "allreduce":
+            y = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+            ms_plain = timed(lambda i: linear(x, ws[i], "residual", out=y), nrot)
+            ms = timed(lambda i: linear_allreduce(x, ws[i], y, comm), nrot)
+            nbytes = n * k * 2 + m * k * 2 + 2 * m * n * 2
+        else:
+            y = comm.alloc((m, n * world), torch.float32)
+            yl = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            ms_plain = timed(lambda i: linear(x, ws[i], "store_f32", out=yl), nrot)
+            ms = timed(lambda i: linear_allgather(x, ws[i], y, comm), nrot)
+            nbytes = n * k * 2 + m * k * 2 + m * n * 4
+        torch.cuda.synchronize()
+        t = torch.tensor([ms, ms_plain], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_plain = float(t[0]), float(t[1])
+        line = {"op": args.op, "world": world, "m": m, "n_local": n, "k_local": k, "us": ms * 1000,
+                "us_plain": ms_plain * 1000, "collective_us": (ms - ms_plain) * 1000,
+                "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind,
+                "status": comm.status(), "weights_rotated": nrot}
+        if world > 1:
+            dist.barrier()
+        comm.close()
+        if rank != 0:
+            return
     elif args.op == "attention":
         b, t, hq, hkv, d, bs = 8, 5, 16, 16, 256, 16
         rng = np.random.default_rng(0)

@@ -246,6 +246,61 @@ int ssd_linear_rownorm(ssd_stream_t stream, const void* x, const void* w, int dt
                        int epilogue, int M, int N, int K, float eps, void* workspace,
                        size_t workspace_bytes);
 
+/* ------------------------------------------------------------ tensor parallelism */
+/*
+ * Tensor-parallel projections with the collective fused into the projection
+ * kernel (no reference counterpart: the reference shards with XLA GSPMD,
+ * jax_ssd/models/sharding.py:10-31, and its collectives are XLA's).  One
+ * process per GPU; every rank owns a "symmetric heap" -- a device buffer of the
+ * same size, carved identically on every rank -- and maps every peer's heap
+ * into its address space (ssd_ipc_export / ssd_ipc_import, CUDA IPC over
+ * NVLink).  The kernels store fp32 tiles straight into the peers' heaps and
+ * signal per-tile arrival flags held in each heap's control block.
+ * All ranks must issue the same collective calls in the same order on one
+ * stream each; a rank that is more than about 5 s late makes the others give up,
+ * record SSD_ERR_TIMEOUT in word 2 of their control block and finish with
+ * incomplete results (nothing hangs).
+ */
+#define SSD_MAX_TP 8
+typedef struct {
+  int rank, world;                 /* this rank, ranks in the group (1..SSD_MAX_TP) */
+  void* heaps[SSD_MAX_TP];         /* heap of rank r as mapped in this process; heaps[rank] = own */
+  size_t heap_bytes;               /* size of every rank's heap */
+  size_t ctrl_offset;              /* control block (ssd_comm_ctrl_bytes), zero-filled before first use */
+  size_t recv_offset, recv_bytes;  /* all-reduce receive area (>= ssd_comm_recv_bytes) */
+} ssd_comm;
+
+/* Bytes of the control block (multiple of 256). */
+size_t ssd_comm_ctrl_bytes(void);
+/* Bytes of the all-reduce receive area for projections of up to max_m x max_n outputs. */
+size_t ssd_comm_recv_bytes(int world, int max_m, int max_n);
+
+/* CUDA IPC: a 64-byte handle of the allocation holding `ptr` and ptr's offset in it. */
+int ssd_ipc_export(const void* ptr, void* handle, size_t* offset);
+/* Map a peer's exported buffer: *ptr = mapped allocation + offset. */
+int ssd_ipc_import(const void* handle, size_t offset, void** ptr);
+/* Unmap a buffer mapped by ssd_ipc_import. */
+int ssd_ipc_close(void* ptr, size_t offset);
+
+/*
+ * Row-parallel projection + all-reduce + residual (the O and down projections
+ * of a tensor-parallel layer): y[M,N] += round_bf16(sum over ranks r, in rank
+ * order, of x_r[M,K] w_r[N,K]^T), where x_r / w_r are rank r's column shards.
+ * bf16 only; every rank ends with bit-identical y.  Uses the
+ * ssd_linear_workspace_size(M, N, K) workspace.
+ */
+int ssd_linear_allreduce(ssd_stream_t stream, const void* x, const void* w, void* y, int M, int N, int K,
+                         void* workspace, size_t workspace_bytes, const ssd_comm* comm);
+
+/*
+ * Column-parallel projection + all-gather (the vocab-parallel LM head):
+ * y[m, rank*N + n] = x[m] . w[n] in fp32, written into y on every rank.  y is a
+ * [M, ldy] fp32 buffer inside the heap, at the same offset on every rank; when
+ * the call's kernel ends, every rank's columns are present.  bf16 only.
+ */
+int ssd_linear_allgather(ssd_stream_t stream, const void* x, const void* w, float* y, int ldy, int M, int N,
+                         int K, void* workspace, size_t workspace_bytes, const ssd_comm* comm);
+
 /* ------------------------------------------------ fused small ops of the forward */
 
 /* x[m] = round(embed[tokens[m]] * round(sqrt(d))) ; tokens [M] int32 */
@@ -283,6 +338,12 @@ typedef struct {
   const float* rope_cos;           /* [rope_max_pos, D/2] */
   const float* rope_sin;
   int rope_max_pos;
+  /* Tensor parallelism: with tp_world > 1 the struct describes rank tp_rank's
+   * shard -- num_heads, num_kv_heads and ffn are per-rank counts (a single KV
+   * head is replicated), w_o / w_down hold the matching column blocks, vocab is
+   * the full vocabulary and embed the full (replicated) table, whose rows
+   * [tp_rank*vocab/tp_world, ...) are this rank's LM-head block. */
+  int tp_rank, tp_world;
 } ssd_gemma_weights;
 
 typedef struct {
@@ -308,6 +369,10 @@ typedef struct {
   int prof_capacity;
   int* prof_count;
   int* prof_kind;
+  /* Tensor parallelism (NULL: none).  When set, the O and down projections
+   * run as ssd_linear_allreduce and the LM head as ssd_linear_allgather, so
+   * `logits` must lie in comm's heap, at the same offset on every rank. */
+  const ssd_comm* comm;
 } ssd_gemma_batch;
 
 size_t ssd_gemma_scratch_size(const ssd_gemma_weights* w, int B, int T, int max_seq_len);

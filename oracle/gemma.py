@@ -138,6 +138,13 @@ class OracleGemma:
     def linear(self, x, w):
         return self.r(x.astype(np.float32) @ w.T)
 
+    def row_parallel(self, x, w, allreduce=None):
+        """round(x @ w^T), the fp32 product summed over the ranks first when sharded."""
+        y = x.astype(np.float32) @ w.T
+        if allreduce is not None:
+            y = allreduce(y.astype(np.float32))
+        return self.r(y)
+
     def inv_rms(self, x):
         xf = x.astype(np.float32)
         ms = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
@@ -156,12 +163,19 @@ class OracleGemma:
         return self.r(np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1))
 
     def forward(self, tokens, pages, block_tables, seq_lens_before, q_lens=None, stop_layer=None, timings=None,
-                with_head=True):
+                with_head=True, allreduce=None, allgather=None, vocab_block=None):
         """tokens[B,T] -> logits[B,T,V] fp32; writes K/V of the new tokens into ``pages``.
 
         Sequence b's new token t (t < q_lens[b]) sits at position
         ``seq_lens_before[b] + t``.  ``pages`` is [2,L,NB,BS,Hkv,D] float32 holding
         bf16-representable values in bf16 mode.
+
+        Tensor-parallel restatement (the sharded CUDA forward): with the
+        weights of one rank's shard, ``allreduce(partial_fp32)`` sums the O and
+        down partial products over the ranks before they are rounded and added
+        to the residual, and the LM head multiplies by the rows
+        ``vocab_block = (v0, nv)`` of the embedding and ``allgather``s the
+        column blocks.
         """
         s = self.s
         bsz, t = tokens.shape
@@ -190,7 +204,7 @@ class OracleGemma:
             paged_kv.write_kv(pages, li, block_tables, wpos, k, v)
             a = paged_kv.paged_verify_attention(q, pages, li, block_tables, seq_after, ql)
             a = self.r(a.astype(np.float32)).reshape(bsz, t, s.num_heads * s.head_dim)
-            x = self.r(x + self.linear(a, lw["wo"]))
+            x = self.r(x + self.row_parallel(a, lw["wo"], allreduce))
             if self.folded:
                 g = self.linear_rownorm(x, lw["wg"])
                 u = self.linear_rownorm(x, lw["wu"])
@@ -199,12 +213,15 @@ class OracleGemma:
                 g = self.linear(h, lw["wg"])
                 u = self.linear(h, lw["wu"])
             m = self.r(self.r(gelu_tanh(g)) * u)
-            x = self.r(x + self.linear(m, lw["wd"]))
+            x = self.r(x + self.row_parallel(m, lw["wd"], allreduce))
         t_layers = _time.perf_counter()
         if not with_head:
             return None
         h = self.rmsnorm(x, self.w["final_norm"])
-        out = (h.astype(np.float32) @ self.w["embed"].T).astype(np.float32)
+        head = self.w["embed"] if vocab_block is None else self.w["embed"][vocab_block[0]:vocab_block[0] + vocab_block[1]]
+        out = (h.astype(np.float32) @ head.T).astype(np.float32)
+        if allgather is not None:
+            out = allgather(out)
         if timings is not None:  # wall-clock split used by the CPU baseline
             timings["layers_s"] = t_layers - t_start
             timings["head_s"] = _time.perf_counter() - t_layers

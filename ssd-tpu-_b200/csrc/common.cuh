@@ -89,23 +89,31 @@ struct OpMax {
   __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a > b ? a : b; }
 };
 
+// Acquire-release fetch-add at GPU scope (the ticket of a split reduction).
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* a, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+  return old;
+}
+
 // "Last block done" ticket: returns true in exactly one block of the group once
 // all `total` blocks of the group have called it.  The counter is reset to 0 by
 // that block, so the workspace stays reusable without a memset.  Each block must
-// have written its partial results before calling (a __threadfence is issued).
+// have written its partial results before calling.  Ordering without per-thread
+// fences: the first barrier puts the block's partial stores before thread 0's
+// acq_rel ticket (release); in the last block the ticket also acquires every
+// other block's partials and the second barrier passes that on to all of its
+// threads, which must read the partials with L2 loads (__ldcg).
 __device__ __forceinline__ bool last_block_of(unsigned int* counter, unsigned int total, bool* smem_flag) {
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned int prev = atomicAdd(counter, 1u);
-    bool last = (prev == total - 1);
-    if (last) atomicExch(counter, 0u);
+    const unsigned int prev = atom_add_acq_rel_gpu(counter, 1u);
+    const bool last = (prev == total - 1);
+    if (last) *reinterpret_cast<volatile unsigned int*>(counter) = 0u;
     *smem_flag = last;
   }
   __syncthreads();
-  bool last = *smem_flag;
-  if (last) __threadfence();
-  return last;
+  return *smem_flag;
 }
 
 // Every workspace starts with a fixed-size region of ticket counters.  It is the

@@ -57,4 +57,28 @@ int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, i
               size_t ws_bytes, int rowscale = 0, float eps = 0.f);
 bool linear_tc_supported(int M, int N, int K);
 
+// ---- tensor-parallel collectives fused into the tcgen05 projection epilogue
+constexpr int kMaxTP = 8;
+constexpr int kFlagTiles = 2048;  // output tiles (128 rows of W) per collective
+// Control block of a rank's symmetric heap: word 0 = sequence number of the
+// last finished collective, word 1 = CTA exit counter, word 2 = error status,
+// then arrival flags [2 parities][kMaxTP sources][kFlagTiles] from byte 256.
+constexpr size_t kCtrlFlagsOffset = 256;
+constexpr size_t kCommCtrlBytes = kCtrlFlagsOffset + sizeof(uint32_t) * 2 * kMaxTP * kFlagTiles;
+enum { COLL_NONE = 0, COLL_ALLREDUCE = 1, COLL_ALLGATHER = 2 };
+
+struct CollArgs {
+  int mode;             // COLL_*
+  int rank, world;
+  char* heaps[kMaxTP];  // every rank's heap base, mapped in this process
+  size_t ctrl_off;      // control block offset (same on every rank)
+  size_t dst_off;       // all-reduce: receive area; all-gather: the fp32 output [M, ldy]
+  int ldy, col_off;     // all-gather: row pitch and first column of this rank's block
+};
+
+// mode ALLREDUCE: y[M,N] (bf16, residual in/out) += round(sum over ranks of x_r w_r^T)
+// mode ALLGATHER: out[M, col_off .. col_off+N) = x w^T (fp32), written on every rank
+int linear_tc_coll(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,
+                   size_t ws_bytes, const CollArgs& ca);
+
 }  // namespace ssd

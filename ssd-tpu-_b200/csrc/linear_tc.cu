@@ -21,6 +21,25 @@
 //     the SM count only, independent of M.
 // Every mbarrier wait is bounded: on timeout the kernel records an error code,
 // stops issuing work, drains what it issued and releases its TMEM.
+//
+// Tensor parallelism fuses the collective into the same kernel.  Every rank
+// maps every other rank's symmetric heap (CUDA IPC over NVLink); the rank that
+// finishes an output tile stores its fp32 values straight into the peers'
+// heaps (plain stores, no TMA, no multicast) and raises one arrival flag per
+// peer and tile, so tile i crosses NVLink while tile i+1 is still being
+// multiplied:
+//   * all-reduce (row-parallel O / down): the partial tiles land in a receive
+//     area [parity][source rank][M][N]; the tile's owner on every rank waits
+//     for all sources' flags and folds them in rank order (so every rank holds
+//     bit-identical sums), adds the residual and stores bf16;
+//   * all-gather (vocab-parallel LM head): the fp32 logits columns land in the
+//     same place of every rank's logits buffer; the kernel's last CTA waits for
+//     every peer's tiles, so the logits are complete when the kernel ends.
+// Collectives are numbered by a device-resident sequence word (so CUDA-graph
+// replays need no host state); flags carry the number and buffers alternate by
+// its parity -- a rank can run at most one collective ahead of another.  Peer
+// waits are bounded in time; on expiry the kernel records SSD_ERR_TIMEOUT in
+// the control block and finishes without the missing data.
 #include <cuda.h>
 
 #include <mutex>
@@ -49,6 +68,10 @@ struct Params {
   float* part;   // [grid][2][M][BM] partial tiles
   unsigned int* counters;  // per tile (self-resetting)
   unsigned int* err;       // error word
+  // fused collective (COLL_NONE: plain epilogue)
+  int coll, rank, world, ldy, col_off;
+  char* heaps[kMaxTP];
+  size_t ctrl_off, dst_off;
 };
 
 __host__ __device__ inline int unit_begin(const Params& p, int c) { return c * p.base + (c < p.rem ? c : p.rem); }
@@ -90,6 +113,44 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
   }
   *abort_flag = 1;
   atomicExch(err, code);
+  return false;
+}
+
+// ---- cross-GPU signalling (system scope: the peers write over NVLink)
+constexpr uint64_t kPeerWaitNs = 5000000000ull;  // a peer that is 5 s late is reported, not awaited
+constexpr uint32_t kPeerWaitPolls = 1u << 27;
+
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t* ctrl_of(const Params& p, int r) {
+  return reinterpret_cast<uint32_t*>(p.heaps[r] + p.ctrl_off);
+}
+// arrival flag on rank `r` for (parity, source rank, tile)
+__device__ __forceinline__ uint32_t* flag_of(const Params& p, int r, uint32_t par, int src, int tile) {
+  return reinterpret_cast<uint32_t*>(p.heaps[r] + p.ctrl_off + kCtrlFlagsOffset) +
+         ((size_t)(par * kMaxTP + src) * kFlagTiles + tile);
+}
+// Bounded wait for a flag another GPU writes; false on timeout.
+__device__ bool wait_peer_flag(const uint32_t* f, uint32_t want) {
+  if (ld_relaxed_sys(f) == want) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kPeerWaitPolls; ++i) {
+    __nanosleep(32);
+    if (ld_relaxed_sys(f) == want) return true;
+    if ((i & 63u) == 63u && global_ns() - t0 > kPeerWaitNs) return false;
+  }
   return false;
 }
 
@@ -156,7 +217,9 @@ struct Cfg {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int MP>
+// COLL: instantiate the fused-collective epilogue (p.coll != COLL_NONE); the
+// plain projection is compiled without it so that its code stays small.
+template <int MP, bool COLL>
 __global__ void __launch_bounds__(kThreads)
 linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const Params p) {
@@ -249,6 +312,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         }
       }
     }
+    __syncwarp();  // the whole warp meets the final barrier together
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -292,11 +356,61 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         for (uint32_t t = 0; t < kWaitLimit && !mbar_try_wait(accf(buf), par); ++t) {}
       }
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
     pdl_wait();  // outputs, residual inputs and the workspace belong to the previous kernel until it ends
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const int row = q * 32 + lane;
+    auto n_of = [&](int tile) { return tile * BM + row; };
+    // ---- fused collective: this call's sequence number, pushes and tile completion
+    const uint32_t cj = COLL ? *reinterpret_cast<volatile uint32_t*>(ctrl_of(p, p.rank)) + 1u : 0u;
+    const uint32_t cpar = cj & 1u;
+    volatile int* coll_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
+    auto push = [&](int m, int n, float v) {  // this rank's value of output (m, n) to every rank
+      const size_t o = p.coll == COLL_ALLREDUCE
+                           ? p.dst_off + sizeof(float) * ((((size_t)cpar * p.world + p.rank) * p.M + m) * (size_t)p.N + n)
+                           : p.dst_off + sizeof(float) * ((size_t)m * p.ldy + p.col_off + n);
+      for (int d = 0; d < p.world; ++d) *reinterpret_cast<float*>(p.heaps[d] + o) = v;
+    };
+    auto coll_finish = [&](int tile) {
+      // the barrier orders every epilogue thread's pushes before thread 64's
+      // system-scope release stores of the flags (release is cumulative)
+      epi_bar();
+      if (threadIdx.x == 64)
+        for (int d = 0; d < p.world; ++d) st_release_sys(flag_of(p, d, cpar, p.rank, tile), cj);
+      if (p.coll != COLL_ALLREDUCE) return;
+      if (warp == 2) {  // lane s waits for source rank s
+        bool ok = true;
+        if (lane < p.world) {
+          ok = wait_peer_flag(flag_of(p, p.rank, cpar, lane, tile), cj);
+          fence_acq_rel_sys();
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) {
+          *coll_ok = ok ? 1 : 0;
+          if (!ok) {
+            atomicExch(p.err, 5u);
+            atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
+          }
+        }
+      }
+      epi_bar();
+      if (!*coll_ok || n_of(tile) >= p.N) return;
+      const int n = n_of(tile);
+      const float* recv = reinterpret_cast<const float*>(p.heaps[p.rank] + p.dst_off) +
+                          (size_t)cpar * p.world * p.M * p.N;
+      for (int m = 0; m < p.M; ++m) {
+        float v[kMaxTP];
+#pragma unroll
+        for (int r = 0; r < kMaxTP; ++r) v[r] = r < p.world ? __ldcg(recv + ((size_t)r * p.M + m) * p.N + n) : 0.f;
+        float sum = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxTP; ++r)
+          if (r < p.world) sum += v[r];  // rank order: identical on every rank
+        epilogue_store<bf16>(SSD_EPI_RESIDUAL, p.y, p.N, m, n, sum, 0.f);
+      }
+    };
     if (p.rowscale) {
       // RMS of each token row (the (1 + w) factor is folded into the weights):
       // warp (q) takes rows m = q, q+4, ...; lanes stride K in 8-element vectors,
@@ -349,8 +463,11 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
           if (m >= p.M) continue;
           if (whole) {
-            if (n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1)))
+            if constexpr (COLL) {
+              if (n < p.N) push(m, n, v[j]);
+            } else if (n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
               epilogue_store<bf16>(p.epi, p.y, p.N, m, n, v[j], up);
+            }
           } else {
             mine[(size_t)m * BM + row] = v[j];
           }
@@ -358,23 +475,28 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       }
       tc_fence_before();
       mbar_arrive(acce(buf));
-      if (whole) continue;
-      // ---- split tile: ticket, then the last contributor folds all partials in K order
-      __threadfence();
+      if (whole) {
+        if constexpr (COLL) coll_finish(tile);
+        continue;
+      }
+      // ---- split tile: ticket, then the last contributor folds all partials in K order.
+      // The barrier orders this CTA's partial stores before thread 64's ticket
+      // (an acq_rel RMW: release of our partials, acquire of the others' for the
+      // last contributor); the second barrier extends the acquire to all
+      // epilogue threads, whose fold loads read L2 (.cg).  No per-thread fence.
       epi_bar();
       const int c_first = cta_of_unit(p, tile * p.KB);
       const int c_last = cta_of_unit(p, tile * p.KB + p.KB - 1);
       if (threadIdx.x == 64) {
-        const unsigned int prev = atomicAdd(&p.counters[tile], 1u);
+        const unsigned int prev = atom_add_acq_rel_gpu(&p.counters[tile], 1u);
         const bool last = prev == (unsigned int)(c_last - c_first);
-        if (last) atomicExch(&p.counters[tile], 0u);
+        if (last) *reinterpret_cast<volatile unsigned int*>(&p.counters[tile]) = 0u;  // self-reset (stream-ordered)
         *last_flag = last ? 1 : 0;
       }
       epi_bar();
       const bool last = *last_flag != 0;
       epi_bar();  // everyone has read the flag before the next tile may rewrite it
       if (!last) continue;
-      __threadfence();
       // Fold the contributors in CTA (= K) order.  Rows are taken 16 at a time and
       // contributors 4 at a time so up to 64 independent L2 loads are in flight
       // per thread; the summation order per output stays c_first .. c_last.
@@ -402,10 +524,14 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         for (int i = 0; i < 16; ++i) {
           if (p.rowscale && i < mn) s[i] = __fmul_rn(s[i], inv_s[m0 + i]);
           const float up = __shfl_down_sync(0xffffffffu, s[i], 1);
-          if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1)))
+          if constexpr (COLL) {
+            if (i < mn && n < p.N) push(m0 + i, n, s[i]);
+          } else if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
             epilogue_store<bf16>(p.epi, p.y, p.N, m0 + i, n, s[i], up);
+          }
         }
       }
+      if constexpr (COLL) coll_finish(tile);
     }
   }
 
@@ -414,6 +540,54 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+  if constexpr (COLL) {
+    // The last CTA to leave (all-gather: after every peer's tiles have arrived)
+    // publishes the sequence number for the next collective.
+    uint32_t* ctrl = ctrl_of(p, p.rank);
+    volatile uint32_t* sm_last = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
+    volatile uint32_t* sm_cj = reinterpret_cast<volatile uint32_t*>(tmem_slot + 3);
+    if (threadIdx.x == 0) {
+      *sm_cj = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1u;
+      __threadfence();
+      *sm_last = atomicAdd(ctrl + 1, 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (*sm_last) {
+      const uint32_t cj = *sm_cj;
+      bool ok = true;
+      if (p.coll == COLL_ALLGATHER) {
+        const int tiles = (p.N + BM - 1) / BM;
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 0;; ++it) {
+          bool all = true;
+          for (int i = threadIdx.x; i < p.world * tiles; i += blockDim.x) {
+            const int src = i / tiles;
+            if (src != p.rank && ld_relaxed_sys(flag_of(p, p.rank, cj & 1u, src, i - src * tiles)) != cj) all = false;
+          }
+          if (__syncthreads_and(all)) break;
+          // one thread decides the timeout so that every thread leaves the loop together
+          const bool expired = threadIdx.x == 0 && (it >= kPeerWaitPolls || global_ns() - t0 > kPeerWaitNs);
+          if (__syncthreads_or(expired)) {
+            ok = false;
+            break;
+          }
+          __nanosleep(64);
+        }
+        fence_acq_rel_sys();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (!ok) {
+          atomicExch(p.err, 5u);
+          atomicExch(ctrl + 2, (unsigned int)SSD_ERR_TIMEOUT);
+        }
+        ctrl[1] = 0u;
+        __threadfence();
+        *reinterpret_cast<volatile uint32_t*>(ctrl) = cj;
+        __threadfence();
+      }
+    }
   }
 }
 
@@ -501,7 +675,7 @@ size_t workspace_bytes(int M, int N, int K) {
 
 template <int MP>
 int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-           int rowscale, float eps) {
+           int rowscale, float eps, const CollArgs* ca) {
   using C = Cfg<MP>;
   CUtensorMap wm, xm;
   if (!weight_map(&wm, w, N, K)) return SSD_ERR_LAUNCH;
@@ -521,12 +695,32 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   p.counters = reinterpret_cast<unsigned int*>(wsb);
   p.err = reinterpret_cast<unsigned int*>(wsb + kCounterBytes);
   p.part = reinterpret_cast<float*>(wsb + kCounterBytes + 256);
-  auto kern = linear_tc_kernel<MP>;
+  p.coll = COLL_NONE;
+  if (ca && ca->mode != COLL_NONE) {
+    p.coll = ca->mode;
+    p.rank = ca->rank;
+    p.world = ca->world;
+    p.ldy = ca->ldy;
+    p.col_off = ca->col_off;
+    for (int r = 0; r < kMaxTP; ++r) p.heaps[r] = r < ca->world ? ca->heaps[r] : nullptr;
+    p.ctrl_off = ca->ctrl_off;
+    p.dst_off = ca->dst_off;
+  }
+  auto kern = p.coll != COLL_NONE ? linear_tc_kernel<MP, true> : linear_tc_kernel<MP, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
     return SSD_ERR_LAUNCH;
   SSD_PDL(kern, grid, kThreads, C::SMEM, st, wm, xm, p);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
+}
+
+template <typename... A>
+int launch_any(int M, A... a) {
+  if (M <= 16) return launch<16>(a...);
+  if (M <= 32) return launch<32>(a...);
+  if (M <= 64) return launch<64>(a...);
+  if (M <= 128) return launch<128>(a...);
+  return launch<256>(a...);
 }
 
 }  // namespace tc
@@ -542,11 +736,17 @@ int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, i
               size_t ws_bytes, int rowscale, float eps) {
   if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
-  if (M <= 16) return tc::launch<16>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
-  if (M <= 32) return tc::launch<32>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
-  if (M <= 64) return tc::launch<64>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
-  if (M <= 128) return tc::launch<128>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
-  return tc::launch<256>(st, x, w, y, epi, M, N, K, ws, rowscale, eps);
+  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, rowscale, eps, (const CollArgs*)nullptr);
+}
+
+int linear_tc_coll(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,
+                   size_t ws_bytes, const CollArgs& ca) {
+  if (!linear_tc_supported(M, N, K)) return SSD_ERR_UNSUPPORTED;
+  if ((N + tc::BM - 1) / tc::BM > kFlagTiles) return SSD_ERR_UNSUPPORTED;
+  if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
+  const int epi = ca.mode == COLL_ALLREDUCE ? SSD_EPI_RESIDUAL : SSD_EPI_STORE_F32;
+  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, 0, 0.f, &ca);
 }
 
 }  // namespace ssd

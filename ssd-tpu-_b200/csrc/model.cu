@@ -178,6 +178,11 @@ Scratch carve(const ssd_gemma_weights* w, int B, int T, int max_seq_len, char* b
 
 }  // namespace
 
+int linear_allreduce_impl(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,
+                          size_t ws_bytes, const ssd_comm* c);
+int linear_allgather_impl(cudaStream_t st, const void* x, const void* w, float* y, int ldy, int M, int N, int K,
+                          void* ws, size_t ws_bytes, const ssd_comm* c);
+
 int linear_dispatch(cudaStream_t st, const void* x, const void* w, int dtype, void* y, int epi, int M, int N, int K,
                     void* ws, size_t ws_bytes, int rowscale = 0, float eps = 0.f) {
   if (dtype == SSD_DTYPE_BF16) {
@@ -282,6 +287,8 @@ static bool weights_ok(const ssd_gemma_weights* w) {
     return false;
   for (int l = 0; l < w->num_layers; ++l)
     if (!w->w_qkv[l] || !w->w_o[l] || !w->w_gate_up[l] || !w->w_down[l]) return false;
+  if (w->tp_world < 0 || w->tp_world > SSD_MAX_TP || w->tp_rank < 0 || (w->tp_world > 1 && w->tp_rank >= w->tp_world))
+    return false;
   return true;
 }
 
@@ -299,6 +306,13 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
   if (M > max_m()) return SSD_ERR_UNSUPPORTED;
   if ((int64_t)bt->max_blocks * bt->block_size < bt->max_seq_len) return SSD_ERR_INVALID;
   if (bt->max_seq_len > w->rope_max_pos) return SSD_ERR_INVALID;
+  if (w->tp_world > 1 && !bt->comm) return SSD_ERR_INVALID;
+  if (bt->comm) {
+    const ssd_comm* c = bt->comm;
+    if (c->world != std::max(w->tp_world, 1) || c->rank != w->tp_rank || w->dtype != SSD_DTYPE_BF16 ||
+        w->vocab % c->world)
+      return SSD_ERR_INVALID;
+  }
   const Scratch s = carve(w, B, T, bt->max_seq_len, reinterpret_cast<char*>(bt->scratch));
   if (bt->scratch_bytes < s.total) return SSD_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
@@ -322,10 +336,10 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     if (capturing) cudaEventRecordWithFlags((cudaEvent_t)ev, st, cudaEventRecordExternal);
     else cudaEventRecord((cudaEvent_t)ev, st);
   };
-  auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k, int rowscale) {
+  auto timed = [&](int kind, auto&& launch) {
     const bool rec = bt->prof_events && nprof < bt->prof_capacity;
     if (rec) rec_event(bt->prof_events[2 * nprof]);
-    const int r = linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes, rowscale, w->eps);
+    const int r = launch();
     if (rec) {
       rec_event(bt->prof_events[2 * nprof + 1]);
       if (bt->prof_kind) bt->prof_kind[nprof] = kind;
@@ -333,6 +347,26 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
       if (bt->prof_count) *bt->prof_count = nprof;
     }
     return r;
+  };
+  auto proj = [&](int kind, const void* x, const void* wt, void* y, int epi, int m, int n, int k, int rowscale) {
+    return timed(kind, [&] {
+      return linear_dispatch(st, x, wt, dt, y, epi, m, n, k, s.lin_ws, s.lin_ws_bytes, rowscale, w->eps);
+    });
+  };
+  // row-parallel projection + residual: all-reduced over the tensor-parallel group when there is one
+  const ssd_comm* comm = bt->comm;
+  auto proj_rowpar = [&](int kind, const void* x, const void* wt, void* y, int m, int n, int k) {
+    if (!comm) return proj(kind, x, wt, y, SSD_EPI_RESIDUAL, m, n, k, 0);
+    return timed(kind, [&] { return linear_allreduce_impl(st, x, wt, y, m, n, k, s.lin_ws, s.lin_ws_bytes, comm); });
+  };
+  // tied LM head, vocab-parallel under tensor parallelism
+  auto lm_head = [&](const void* x, int m) {
+    if (!comm) return proj(4, x, w->embed, bt->logits, SSD_EPI_STORE_F32, m, w->vocab, d, 0);
+    const int vloc = w->vocab / comm->world;
+    const void* wt = reinterpret_cast<const bf16*>(w->embed) + (size_t)comm->rank * vloc * d;
+    return timed(4, [&] {
+      return linear_allgather_impl(st, x, wt, bt->logits, w->vocab, m, vloc, d, s.lin_ws, s.lin_ws_bytes, comm);
+    });
   };
   if (bt->prof_count) *bt->prof_count = 0;
 
@@ -350,9 +384,9 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     SSD_TRY(ssd_paged_verify_attention(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
                                        bt->block_tables, bt->max_blocks, s.seq_after, s.qlen, s.attn, scale, B, T,
                                        hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes));
-    SSD_TRY(proj(1, s.attn, w->w_o[l], s.x, SSD_EPI_RESIDUAL, M, d, hq * D, 0));
+    SSD_TRY(proj_rowpar(1, s.attn, w->w_o[l], s.x, M, d, hq * D));
     SSD_TRY(proj(2, s.x, w->w_gate_up[l], s.act, SSD_EPI_GEGLU, M, 2 * F, d, 1));  // mlp_norm folded likewise
-    SSD_TRY(proj(3, s.act, w->w_down[l], s.x, SSD_EPI_RESIDUAL, M, d, F, 0));
+    SSD_TRY(proj_rowpar(3, s.act, w->w_down[l], s.x, M, d, F));
   }
   if (!bt->logits) return SSD_OK;  // prompt chunk: only the K/V rows were needed
   SSD_TRY(ssd_rmsnorm(stream, s.x, w->final_norm, dt, s.h, M, d, w->eps));
@@ -362,9 +396,9 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     else
       SSD_PDL(gather_last_kernel<float>, B, 256, 0, st, (const float*)s.h, s.qlen, T, d, (float*)s.hl);
     SSD_CHECK_LAUNCH();
-    SSD_TRY(proj(4, s.hl, w->embed, bt->logits, SSD_EPI_STORE_F32, B, w->vocab, d, 0));
+    SSD_TRY(lm_head(s.hl, B));
   } else {
-    SSD_TRY(proj(4, s.h, w->embed, bt->logits, SSD_EPI_STORE_F32, M, w->vocab, d, 0));
+    SSD_TRY(lm_head(s.h, M));
   }
 #undef SSD_TRY
   return SSD_OK;

@@ -58,7 +58,25 @@ SIGNATURES = {
     "ssd_gemma_scratch_size": (_sz, [_p, _i, _i, _i]),
     "ssd_gemma_forward": (_i, [_p, _p, _p]),
     "ssd_normal_fill": (_i, [_p, _p, _i, _i64, _f, _u64]),
+    "ssd_comm_ctrl_bytes": (_sz, []),
+    "ssd_comm_recv_bytes": (_sz, [_i, _i, _i]),
+    "ssd_ipc_export": (_i, [_p, _p, C.POINTER(_sz)]),
+    "ssd_ipc_import": (_i, [_p, _sz, C.POINTER(_p)]),
+    "ssd_ipc_close": (_i, [_p, _sz]),
+    "ssd_linear_allreduce": (_i, [_p, _p, _p, _p, _i, _i, _i, _p, _sz, _p]),
+    "ssd_linear_allgather": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
 }
+
+SSD_MAX_TP = 8
+
+
+class CommC(C.Structure):
+    """ssd_comm."""
+
+    _fields_ = [
+        ("rank", _i), ("world", _i), ("heaps", _p * SSD_MAX_TP), ("heap_bytes", _sz),
+        ("ctrl_offset", _sz), ("recv_offset", _sz), ("recv_bytes", _sz),
+    ]
 
 
 class GemmaWeightsC(C.Structure):
@@ -70,6 +88,7 @@ class GemmaWeightsC(C.Structure):
         ("embed", _p), ("final_norm", _p),
         ("w_qkv", C.POINTER(_p)), ("w_o", C.POINTER(_p)), ("w_gate_up", C.POINTER(_p)), ("w_down", C.POINTER(_p)),
         ("rope_cos", _p), ("rope_sin", _p), ("rope_max_pos", _i),
+        ("tp_rank", _i), ("tp_world", _i),
     ]
 
 
@@ -83,6 +102,7 @@ class GemmaBatchC(C.Structure):
         ("scratch", _p), ("scratch_bytes", _sz),
         ("prof_events", C.POINTER(_p)), ("prof_capacity", _i), ("prof_count", C.POINTER(_i)),
         ("prof_kind", C.POINTER(_i)),
+        ("comm", C.POINTER(CommC)),
     ]
 
 

@@ -61,3 +61,29 @@ def max_tokens_per_forward(dtype=None) -> int:
     if dtype == torch.float32:
         return 16
     return int(lib().ssd_linear_max_m())
+
+
+def linear_allreduce(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, comm, ws_key: str = "linear") -> torch.Tensor:
+    """y[M,N] += sum over the tensor-parallel ranks of x_r w_r^T (bf16; ``ssd_linear_allreduce``)."""
+    import ctypes as C
+
+    m, k = x.shape
+    n = w.shape[0]
+    nbytes = lib().ssd_linear_workspace_size(m, n, k)
+    ws = workspace(x.device, ws_key, nbytes)
+    check(lib().ssd_linear_allreduce(stream_ptr(), ptr(x), ptr(w), ptr(y), m, n, k, ptr(ws), ws.numel(),
+                                     C.byref(comm.cstruct)), "ssd_linear_allreduce")
+    return y
+
+
+def linear_allgather(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, comm, ws_key: str = "linear") -> torch.Tensor:
+    """y[M, rank*N:(rank+1)*N] = x w^T (fp32) on every rank; y from ``comm.alloc`` (``ssd_linear_allgather``)."""
+    import ctypes as C
+
+    m, k = x.shape
+    n = w.shape[0]
+    nbytes = lib().ssd_linear_workspace_size(m, n, k)
+    ws = workspace(x.device, ws_key, nbytes)
+    check(lib().ssd_linear_allgather(stream_ptr(), ptr(x), ptr(w), ptr(y), y.shape[-1], m, n, k, ptr(ws),
+                                     ws.numel(), C.byref(comm.cstruct)), "ssd_linear_allgather")
+    return y

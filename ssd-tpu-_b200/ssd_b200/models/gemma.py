@@ -70,6 +70,10 @@ PRESETS = {
     "toy-draft": GemmaShape(1, 256, 4, 1, 64, 1024, 1024),
     "gemma-7b": GemmaShape(28, 3072, 16, 16, 256, 24576, 256000),
     "gemma-2b": GemmaShape(18, 2048, 8, 1, 256, 16384, 256000),
+    # small bf16 pair whose every projection suits the tcgen05 path at 1..8 ranks
+    # (tensor-parallel tests): 8 heads of 64, FFN 1024, vocab 2048
+    "tp-target": GemmaShape(2, 256, 8, 8, 64, 1024, 2048),
+    "tp-draft": GemmaShape(1, 256, 8, 1, 64, 1024, 2048),
 }
 
 EMBED_STD = 0.005
@@ -115,6 +119,7 @@ class GemmaWeights:
         self.rope_cos = torch.from_numpy(cos).to(self.device)
         self.rope_sin = torch.from_numpy(sin).to(self.device)
         self.max_pos = max_pos
+        self.tp_rank, self.tp_world = 0, 1  # set by runtime.tensor_parallel.shard_weights
         self._cstruct = None
 
     # ------------------------------------------------------------ init
@@ -206,6 +211,7 @@ class GemmaWeights:
             P = C.POINTER(C.c_void_p)
             cs.w_qkv, cs.w_o, cs.w_gate_up, cs.w_down = [C.cast(a, P) for a in self._arrays]
             cs.rope_cos, cs.rope_sin, cs.rope_max_pos = ptr(self.rope_cos), ptr(self.rope_sin), self.max_pos
+            cs.tp_rank, cs.tp_world = self.tp_rank, self.tp_world
             self._cstruct = cs
         return self._cstruct
 
@@ -215,13 +221,22 @@ class GemmaWeights:
 
 
 class GemmaRunner:
-    """One ``ssd_gemma_forward`` per call; scratch sized for (max_batch, max_tokens)."""
+    """One ``ssd_gemma_forward`` per call; scratch sized for (max_batch, max_tokens).
 
-    def __init__(self, weights: GemmaWeights, max_batch: int, max_tokens: int, max_seq_len: int):
+    With ``comm`` (a ``runtime.tensor_parallel.TPComm``) the weights are one
+    rank's shard and the logits buffers passed to ``forward`` must come from
+    ``comm.alloc`` (the LM head all-gathers into them).
+    """
+
+    def __init__(self, weights: GemmaWeights, max_batch: int, max_tokens: int, max_seq_len: int, comm=None):
         self.w = weights
         self.max_batch = max_batch
         self.max_tokens = max_tokens
         self.max_seq_len = max_seq_len
+        self.comm = comm
+        if weights.tp_world > 1 and comm is None:
+            raise ValueError("sharded weights need the tensor-parallel comm")
+        self._comm_ptr = C.pointer(comm.cstruct) if comm is not None else None
         self._scratch = {}
 
     def scratch(self, b: int, t: int) -> torch.Tensor:
@@ -247,6 +262,7 @@ class GemmaRunner:
         bt.max_seq_len = self.max_seq_len
         bt.logits, bt.logits_last_only = ptr(logits), int(bool(last_only))
         bt.scratch, bt.scratch_bytes = ptr(sc), sc.numel()
+        bt.comm = self._comm_ptr
         if prof is not None:
             prof.attach(bt)
         check(lib().ssd_gemma_forward(stream_ptr(stream), C.byref(self.w.cstruct()), C.byref(bt)),

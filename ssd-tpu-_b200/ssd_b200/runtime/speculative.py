@@ -39,34 +39,40 @@ from .page_manager import PageManager
 
 
 class _Model:
-    def __init__(self, weights: GemmaWeights, max_seq_len: int, block_size: int, k: int):
+    def __init__(self, weights: GemmaWeights, max_seq_len: int, block_size: int, k: int, comm=None):
         s = weights.shape
         self.w = weights
         self.num_blocks = (max_seq_len + block_size - 1) // block_size + 2
         self.cache = KVCacheState.allocate(s.num_layers, self.num_blocks, block_size, s.num_kv_heads, s.head_dim,
                                            dtype=weights.dtype, device=weights.device)
         self.pm = PageManager(block_size, self.num_blocks, max_seqs=1, device=weights.device)
-        self.runner = GemmaRunner(weights, 1, max(k + 1, max_tokens_per_forward(weights.dtype)), max_seq_len)
+        self.runner = GemmaRunner(weights, 1, max(k + 1, max_tokens_per_forward(weights.dtype)), max_seq_len,
+                                  comm=comm)
         self.chunk = min(64, max_tokens_per_forward(weights.dtype))
         self.n = 0  # tokens in the cache
 
 
 class SpeculativeDecoder:
     def __init__(self, target: GemmaWeights, draft: GemmaWeights, k: int = 4, max_seq_len: int = 1024,
-                 block_size: int = 16, use_graphs: bool = True, timer=None):
+                 block_size: int = 16, use_graphs: bool = True, timer=None, comm=None):
+        """``comm``: tensor-parallel group (``runtime.tensor_parallel.TPComm``); the
+        weights are then this rank's shards and every rank runs the same steps."""
         self.k = k
         self.dev = target.device
         self.max_seq_len = max_seq_len
-        self.t = _Model(target, max_seq_len, block_size, k)
-        self.d = _Model(draft, max_seq_len, block_size, k)
+        self.comm = comm
+        self.t = _Model(target, max_seq_len, block_size, k, comm)
+        self.d = _Model(draft, max_seq_len, block_size, k, comm)
         V = target.shape.vocab
         if draft.shape.vocab != V:
             raise ValueError("target and draft must share the vocabulary")
         dev = self.dev
         self.vt = torch.zeros((1, k + 1), dtype=torch.int32, device=dev)   # [recovery, draft...]
         self.feed = torch.zeros((1, 2), dtype=torch.int32, device=dev)
-        self.logits_t = torch.empty((1, k + 1, V), dtype=torch.float32, device=dev)
-        self.logits_d = torch.empty((1, V), dtype=torch.float32, device=dev)
+        buf = comm.alloc if comm is not None else (
+            lambda shape, dtype: torch.empty(shape, dtype=dtype, device=dev))
+        self.logits_t = buf((1, k + 1, V), torch.float32)  # written by every rank's LM head block
+        self.logits_d = buf((1, V), torch.float32)
         self.acc_rec = torch.zeros(2, dtype=torch.int32, device=dev)
         self.mask = torch.empty((1, k + 1), dtype=torch.uint8, device=dev)
         self.host = torch.zeros(2, dtype=torch.int32).pin_memory()
@@ -232,10 +238,12 @@ class SpeculativeDecoder:
 class GreedyDecoder:
     """Target-only greedy decode (the AR loop of engine.py:162-211) on the same kernels."""
 
-    def __init__(self, target: GemmaWeights, max_seq_len: int = 1024, block_size: int = 16):
-        self.t = _Model(target, max_seq_len, block_size, 1)
+    def __init__(self, target: GemmaWeights, max_seq_len: int = 1024, block_size: int = 16, comm=None):
+        self.t = _Model(target, max_seq_len, block_size, 1, comm)
         self.dev = target.device
-        self.lg = torch.empty((1, target.shape.vocab), dtype=torch.float32, device=self.dev)
+        V = target.shape.vocab
+        self.lg = comm.alloc((1, V), torch.float32) if comm is not None else torch.empty(
+            (1, V), dtype=torch.float32, device=self.dev)
 
     def generate(self, prompt: list[int], max_new: int) -> list[int]:
         t, dev, lg = self.t, self.dev, self.lg

@@ -259,7 +259,8 @@ int ssd_linear_rownorm(ssd_stream_t stream, const void* x, const void* w, int dt
  * All ranks must issue the same collective calls in the same order on one
  * stream each; a rank that is more than about 5 s late makes the others give up,
  * record SSD_ERR_TIMEOUT in word 2 of their control block and finish with
- * incomplete results (nothing hangs).
+ * incomplete results (nothing hangs).  The control block also holds per-tile
+ * delivery counts and flags (device state, so CUDA graphs replay the calls).
  */
 #define SSD_MAX_TP 8
 typedef struct {
@@ -268,6 +269,7 @@ typedef struct {
   size_t heap_bytes;               /* size of every rank's heap */
   size_t ctrl_offset;              /* control block (ssd_comm_ctrl_bytes), zero-filled before first use */
   size_t recv_offset, recv_bytes;  /* all-reduce receive area (>= ssd_comm_recv_bytes) */
+  int recv_rows, recv_tiles;       /* its shape: the max_m and ceil(max_n / 128) it was sized for */
 } ssd_comm;
 
 /* Bytes of the control block (multiple of 256). */

@@ -45,7 +45,7 @@ template <> struct Vec16<float> { static constexpr int N = 4; };
 template <int N>
 __device__ __forceinline__ void load_n(const bf16* p, float* f) {
   if constexpr (N == 8) {
-    unpack8(ldg_nc_v4(p), f);
+    unpack8(ld_act_v4(p), f);
   } else if constexpr (N == 4) {
     uint2 u = *reinterpret_cast<const uint2*>(p);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -82,8 +82,8 @@ struct RowInfo {
 // (lane-strided over splits, xor-tree sums: an empty split's exact zeros leave
 // them unchanged), then every output element sums w_s * o_s in split order.
 template <typename KV, int D>
-__device__ __forceinline__ void attention_fold(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
-                                               KV* __restrict__ out, int64_t grp_id, int nsplit, int seq_len,
+__device__ __forceinline__ void attention_fold(const float* ws_o, const float2* ws_ml,
+                                               KV* out, int64_t grp_id, int nsplit, int seq_len,
                                                int nrows, int row0, int G, int T, int hq, int kvh, int b,
                                                float* wsm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -128,11 +128,11 @@ __device__ __forceinline__ void attention_fold(const float* __restrict__ ws_o, c
 
 template <typename KV, int D>
 __global__ void __launch_bounds__(kAttnThreads)
-paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, int num_layers, int num_blocks,
-                       int block_size, int hkv, int layer, const int32_t* __restrict__ block_tables,
-                       int max_blocks, const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ q_lens,
-                       KV* __restrict__ out, float scale, int T, int hq, int row_groups, int nsplit,
-                       float* __restrict__ ws_o, float2* __restrict__ ws_ml, unsigned int* __restrict__ counters) {
+paged_attention_kernel(const KV* q, const KV* pages, int num_layers, int num_blocks,
+                       int block_size, int hkv, int layer, const int32_t* block_tables,
+                       int max_blocks, const int32_t* seq_lens, const int32_t* q_lens,
+                       KV* out, float scale, int T, int hq, int row_groups, int nsplit,
+                       float* ws_o, float2* ws_ml, unsigned int* counters) {
   using S = AttnSmem<KV, D>;
   constexpr int V16 = Vec16<KV>::N;      // elements per 16-byte load
   constexpr int DPL = D / 32;            // head dims per lane in P.V
@@ -209,7 +209,7 @@ paged_attention_kernel(const KV* __restrict__ q, const KV* __restrict__ pages, i
     const int64_t off = __shfl_sync(0xffffffffu, my_off, j);
 #pragma unroll
     for (int c = 0; c < KCH; ++c)
-      kraw[rd][c] = (j < jn) ? ldg_nc_v4(kbase + off + c * 8 * V16 + li * V16) : make_uint4(0, 0, 0, 0);
+      kraw[rd][c] = (j < jn) ? ld_act_v4(kbase + off + c * 8 * V16 + li * V16) : make_uint4(0, 0, 0, 0);
   }
 
   // q rows -> fp32 smem (zeros for padding rows), while the K loads are in flight
@@ -386,11 +386,11 @@ struct TcSmem {
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-paged_attention_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ pages, int num_layers,
-                          int num_blocks, int block_size, int hkv, int layer, const int32_t* __restrict__ block_tables,
-                          int max_blocks, const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ q_lens,
-                          bf16* __restrict__ out, float scale, int T, int hq, int row_groups, int nsplit,
-                          float* __restrict__ ws_o, float2* __restrict__ ws_ml, unsigned int* __restrict__ counters) {
+paged_attention_tc_kernel(const bf16* q, const bf16* pages, int num_layers,
+                          int num_blocks, int block_size, int hkv, int layer, const int32_t* block_tables,
+                          int max_blocks, const int32_t* seq_lens, const int32_t* q_lens,
+                          bf16* out, float scale, int T, int hq, int row_groups, int nsplit,
+                          float* ws_o, float2* ws_ml, unsigned int* counters) {
   using S = TcSmem<D>;
   constexpr int ST = S::STRIDE;
   constexpr int KSTEPS = D / 16;
@@ -585,10 +585,10 @@ paged_attention_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ p
 
 // ---------------------------------------------------------------- K2
 template <typename KV>
-__global__ void kv_write_kernel(KV* __restrict__ pages, int num_layers, int num_blocks, int block_size, int hkv,
-                                int D, int layer, const int32_t* __restrict__ block_tables, int max_blocks,
-                                const int32_t* __restrict__ positions, const KV* __restrict__ k,
-                                const KV* __restrict__ v, int T) {
+__global__ void kv_write_kernel(KV* pages, int num_layers, int num_blocks, int block_size, int hkv,
+                                int D, int layer, const int32_t* block_tables, int max_blocks,
+                                const int32_t* positions, const KV* k,
+                                const KV* v, int T) {
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.y, t = blockIdx.x;
@@ -609,11 +609,11 @@ __global__ void kv_write_kernel(KV* __restrict__ pages, int num_layers, int num_
 // RoPE on q and k of a fused qkv row, q -> q_out, k (rotated) and v -> pages.
 // grid (Hq + Hkv, T, B): one CTA per head of one token, one thread per rotation pair.
 template <typename KV>
-__global__ void rope_kv_write_kernel(const KV* __restrict__ qkv, KV* __restrict__ q_out, KV* __restrict__ pages,
+__global__ void rope_kv_write_kernel(const KV* qkv, KV* q_out, KV* pages,
                                      int num_layers, int num_blocks, int block_size, int hq, int hkv, int D,
-                                     int layer, const int32_t* __restrict__ block_tables, int max_blocks,
-                                     const int32_t* __restrict__ positions, const float* __restrict__ cos_t,
-                                     const float* __restrict__ sin_t, int rope_max_pos, int T) {
+                                     int layer, const int32_t* block_tables, int max_blocks,
+                                     const int32_t* positions, const float* cos_t,
+                                     const float* sin_t, int rope_max_pos, int T) {
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x, t = blockIdx.y, b = blockIdx.z;

@@ -52,11 +52,15 @@ static_assert(SSD_MAX_TP == kMaxTP, "SSD_MAX_TP mismatch");
 int linear_allreduce_impl(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,
                           size_t ws_bytes, const ssd_comm* c) {
   if (!comm_ok(c) || !x || !w || !y || M <= 0 || N <= 0 || K <= 0) return SSD_ERR_INVALID;
-  if (ssd_comm_recv_bytes(c->world, M, N) > c->recv_bytes || c->recv_offset % 256 ||
+  const int tiles = (N + 127) / 128;
+  if (M > c->recv_rows || tiles > c->recv_tiles || c->recv_offset % 256 ||
+      ssd_comm_recv_bytes(c->world, c->recv_rows, c->recv_tiles * 128) > c->recv_bytes ||
       c->recv_offset + c->recv_bytes > c->heap_bytes)
     return SSD_ERR_INVALID;
   CollArgs a = coll_args(c, COLL_ALLREDUCE);
   a.dst_off = c->recv_offset;
+  a.recv_rows = c->recv_rows;
+  a.recv_tiles = c->recv_tiles;
   return linear_tc_coll(st, x, w, y, M, N, K, ws, ws_bytes, a);
 }
 
@@ -84,7 +88,8 @@ extern "C" size_t ssd_comm_ctrl_bytes(void) { return align_up256(kCommCtrlBytes)
 
 extern "C" size_t ssd_comm_recv_bytes(int world, int max_m, int max_n) {
   if (world <= 0 || max_m <= 0 || max_n <= 0) return 0;
-  return align_up256(sizeof(float) * 2 * (size_t)world * max_m * max_n);
+  const size_t tiles = (size_t)(max_n + 127) / 128;  // slots [2][tiles][world][max_m][128] fp32
+  return align_up256(sizeof(float) * 2 * tiles * world * (size_t)max_m * 128);
 }
 
 extern "C" int ssd_ipc_export(const void* ptr, void* handle, size_t* offset) {

@@ -136,6 +136,26 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   }
 }
 
+// Loads of data that an earlier kernel of the stream wrote.  Every kernel is
+// launched with programmatic dependent launch, so a grid is already resident
+// while its predecessor still writes; the non-coherent read-only path
+// (ld.global.nc, which the compiler may also pick for const __restrict__
+// pointers) can then serve stale lines even after griddepcontrol.wait.
+// Activations, logits, token ids, positions and page tables are therefore read
+// through L2 (ld.global.cg); only weights and constant tables that no kernel
+// writes use ldg_nc_v4.  Kernel parameters carry no __restrict__ for the same
+// reason.
+__device__ __forceinline__ uint4 ld_act_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ T ld_act(const T* p) {
+  return __ldcg(p);
+}
+
+// Weights and constant tables only (see ld_act_v4).
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

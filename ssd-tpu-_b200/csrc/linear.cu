@@ -44,8 +44,8 @@ template <> struct WVec<float> {
 
 template <typename T, int MMAX, int ROWS>
 __global__ void __launch_bounds__(kLinThreads)
-linear_cc_kernel(const T* __restrict__ x, const T* __restrict__ w, void* __restrict__ y, int epi, int M, int N,
-                 int K, int splits, int kc, float* __restrict__ ws, unsigned int* __restrict__ counters,
+linear_cc_kernel(const T* x, const T* w, void* y, int epi, int M, int N,
+                 int K, int splits, int kc, float* ws, unsigned int* counters,
                  int rowscale, float eps) {
   constexpr int VN = WVec<T>::N;
   constexpr int STEP = 32 * VN;

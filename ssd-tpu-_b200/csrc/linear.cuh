@@ -60,11 +60,14 @@ bool linear_tc_supported(int M, int N, int K);
 // ---- tensor-parallel collectives fused into the tcgen05 projection epilogue
 constexpr int kMaxTP = 8;
 constexpr int kFlagTiles = 2048;  // output tiles (128 rows of W) per collective
-// Control block of a rank's symmetric heap: word 0 = sequence number of the
-// last finished collective, word 1 = CTA exit counter, word 2 = error status,
-// then arrival flags [2 parities][kMaxTP sources][kFlagTiles] from byte 256.
-constexpr size_t kCtrlFlagsOffset = 256;
-constexpr size_t kCommCtrlBytes = kCtrlFlagsOffset + sizeof(uint32_t) * 2 * kMaxTP * kFlagTiles;
+// Control block of a rank's symmetric heap: word 2 = error status; from byte
+// 256 the per-tile counters (how many collectives this rank has finished for
+// output tile t -- every rank makes the same calls, so the counts agree), then
+// the arrival flags [kMaxTP source ranks][kFlagTiles]: flag[s][t] holds the
+// count of the last tile t that rank s has delivered here.
+constexpr size_t kCtrlCountersOffset = 256;
+constexpr size_t kCtrlFlagsOffset = kCtrlCountersOffset + sizeof(uint32_t) * kFlagTiles;
+constexpr size_t kCommCtrlBytes = kCtrlFlagsOffset + sizeof(uint32_t) * kMaxTP * kFlagTiles;
 enum { COLL_NONE = 0, COLL_ALLREDUCE = 1, COLL_ALLGATHER = 2 };
 
 struct CollArgs {
@@ -74,6 +77,7 @@ struct CollArgs {
   size_t ctrl_off;      // control block offset (same on every rank)
   size_t dst_off;       // all-reduce: receive area; all-gather: the fp32 output [M, ldy]
   int ldy, col_off;     // all-gather: row pitch and first column of this rank's block
+  int recv_rows, recv_tiles;  // all-reduce: receive slots [2][recv_tiles][world][recv_rows][128] fp32
 };
 
 // mode ALLREDUCE: y[M,N] (bf16, residual in/out) += round(sum over ranks of x_r w_r^T)

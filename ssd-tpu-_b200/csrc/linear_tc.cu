@@ -35,9 +35,13 @@
 //   * all-gather (vocab-parallel LM head): the fp32 logits columns land in the
 //     same place of every rank's logits buffer; the kernel's last CTA waits for
 //     every peer's tiles, so the logits are complete when the kernel ends.
-// Collectives are numbered by a device-resident sequence word (so CUDA-graph
-// replays need no host state); flags carry the number and buffers alternate by
-// its parity -- a rank can run at most one collective ahead of another.  Peer
+// Each rank counts, per output tile, the collectives it has finished (device
+// memory, so CUDA-graph replays need no host state; every rank makes the same
+// calls, so the counts agree).  A delivery of tile t carries the count as its
+// flag value, and the all-reduce receive slots [parity][tile][source] alternate
+// by the count's parity -- a rank can be at most one delivery of a tile ahead of
+// another.  The tile's owner on every rank waits for all peers' deliveries of
+// that tile, so a kernel ends only when all of its tiles have arrived.  Peer
 // waits are bounded in time; on expiry the kernel records SSD_ERR_TIMEOUT in
 // the control block and finishes without the missing data.
 #include <cuda.h>
@@ -69,7 +73,7 @@ struct Params {
   unsigned int* counters;  // per tile (self-resetting)
   unsigned int* err;       // error word
   // fused collective (COLL_NONE: plain epilogue)
-  int coll, rank, world, ldy, col_off;
+  int coll, rank, world, ldy, col_off, recv_rows, recv_tiles;
   char* heaps[kMaxTP];
   size_t ctrl_off, dst_off;
 };
@@ -137,10 +141,16 @@ __device__ __forceinline__ uint64_t global_ns() {
 __device__ __forceinline__ uint32_t* ctrl_of(const Params& p, int r) {
   return reinterpret_cast<uint32_t*>(p.heaps[r] + p.ctrl_off);
 }
-// arrival flag on rank `r` for (parity, source rank, tile)
-__device__ __forceinline__ uint32_t* flag_of(const Params& p, int r, uint32_t par, int src, int tile) {
-  return reinterpret_cast<uint32_t*>(p.heaps[r] + p.ctrl_off + kCtrlFlagsOffset) +
-         ((size_t)(par * kMaxTP + src) * kFlagTiles + tile);
+// arrival flag on rank `r` for (source rank, tile)
+__device__ __forceinline__ uint32_t* flag_of(const Params& p, int r, int src, int tile) {
+  return reinterpret_cast<uint32_t*>(p.heaps[r] + p.ctrl_off + kCtrlFlagsOffset) + ((size_t)src * kFlagTiles + tile);
+}
+// this rank's count of finished collectives for output tile `tile`
+__device__ __forceinline__ uint32_t* tile_count_of(const Params& p, int tile) {
+  return reinterpret_cast<uint32_t*>(p.heaps[p.rank] + p.ctrl_off + kCtrlCountersOffset) + tile;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
 }
 // Bounded wait for a flag another GPU writes; false on timeout.
 __device__ bool wait_peer_flag(const uint32_t* f, uint32_t want) {
@@ -363,32 +373,34 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const int row = q * 32 + lane;
     auto n_of = [&](int tile) { return tile * BM + row; };
-    // ---- fused collective: this call's sequence number, pushes and tile completion
-    const uint32_t cj = COLL ? *reinterpret_cast<volatile uint32_t*>(ctrl_of(p, p.rank)) + 1u : 0u;
-    const uint32_t cpar = cj & 1u;
+    // ---- fused collective: pushes of a finished tile and its completion
     volatile int* coll_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
-    auto push = [&](int m, int n, float v) {  // this rank's value of output (m, n) to every rank
+    auto tile_count = [&](int tile) { return *reinterpret_cast<volatile uint32_t*>(tile_count_of(p, tile)) + 1u; };
+    auto push = [&](uint32_t jt, int tile, int m, int n, float v) {  // value of output (m, n) to every rank
       const size_t o = p.coll == COLL_ALLREDUCE
-                           ? p.dst_off + sizeof(float) * ((((size_t)cpar * p.world + p.rank) * p.M + m) * (size_t)p.N + n)
+                           ? p.dst_off + sizeof(float) * (((((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world + p.rank) *
+                                                               p.recv_rows + m) * BM + (n - tile * BM))
                            : p.dst_off + sizeof(float) * ((size_t)m * p.ldy + p.col_off + n);
       for (int d = 0; d < p.world; ++d) *reinterpret_cast<float*>(p.heaps[d] + o) = v;
     };
-    auto coll_finish = [&](int tile) {
-      // the barrier orders every epilogue thread's pushes before thread 64's
-      // system-scope release stores of the flags (release is cumulative)
+    auto coll_finish = [&](uint32_t jt, int tile) {
+      // the barrier puts every epilogue thread's pushes before thread 64's
+      // system-scope fence and flag stores (cumulativity)
       epi_bar();
-      if (threadIdx.x == 64)
-        for (int d = 0; d < p.world; ++d) st_release_sys(flag_of(p, d, cpar, p.rank, tile), cj);
-      if (p.coll != COLL_ALLREDUCE) return;
-      if (warp == 2) {  // lane s waits for source rank s
+      if (threadIdx.x == 64) {
+        fence_acq_rel_sys();
+        for (int d = 0; d < p.world; ++d) st_relaxed_sys(flag_of(p, d, p.rank, tile), jt);
+      }
+      if (warp == 2) {  // lane s waits for source rank s's delivery of this tile
         bool ok = true;
-        if (lane < p.world) {
-          ok = wait_peer_flag(flag_of(p, p.rank, cpar, lane, tile), cj);
+        if (lane < p.world && lane != p.rank) {
+          ok = wait_peer_flag(flag_of(p, p.rank, lane, tile), jt);
           fence_acq_rel_sys();
         }
         ok = __all_sync(0xffffffffu, ok);
         if (lane == 0) {
           *coll_ok = ok ? 1 : 0;
+          *tile_count_of(p, tile) = jt;
           if (!ok) {
             atomicExch(p.err, 5u);
             atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
@@ -396,18 +408,19 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         }
       }
       epi_bar();
-      if (!*coll_ok || n_of(tile) >= p.N) return;
-      const int n = n_of(tile);
-      const float* recv = reinterpret_cast<const float*>(p.heaps[p.rank] + p.dst_off) +
-                          (size_t)cpar * p.world * p.M * p.N;
+      const int n = tile * BM + row;
+      if (p.coll != COLL_ALLREDUCE || !*coll_ok || n >= p.N) return;
+      // fold the ranks' partial tiles in rank order: identical sums on every rank
+      const float* slot = reinterpret_cast<const float*>(p.heaps[p.rank] + p.dst_off) +
+                          (((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world) * p.recv_rows * BM + row;
       for (int m = 0; m < p.M; ++m) {
         float v[kMaxTP];
 #pragma unroll
-        for (int r = 0; r < kMaxTP; ++r) v[r] = r < p.world ? __ldcg(recv + ((size_t)r * p.M + m) * p.N + n) : 0.f;
+        for (int r = 0; r < kMaxTP; ++r) v[r] = r < p.world ? __ldcg(slot + ((size_t)r * p.recv_rows + m) * BM) : 0.f;
         float sum = 0.f;
 #pragma unroll
         for (int r = 0; r < kMaxTP; ++r)
-          if (r < p.world) sum += v[r];  // rank order: identical on every rank
+          if (r < p.world) sum += v[r];
         epilogue_store<bf16>(SSD_EPI_RESIDUAL, p.y, p.N, m, n, sum, 0.f);
       }
     };
@@ -420,7 +433,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         float acc = 0.f;
         for (int k0 = lane * 8; k0 < p.K; k0 += 32 * 8) {
           float f[8];
-          unpack8(ldg_nc_v4(xr + k0), f);
+          unpack8(ld_act_v4(xr + k0), f);
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
         }
@@ -449,6 +462,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * MP);
       const int n = tile * BM + row;
       const bool whole = (kb_begin == 0 && kb_end == p.KB);
+      const uint32_t jt_whole = (COLL && whole) ? tile_count(tile) : 0u;
       float* mine = p.part + ((size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.M) * BM;
 #pragma unroll 1
       for (int c0 = 0; c0 < MP; c0 += 16) {
@@ -464,7 +478,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           if (m >= p.M) continue;
           if (whole) {
             if constexpr (COLL) {
-              if (n < p.N) push(m, n, v[j]);
+              if (n < p.N) push(jt_whole, tile, m, n, v[j]);
             } else if (n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
               epilogue_store<bf16>(p.epi, p.y, p.N, m, n, v[j], up);
             }
@@ -476,7 +490,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       tc_fence_before();
       mbar_arrive(acce(buf));
       if (whole) {
-        if constexpr (COLL) coll_finish(tile);
+        if constexpr (COLL) coll_finish(jt_whole, tile);
         continue;
       }
       // ---- split tile: ticket, then the last contributor folds all partials in K order.
@@ -497,6 +511,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       const bool last = *last_flag != 0;
       epi_bar();  // everyone has read the flag before the next tile may rewrite it
       if (!last) continue;
+      const uint32_t jt = COLL ? tile_count(tile) : 0u;
       // Fold the contributors in CTA (= K) order.  Rows are taken 16 at a time and
       // contributors 4 at a time so up to 64 independent L2 loads are in flight
       // per thread; the summation order per output stays c_first .. c_last.
@@ -525,13 +540,13 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           if (p.rowscale && i < mn) s[i] = __fmul_rn(s[i], inv_s[m0 + i]);
           const float up = __shfl_down_sync(0xffffffffu, s[i], 1);
           if constexpr (COLL) {
-            if (i < mn && n < p.N) push(m0 + i, n, s[i]);
+            if (i < mn && n < p.N) push(jt, tile, m0 + i, n, s[i]);
           } else if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
             epilogue_store<bf16>(p.epi, p.y, p.N, m0 + i, n, s[i], up);
           }
         }
       }
-      if constexpr (COLL) coll_finish(tile);
+      if constexpr (COLL) coll_finish(jt, tile);
     }
   }
 
@@ -540,54 +555,6 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
-  }
-  if constexpr (COLL) {
-    // The last CTA to leave (all-gather: after every peer's tiles have arrived)
-    // publishes the sequence number for the next collective.
-    uint32_t* ctrl = ctrl_of(p, p.rank);
-    volatile uint32_t* sm_last = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
-    volatile uint32_t* sm_cj = reinterpret_cast<volatile uint32_t*>(tmem_slot + 3);
-    if (threadIdx.x == 0) {
-      *sm_cj = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1u;
-      __threadfence();
-      *sm_last = atomicAdd(ctrl + 1, 1u) == gridDim.x - 1 ? 1u : 0u;
-    }
-    __syncthreads();
-    if (*sm_last) {
-      const uint32_t cj = *sm_cj;
-      bool ok = true;
-      if (p.coll == COLL_ALLGATHER) {
-        const int tiles = (p.N + BM - 1) / BM;
-        const uint64_t t0 = global_ns();
-        for (uint32_t it = 0;; ++it) {
-          bool all = true;
-          for (int i = threadIdx.x; i < p.world * tiles; i += blockDim.x) {
-            const int src = i / tiles;
-            if (src != p.rank && ld_relaxed_sys(flag_of(p, p.rank, cj & 1u, src, i - src * tiles)) != cj) all = false;
-          }
-          if (__syncthreads_and(all)) break;
-          // one thread decides the timeout so that every thread leaves the loop together
-          const bool expired = threadIdx.x == 0 && (it >= kPeerWaitPolls || global_ns() - t0 > kPeerWaitNs);
-          if (__syncthreads_or(expired)) {
-            ok = false;
-            break;
-          }
-          __nanosleep(64);
-        }
-        fence_acq_rel_sys();
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        if (!ok) {
-          atomicExch(p.err, 5u);
-          atomicExch(ctrl + 2, (unsigned int)SSD_ERR_TIMEOUT);
-        }
-        ctrl[1] = 0u;
-        __threadfence();
-        *reinterpret_cast<volatile uint32_t*>(ctrl) = cj;
-        __threadfence();
-      }
-    }
   }
 }
 
@@ -705,6 +672,8 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
     for (int r = 0; r < kMaxTP; ++r) p.heaps[r] = r < ca->world ? ca->heaps[r] : nullptr;
     p.ctrl_off = ca->ctrl_off;
     p.dst_off = ca->dst_off;
+    p.recv_rows = ca->recv_rows;
+    p.recv_tiles = ca->recv_tiles;
   }
   auto kern = p.coll != COLL_NONE ? linear_tc_kernel<MP, true> : linear_tc_kernel<MP, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)

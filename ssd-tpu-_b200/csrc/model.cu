@@ -21,7 +21,7 @@ namespace ssd {
 namespace {
 
 template <typename T>
-__global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __restrict__ E, T* __restrict__ x, int d,
+__global__ void embed_kernel(const int32_t* tokens, const T* E, T* x, int d,
                              int vocab, float scale) {
   pdl_wait();
   pdl_trigger();
@@ -35,7 +35,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const T* __rest
 // One CTA per row.  bf16 rows with d % 8 == 0 are read once as 16-byte vectors
 // kept in registers (d <= 8 * 256 * 4); other shapes take the scalar loop.
 template <typename T>
-__global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int d, float eps) {
+__global__ void rmsnorm_kernel(const T* x, const T* w, T* y, int d, float eps) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
@@ -53,8 +53,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
     y[(int64_t)m * d + i] = from_f<T>(__fmul_rn(__fmul_rn(to_f(xr[i]), inv), __fadd_rn(1.0f, to_f(w[i]))));
 }
 
-__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                              bf16* __restrict__ y, int d, float eps) {
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* x, const bf16* w,
+                                                              bf16* y, int d, float eps) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
@@ -97,9 +97,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __res
 }
 
 // positions[b*T+t] = seq_lens_before[b] + t for t < q_lens[b], else -1; seq_after[b].
-__global__ void positions_kernel(const int32_t* __restrict__ slb, const int32_t* __restrict__ ql, int B, int T,
-                                 int32_t* __restrict__ pos, int32_t* __restrict__ seq_after,
-                                 int32_t* __restrict__ qlen_out) {
+__global__ void positions_kernel(const int32_t* slb, const int32_t* ql, int B, int T,
+                                 int32_t* pos, int32_t* seq_after,
+                                 int32_t* qlen_out) {
   pdl_wait();
   pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * T; i += gridDim.x * blockDim.x) {
@@ -115,8 +115,8 @@ __global__ void positions_kernel(const int32_t* __restrict__ slb, const int32_t*
 
 // rows[b] = h[b*T + q_lens[b]-1]  (last valid token per sequence)
 template <typename T>
-__global__ void gather_last_kernel(const T* __restrict__ h, const int32_t* __restrict__ qlen, int tq, int d,
-                                   T* __restrict__ out) {
+__global__ void gather_last_kernel(const T* h, const int32_t* qlen, int tq, int d,
+                                   T* out) {
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x;

@@ -10,10 +10,10 @@
 namespace ssd {
 namespace {
 
-__global__ void spec_lookup_kernel(const int32_t* __restrict__ keys, const uint8_t* __restrict__ valid, int N,
-                                   const int32_t* __restrict__ req, int B, const int32_t* __restrict__ tokens, int K,
-                                   uint8_t* __restrict__ hit, int32_t* __restrict__ idx,
-                                   int32_t* __restrict__ out_tokens) {
+__global__ void spec_lookup_kernel(const int32_t* keys, const uint8_t* valid, int N,
+                                   const int32_t* req, int B, const int32_t* tokens, int K,
+                                   uint8_t* hit, int32_t* idx,
+                                   int32_t* out_tokens) {
   pdl_wait();
   pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -32,8 +32,8 @@ __global__ void spec_lookup_kernel(const int32_t* __restrict__ keys, const uint8
   for (int j = lane; j < K; j += 32) out_tokens[(int64_t)warp * K + j] = h ? tokens[(int64_t)best * K + j] : 0;
 }
 
-__global__ void spec_gather_logits_kernel(const float* __restrict__ logits, int64_t row, const int32_t* __restrict__ idx,
-                                          int B, float* __restrict__ out) {
+__global__ void spec_gather_logits_kernel(const float* logits, int64_t row, const int32_t* idx,
+                                          int B, float* out) {
   pdl_wait();
   pdl_trigger();
   const int64_t total = (int64_t)B * row;

@@ -40,7 +40,7 @@ __device__ __forceinline__ void chunk_bounds(int V, int nchunks, int c, int& lo,
 }
 
 // Thread-local first-occurrence argmax over x[lo:hi).
-__device__ __forceinline__ void scan_argmax(const float* __restrict__ row, int lo, int hi, bool vec_ok,
+__device__ __forceinline__ void scan_argmax(const float* row, int lo, int hi, bool vec_ok,
                                             float& best, int& bidx) {
   best = -INFINITY;
   bidx = 0x7fffffff;
@@ -51,7 +51,7 @@ __device__ __forceinline__ void scan_argmax(const float* __restrict__ row, int l
     for (; i + 3 * kScanThreads < nv; i += 4 * kScanThreads) {
       float4 a[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] = __ldg(p + i + u * kScanThreads);
+      for (int u = 0; u < 4; ++u) a[u] = __ldcg(p + i + u * kScanThreads);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int base = lo + 4 * (i + u * kScanThreads);
@@ -62,7 +62,7 @@ __device__ __forceinline__ void scan_argmax(const float* __restrict__ row, int l
       }
     }
     for (; i < nv; i += kScanThreads) {
-      float4 a = __ldg(p + i);
+      float4 a = __ldcg(p + i);
       const int base = lo + 4 * i;
       if (a.x > best) { best = a.x; bidx = base; }
       if (a.y > best) { best = a.y; bidx = base + 1; }
@@ -70,12 +70,12 @@ __device__ __forceinline__ void scan_argmax(const float* __restrict__ row, int l
       if (a.w > best) { best = a.w; bidx = base + 3; }
     }
     for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) {
-      float v = __ldg(row + j);
+      float v = __ldcg(row + j);
       if (v > best) { best = v; bidx = j; }
     }
   } else {
     for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
-      float v = __ldg(row + j);
+      float v = __ldcg(row + j);
       if (v > best) { best = v; bidx = j; }
     }
   }
@@ -90,12 +90,12 @@ __device__ __forceinline__ unsigned long long thread_key(float best, int bidx) {
 // grid (nchunks, rows); rows = B*(K+1) (verify) or rows (argmax_rows, K = 0).
 // group = b for verify (all K+1 rows), row for argmax_rows.
 __global__ void __launch_bounds__(kScanThreads)
-greedy_scan_kernel(const float* __restrict__ x, int64_t ld, int V, int kp1, int nchunks,
-                   bool vec_ok, unsigned int* __restrict__ counters,
-                   unsigned long long* __restrict__ partial, const int32_t* __restrict__ spec,
-                   int32_t* __restrict__ accept_until, int32_t* __restrict__ recovery,
-                   uint8_t* __restrict__ mask, int32_t* __restrict__ target_tokens,
-                   int32_t* __restrict__ argmax_out) {
+greedy_scan_kernel(const float* x, int64_t ld, int V, int kp1, int nchunks,
+                   bool vec_ok, unsigned int* counters,
+                   unsigned long long* partial, const int32_t* spec,
+                   int32_t* accept_until, int32_t* recovery,
+                   uint8_t* mask, int32_t* target_tokens,
+                   int32_t* argmax_out) {
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
   __shared__ int tt[64];
@@ -163,11 +163,11 @@ __device__ __forceinline__ float prob_of(float logit, float temp, float m, float
 // then (last CTA per sequence) the accept loop.  Rows per sequence: nP target
 // rows (lp[off .. K]) followed by K draft rows (lq[0 .. K-1]).
 __global__ void __launch_bounds__(kScanThreads)
-sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, int K, int V,
+sample_stats_kernel(const float* lp, const float* lq, int K, int V,
                     int off, int nchunks, bool vec_ok, float tp, float tq,
-                    unsigned int* __restrict__ counters, float2* __restrict__ part,
-                    const int32_t* __restrict__ spec, const float* __restrict__ u_accept,
-                    SampleDecision* __restrict__ dec) {
+                    unsigned int* counters, float2* part,
+                    const int32_t* spec, const float* u_accept,
+                    SampleDecision* dec) {
   __shared__ float redf[32];
   __shared__ bool is_last;
   __shared__ float2 stats[130];
@@ -191,12 +191,12 @@ sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, 
     const int nv = (hi - lo) >> 2;
     const float4* p = reinterpret_cast<const float4*>(row + lo);
     for (int i = threadIdx.x; i < nv; i += kScanThreads) {
-      float4 a = __ldg(p + i);
+      float4 a = __ldcg(p + i);
       push(a.x); push(a.y); push(a.z); push(a.w);
     }
-    for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) push(__ldg(row + j));
+    for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) push(__ldcg(row + j));
   } else {
-    for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) push(__ldg(row + j));
+    for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) push(__ldcg(row + j));
   }
   const float M = block_reduce(m, redf, OpMax());
   float sc = (m == -INFINITY) ? 0.f : s * expf(__fsub_rn(m, M));
@@ -226,8 +226,8 @@ sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, 
     const int tok = spec[(int64_t)b * (K + 1) + j + 1];
     const float2 pst = stats[j];  // target row j+off is stored at index j
     const float2 qst = stats[nP + j];
-    const float pv = prob_of(__ldg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok), tp, pst.x, pst.y);
-    const float qv = prob_of(__ldg(lq + ((int64_t)b * K + j) * V + tok), tq, qst.x, qst.y);
+    const float pv = prob_of(__ldcg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok), tp, pst.x, pst.y);
+    const float qv = prob_of(__ldcg(lq + ((int64_t)b * K + j) * V + tok), tq, qst.x, qst.y);
     const float ratio = fminf(1.0f, __fdiv_rn(pv, fmaxf(qv, 1e-12f)));
     if (u_accept[(int64_t)b * K + j] < ratio) ++acc; else break;
   }
@@ -246,9 +246,9 @@ sample_stats_kernel(const float* __restrict__ lp, const float* __restrict__ lq, 
 
 // Pass 2: residual mass sum_v max(p_v - x q_v, 0) (skipped for bonus rows).
 __global__ void __launch_bounds__(kScanThreads)
-sample_residual_kernel(const float* __restrict__ lp, const float* __restrict__ lq, int K, int V,
-                       int nchunks, float tp, float tq, float sx, unsigned int* __restrict__ counters,
-                       float* __restrict__ part, SampleDecision* __restrict__ dec) {
+sample_residual_kernel(const float* lp, const float* lq, int K, int V,
+                       int nchunks, float tp, float tq, float sx, unsigned int* counters,
+                       float* part, SampleDecision* dec) {
   __shared__ float redf[32];
   __shared__ bool is_last;
   pdl_wait();
@@ -262,8 +262,8 @@ sample_residual_kernel(const float* __restrict__ lp, const float* __restrict__ l
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
   float s = 0.f;
   for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
-    const float p = prob_of(__ldg(prow + j), tp, d.mp, d.sp);
-    const float q = prob_of(__ldg(qrow + j), tq, d.mq, d.sq);
+    const float p = prob_of(__ldcg(prow + j), tp, d.mp, d.sp);
+    const float q = prob_of(__ldcg(qrow + j), tq, d.mq, d.sq);
     s += fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f);
   }
   s = block_reduce(s, redf, OpSum());
@@ -278,11 +278,11 @@ sample_residual_kernel(const float* __restrict__ lp, const float* __restrict__ l
 
 // Pass 3: Gumbel-max categorical draw over log(r + 1e-12).
 __global__ void __launch_bounds__(kScanThreads)
-sample_draw_kernel(const float* __restrict__ lp, const float* __restrict__ lq,
-                   const float* __restrict__ u_gumbel, int K, int V, int nchunks, float tp, float tq,
-                   float sx, unsigned int* __restrict__ counters, unsigned long long* __restrict__ part,
-                   const SampleDecision* __restrict__ dec, int32_t* __restrict__ accept_until,
-                   int32_t* __restrict__ recovery, uint8_t* __restrict__ mask) {
+sample_draw_kernel(const float* lp, const float* lq,
+                   const float* u_gumbel, int K, int V, int nchunks, float tp, float tq,
+                   float sx, unsigned int* counters, unsigned long long* part,
+                   const SampleDecision* dec, int32_t* accept_until,
+                   int32_t* recovery, uint8_t* mask) {
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
   pdl_wait();
@@ -296,15 +296,15 @@ sample_draw_kernel(const float* __restrict__ lp, const float* __restrict__ lq,
   float best = -INFINITY;
   int bidx = 0x7fffffff;
   for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
-    const float p = prob_of(__ldg(prow + j), tp, d.mp, d.sp);
+    const float p = prob_of(__ldcg(prow + j), tp, d.mp, d.sp);
     float r;
     if (d.bonus) {
       r = p;
     } else {
-      const float q = prob_of(__ldg(qrow + j), tq, d.mq, d.sq);
+      const float q = prob_of(__ldcg(qrow + j), tq, d.mq, d.sq);
       r = __fdiv_rn(fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f), d.rsum);
     }
-    const float g = -logf(-logf(__ldg(urow + j)));
+    const float g = -logf(-logf(__ldcg(urow + j)));
     const float score = __fadd_rn(logf(__fadd_rn(r, 1e-12f)), g);
     if (score > best) { best = score; bidx = j; }
   }

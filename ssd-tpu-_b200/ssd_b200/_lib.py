@@ -75,7 +75,7 @@ class CommC(C.Structure):
 
     _fields_ = [
         ("rank", _i), ("world", _i), ("heaps", _p * SSD_MAX_TP), ("heap_bytes", _sz),
-        ("ctrl_offset", _sz), ("recv_offset", _sz), ("recv_bytes", _sz),
+        ("ctrl_offset", _sz), ("recv_offset", _sz), ("recv_bytes", _sz), ("recv_rows", _i), ("recv_tiles", _i),
     ]
 
 

@@ -91,6 +91,7 @@ class TPComm:
         c.ctrl_offset = 0
         c.recv_offset = self.ctrl_bytes
         c.recv_bytes = self.recv_bytes
+        c.recv_rows, c.recv_tiles = max_m, (max_n + 127) // 128
         self.cstruct = c
         self.max_m, self.max_n = max_m, max_n
 
@@ -110,8 +111,10 @@ class TPComm:
         """Word 2 of the control block: 0, or SSD_ERR_TIMEOUT after a peer wait gave up."""
         return int(self.heap[8:12].view(torch.int32).item())
 
-    def sequence(self) -> int:
-        return int(self.heap[0:4].view(torch.int32).item()) & 0xFFFFFFFF
+    def tile_counts(self, n: int = 8) -> list[int]:
+        """Collectives finished so far for output tiles 0..n-1 (device counters)."""
+        off = 256
+        return [int(v) & 0xFFFFFFFF for v in self.heap[off:off + 4 * n].view(torch.int32).tolist()]
 
     def close(self) -> None:
         L = lib()

@@ -228,7 +228,7 @@ def run_ours(args):
         target = shard_weights(GemmaWeights.random(st_, seed=1000), rank, world)
         draft = shard_weights(GemmaWeights.random(sd_, seed=2000), rank, world)
         torch.cuda.empty_cache()
-        comm = TPComm(heap_bytes=192 << 20, max_m=256, max_n=max(st_.d_model, sd_.d_model))
+        comm = TPComm(heap_bytes=192 << 20, max_m=64, max_n=max(st_.d_model, sd_.d_model))
         rng = np.random.default_rng(0)
     else:
         target = GemmaWeights.random(st_, seed=1000 + rank)

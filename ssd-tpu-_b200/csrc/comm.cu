@@ -88,8 +88,8 @@ extern "C" size_t ssd_comm_ctrl_bytes(void) { return align_up256(kCommCtrlBytes)
 
 extern "C" size_t ssd_comm_recv_bytes(int world, int max_m, int max_n) {
   if (world <= 0 || max_m <= 0 || max_n <= 0) return 0;
-  const size_t tiles = (size_t)(max_n + 127) / 128;  // slots [2][tiles][world][max_m][128] fp32
-  return align_up256(sizeof(float) * 2 * tiles * world * (size_t)max_m * 128);
+  const size_t tiles = (size_t)(max_n + 127) / 128;  // slots [2][tiles][world][max_m][128] of 64-bit words
+  return align_up256(sizeof(uint64_t) * 2 * tiles * world * (size_t)max_m * 128);
 }
 
 extern "C" int ssd_ipc_export(const void* ptr, void* handle, size_t* offset) {

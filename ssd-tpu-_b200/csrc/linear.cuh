@@ -77,7 +77,7 @@ struct CollArgs {
   size_t ctrl_off;      // control block offset (same on every rank)
   size_t dst_off;       // all-reduce: receive area; all-gather: the fp32 output [M, ldy]
   int ldy, col_off;     // all-gather: row pitch and first column of this rank's block
-  int recv_rows, recv_tiles;  // all-reduce: receive slots [2][recv_tiles][world][recv_rows][128] fp32
+  int recv_rows, recv_tiles;  // all-reduce: receive slots [2][recv_tiles][world][recv_rows][128] (fp32 | count << 32)
 };
 
 // mode ALLREDUCE: y[M,N] (bf16, residual in/out) += round(sum over ranks of x_r w_r^T)

@@ -24,17 +24,19 @@
 //
 // Tensor parallelism fuses the collective into the same kernel.  Every rank
 // maps every other rank's symmetric heap (CUDA IPC over NVLink); the rank that
-// finishes an output tile stores its fp32 values straight into the peers'
-// heaps (plain stores, no TMA, no multicast) and raises one arrival flag per
-// peer and tile, so tile i crosses NVLink while tile i+1 is still being
-// multiplied:
-//   * all-reduce (row-parallel O / down): the partial tiles land in a receive
-//     area [parity][source rank][M][N]; the tile's owner on every rank waits
-//     for all sources' flags and folds them in rank order (so every rank holds
-//     bit-identical sums), adds the residual and stores bf16;
+// finishes an output tile stores its values straight into the peers' heaps
+// (plain stores, no TMA, no multicast), so tile i crosses NVLink while tile i+1
+// is still being multiplied:
+//   * all-reduce (row-parallel O / down): each value travels as one 64-bit word
+//     (fp32 bits, delivery count) into a receive slot [parity][tile][source
+//     rank][row][128]; the tile's owner on every rank polls the words of all
+//     sources (data and tag arrive together: no flags, no fences), folds them
+//     in rank order (so every rank holds bit-identical sums), adds the residual
+//     and stores bf16;
 //   * all-gather (vocab-parallel LM head): the fp32 logits columns land in the
-//     same place of every rank's logits buffer; the kernel's last CTA waits for
-//     every peer's tiles, so the logits are complete when the kernel ends.
+//     same place of every rank's logits buffer, followed by one arrival flag
+//     per peer and tile; the tile's owner waits for the peers' flags of that
+//     tile, so the logits are complete when the kernel ends.
 // Each rank counts, per output tile, the collectives it has finished (device
 // memory, so CUDA-graph replays need no host state; every rank makes the same
 // calls, so the counts agree).  A delivery of tile t carries the count as its
@@ -151,6 +153,14 @@ __device__ __forceinline__ uint32_t* tile_count_of(const Params& p, int tile) {
 }
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* a, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* a, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* a) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
 }
 // Bounded wait for a flag another GPU writes; false on timeout.
 __device__ bool wait_peer_flag(const uint32_t* f, uint32_t want) {
@@ -374,18 +384,78 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     const int row = q * 32 + lane;
     auto n_of = [&](int tile) { return tile * BM + row; };
     // ---- fused collective: pushes of a finished tile and its completion
-    volatile int* coll_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
     auto tile_count = [&](int tile) { return *reinterpret_cast<volatile uint32_t*>(tile_count_of(p, tile)) + 1u; };
     auto push = [&](uint32_t jt, int tile, int m, int n, float v) {  // value of output (m, n) to every rank
-      const size_t o = p.coll == COLL_ALLREDUCE
-                           ? p.dst_off + sizeof(float) * (((((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world + p.rank) *
-                                                               p.recv_rows + m) * BM + (n - tile * BM))
-                           : p.dst_off + sizeof(float) * ((size_t)m * p.ldy + p.col_off + n);
-      for (int d = 0; d < p.world; ++d) *reinterpret_cast<float*>(p.heaps[d] + o) = v;
+      if (p.coll == COLL_ALLREDUCE) {
+        // one 64-bit word: fp32 bits | delivery count << 32 (single-copy atomic, so
+        // the receiver polls the data itself -- no flag, no fence)
+        const size_t o = p.dst_off + sizeof(uint64_t) * (((((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world +
+                                                           p.rank) * p.recv_rows + m) * BM + (n - tile * BM));
+        const uint64_t w = ((uint64_t)jt << 32) | __float_as_uint(v);
+        for (int d = 0; d < p.world; ++d) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(p.heaps[d] + o), w);
+      } else {
+        const size_t o = p.dst_off + sizeof(float) * ((size_t)m * p.ldy + p.col_off + n);
+        for (int d = 0; d < p.world; ++d) *reinterpret_cast<float*>(p.heaps[d] + o) = v;
+      }
     };
     auto coll_finish = [&](uint32_t jt, int tile) {
-      // the barrier puts every epilogue thread's pushes before thread 64's
-      // system-scope fence and flag stores (cumulativity)
+      const int n = tile * BM + row;
+      if (p.coll == COLL_ALLREDUCE) {
+        // every thread polls its own (m, row) words of all sources -- the words it
+        // pushed itself included, so no barrier orders the CTA's pushes -- and
+        // folds them in rank order: bit-identical sums on every rank
+        if (n < p.N) {
+          const uint64_t* slot = reinterpret_cast<const uint64_t*>(p.heaps[p.rank] + p.dst_off) +
+                                 (((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world) * p.recv_rows * BM + row;
+          bool ok = true;
+          for (int m0 = 0; m0 < p.M; m0 += 4) {
+            uint64_t w[4][kMaxTP];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int r = 0; r < kMaxTP; ++r)
+                w[i][r] = (m0 + i < p.M && r < p.world)
+                              ? ld_relaxed_sys_u64(slot + ((size_t)r * p.recv_rows + m0 + i) * BM)
+                              : ((uint64_t)jt << 32);
+            for (uint32_t it = 0;; ++it) {  // late words: poll again (bounded)
+              bool all = true;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int r = 0; r < kMaxTP; ++r)
+                  if ((uint32_t)(w[i][r] >> 32) != jt) {
+                    all = false;
+                    w[i][r] = ld_relaxed_sys_u64(slot + ((size_t)r * p.recv_rows + m0 + i) * BM);
+                  }
+              if (all) break;
+              if (it >= kPeerWaitPolls) {
+                ok = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (m0 + i >= p.M) break;
+              float sum = 0.f;
+#pragma unroll
+              for (int r = 0; r < kMaxTP; ++r)
+                if (r < p.world) sum += __uint_as_float((uint32_t)w[i][r]);
+              epilogue_store<bf16>(SSD_EPI_RESIDUAL, p.y, p.N, m0 + i, n, sum, 0.f);
+            }
+            if (!ok) break;
+          }
+          if (!ok) {
+            atomicExch(p.err, 5u);
+            atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
+          }
+        }
+        epi_bar();  // every thread has read the tile count before it advances
+        if (threadIdx.x == 64) *tile_count_of(p, tile) = jt;
+        return;
+      }
+      // all-gather: the barrier puts every epilogue thread's pushes before thread
+      // 64's system-scope fence and flag stores (cumulativity)
       epi_bar();
       if (threadIdx.x == 64) {
         fence_acq_rel_sys();
@@ -399,29 +469,12 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         }
         ok = __all_sync(0xffffffffu, ok);
         if (lane == 0) {
-          *coll_ok = ok ? 1 : 0;
           *tile_count_of(p, tile) = jt;
           if (!ok) {
             atomicExch(p.err, 5u);
             atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
           }
         }
-      }
-      epi_bar();
-      const int n = tile * BM + row;
-      if (p.coll != COLL_ALLREDUCE || !*coll_ok || n >= p.N) return;
-      // fold the ranks' partial tiles in rank order: identical sums on every rank
-      const float* slot = reinterpret_cast<const float*>(p.heaps[p.rank] + p.dst_off) +
-                          (((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world) * p.recv_rows * BM + row;
-      for (int m = 0; m < p.M; ++m) {
-        float v[kMaxTP];
-#pragma unroll
-        for (int r = 0; r < kMaxTP; ++r) v[r] = r < p.world ? __ldcg(slot + ((size_t)r * p.recv_rows + m) * BM) : 0.f;
-        float sum = 0.f;
-#pragma unroll
-        for (int r = 0; r < kMaxTP; ++r)
-          if (r < p.world) sum += v[r];
-        epilogue_store<bf16>(SSD_EPI_RESIDUAL, p.y, p.N, m, n, sum, 0.f);
       }
     };
     if (p.rowscale) {

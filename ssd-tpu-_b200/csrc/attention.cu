@@ -26,7 +26,11 @@
 // every reduction of a row runs in a fixed order, and fully masked warps or
 // splits contribute exact zeros, so a query's output does not depend on T or
 // on the other rows -- a k+1-token verify reproduces one-token decodes bit for bit.
+#include <mutex>
+#include <unordered_map>
+
 #include "common.cuh"
+#include "linear.cuh"
 
 namespace ssd {
 namespace {
@@ -81,15 +85,15 @@ struct RowInfo {
 // w_s = exp(m_s - M) and the normaliser L are computed once per row by one warp
 // (lane-strided over splits, xor-tree sums: an empty split's exact zeros leave
 // them unchanged), then every output element sums w_s * o_s in split order.
-template <typename KV, int D>
+template <typename KV, int D, int CHUNK = kChunk, int NTHREADS = kAttnThreads>
 __device__ __forceinline__ void attention_fold(const float* ws_o, const float2* ws_ml,
                                                KV* out, int64_t grp_id, int nsplit, int seq_len,
                                                int nrows, int row0, int G, int T, int hq, int kvh, int b,
                                                float* wsm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ns = max(1, min(nsplit, (seq_len + kChunk - 1) / kChunk));
+  const int ns = max(1, min(nsplit, (seq_len + CHUNK - 1) / CHUNK));
   __shared__ float inv_l[kRows];
-  for (int r = warp; r < nrows; r += kWarpsA) {
+  for (int r = warp; r < nrows; r += NTHREADS / 32) {
     const int64_t rb = grp_id * nsplit * kRows + r;
     float mloc = -INFINITY;
     for (int s = lane; s < ns; s += 32) mloc = fmaxf(mloc, __ldcg(&ws_ml[rb + (int64_t)s * kRows]).x);
@@ -105,7 +109,7 @@ __device__ __forceinline__ void attention_fold(const float* ws_o, const float2* 
     if (lane == 0) inv_l[r] = L;
   }
   __syncthreads();
-  for (int i = tid; i < nrows * D; i += kAttnThreads) {
+  for (int i = tid; i < nrows * D; i += NTHREADS) {
     const int r = i / D, d = i % D;
     const int64_t rb = grp_id * nsplit * kRows + r;
     const float* wr = wsm + r * 256;
@@ -583,6 +587,344 @@ paged_attention_tc_kernel(const bf16* q, const bf16* pages, int num_layers,
   attention_fold<bf16, D>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq, kvh, b, os);
 }
 
+// ---------------------------------------------------------------- K1, bf16, TMA-pipelined
+// The verify/decode attention for bf16 pages of 16 rows.  A CTA owns one
+// (sequence, KV head, row group) and a fixed 256-position split (16 pages):
+//   * warp 0 (one lane) is the producer: it reads the page table and streams
+//     each page's K and V rows into a ring of shared-memory stages with TMA
+//     (a 5-D tensor map over the cache, box = 16 rows x 64 dims, 128-byte
+//     swizzle, no multicast), one mbarrier per stage;
+//   * warps 1-4 are consumers: consumer c takes pages c, c+4, c+8, c+12 and
+//     keeps an online-softmax state per query row (running max, sum and the
+//     16 x D accumulator in registers) across its pages: S = Q K^T and O += P V
+//     with mma.sync m16n8k16 (bf16 in, fp32 accumulate), fragments via
+//     ldmatrix from the swizzled stages;
+//   * the four consumers' states are combined in warp order; a group whose
+//     context fits one split writes its output directly, otherwise the split
+//     writes a partial and the group's last split folds them in split order.
+// Rows of a page past the end of the context are zeroed in the stage before
+// P.V (masked probabilities are exact zeros, stale rows must not be NaN).
+// 160 threads and ~106 KB of shared memory: two CTAs per SM, up to 12 pages
+// (192 KB) of K/V in flight per SM.  Batch invariance as for the other
+// kernels: splits, page ownership and every reduction order are fixed.
+constexpr int kTmaChunk = 256;                  // positions per split
+constexpr int kTmaPage = 16;                    // rows per page (TMA box height)
+constexpr int kTmaConsumers = 4;
+constexpr int kTmaThreads = 32 * (1 + kTmaConsumers);
+constexpr uint32_t kTmaWaitLimit = 1u << 24;
+
+__device__ __forceinline__ void tmb_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void tmb_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tmb_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool tmb_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait; false after kTmaWaitLimit polls (the caller records the error and stops)
+__device__ __forceinline__ bool tmb_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kTmaWaitLimit; ++i)
+    if (tmb_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+      "[%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+template <int D>
+struct TmaSmem {
+  static constexpr int CHUNKS = D / 64;                          // 128-byte swizzle rows per page row
+  static constexpr uint32_t PLANE = kTmaPage * D * 2;            // K (or V) of one page: 16 x D bf16
+  static constexpr uint32_t STAGE = 2 * PLANE;
+  static constexpr int STAGES = D == 256 ? 6 : D == 128 ? 12 : 16;
+  static constexpr int QST = D + 8;                              // padded Q rows (ldmatrix conflict-free)
+  static constexpr size_t ring = (size_t)STAGES * STAGE;
+  static constexpr size_t q_off = ring;
+  static constexpr size_t q_bytes = 2ull * 16 * QST;
+  static constexpr size_t bar_off = q_off + q_bytes;
+  static constexpr size_t ml_off = bar_off + 8 * 2 * STAGES + 16;
+  static constexpr size_t total = 1024 + ml_off + sizeof(float2) * kTmaConsumers * kRows;
+  static constexpr size_t o_bytes = sizeof(float) * kTmaConsumers * kRows * D;   // aliases the ring
+  static_assert(o_bytes <= ring, "consumer outputs must fit in the ring");
+};
+
+// byte offset of (row, dim) inside one page plane laid out as [chunk][row][128 B], 128-byte swizzle
+__device__ __forceinline__ uint32_t sw_off(int row, int dim) {
+  const int c = dim >> 6, u = (dim >> 3) & 7;
+  return (uint32_t)(c * (kTmaPage * 128) + row * 128 + ((u ^ (row & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTmaThreads, 2)
+paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16* q, int num_layers, int num_blocks,
+                           int hkv, int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
+                           const int32_t* q_lens, bf16* out, float scale, int T, int hq, int row_groups, int nsplit,
+                           float* ws_o, float2* ws_ml, unsigned int* counters, unsigned int* err) {
+  using S = TmaSmem<D>;
+  constexpr int KSTEPS = D / 16;
+  constexpr int NT = D / 8;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* gb = smem_raw + (base - raw);
+  bf16* qs = reinterpret_cast<bf16*>(gb + S::q_off);
+  float* os = reinterpret_cast<float*>(gb);                        // [consumer][kRows][D], after the ring is done
+  float2* mls = reinterpret_cast<float2*>(gb + S::ml_off);
+  const uint32_t bars = base + (uint32_t)S::bar_off;
+  auto full = [&](int st) { return bars + 8u * st; };
+  auto empty = [&](int st) { return bars + 8u * (S::STAGES + st); };
+  __shared__ RowInfo ri;
+  __shared__ bool is_last;
+  __shared__ int s_abort;
+
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / row_groups, rg = blockIdx.y % row_groups;
+  const int b = blockIdx.z;
+  const int G = hq / hkv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    for (int st = 0; st < S::STAGES; ++st) {
+      tmb_init(full(st), 1);
+      tmb_init(empty(st), 1);
+    }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&kvmap) : "memory");
+  }
+  pdl_wait();
+  const int seq_len = ld_act(seq_lens + b);
+  const int ql = q_lens ? ld_act(q_lens + b) : T;
+  const int total_rows = G * T;
+  const int row0 = rg * kRows;
+  if (tid == 0) {
+    ri.nrows = min(kRows, total_rows - row0);
+    for (int r = 0; r < kRows; ++r) {
+      const int gr = row0 + r;
+      const int t = gr / G;
+      ri.pos[r] = (r < ri.nrows && t < ql) ? seq_len - ql + t : -1;
+    }
+  }
+  __syncthreads();
+  const int nrows = ri.nrows;
+  int kmax = 0;
+  for (int r = 0; r < nrows; ++r) kmax = max(kmax, ri.pos[r] + 1);
+  const int k_begin = split * kTmaChunk;
+  const int k_end = min(min(min(k_begin + kTmaChunk, kmax), seq_len), max_blocks * kTmaPage);
+  const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
+  const int ns = max(1, min(nsplit, (seq_len + kTmaChunk - 1) / kTmaChunk));
+  const int npages = k_end > k_begin ? (k_end - k_begin + kTmaPage - 1) / kTmaPage : 0;
+
+  int issued = 0;  // pages the producer lane has put in flight
+  __shared__ int s_blk[kTmaChunk / kTmaPage];
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // the split's page-table entries in one parallel load (not one L2 round trip per page)
+    if (lane < npages) {
+      int blk = ld_act(block_tables + (int64_t)b * max_blocks + (k_begin / kTmaPage + lane));
+      s_blk[lane] = ((unsigned)blk >= (unsigned)num_blocks) ? 0 : blk;
+    }
+    __syncwarp();
+    if (lane == 0 && npages > 0) {
+      for (int j = 0; j < npages; ++j, ++issued) {
+        const int st = j % S::STAGES;
+        if (j >= S::STAGES && !tmb_wait(empty(st), (uint32_t)((j / S::STAGES) - 1) & 1u)) {
+          s_abort = 1;
+          atomicExch(err, 1u);
+          break;
+        }
+        const int blk = s_blk[j];
+        const int kpage = layer * num_blocks + blk;                      // plane 0 (K)
+        const int vpage = (num_layers + layer) * num_blocks + blk;       // plane 1 (V)
+        const uint32_t dst = base + (uint32_t)st * S::STAGE;
+        tmb_expect_tx(full(st), S::STAGE);
+#pragma unroll
+        for (int c = 0; c < S::CHUNKS; ++c) {
+          tma_load_5d(dst + (uint32_t)c * (kTmaPage * 128), &kvmap, full(st), 0, c, kvh, 0, kpage);
+          tma_load_5d(dst + S::PLANE + (uint32_t)c * (kTmaPage * 128), &kvmap, full(st), 0, c, kvh, 0, vpage);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int c = warp - 1;
+    // Q rows (bf16, zero padding rows) -- consumers share this work
+    for (int i = tid - 32; i < 16 * (D / 8); i += 32 * kTmaConsumers) {
+      const int r = i / (D / 8), cc = i % (D / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < nrows && ri.pos[r] >= 0) {
+        const int gr = row0 + r, t = gr / G, g = gr % G;
+        v = ld_act_v4(q + (((int64_t)b * T + t) * hq + kvh * G + g) * D + cc * 8);
+      }
+      *reinterpret_cast<uint4*>(qs + r * S::QST + cc * 8) = v;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kTmaConsumers) : "memory");
+    const int rA = lane >> 2;
+    const int prow = (rA < nrows) ? ri.pos[rA] : -1;
+    float m_run = -INFINITY, l_run = 0.f;
+    float oacc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oacc[nt][e] = 0.f;
+    const uint32_t qaddr0 = (uint32_t)__cvta_generic_to_shared(qs);
+    const int lr = lane & 7, lm = lane >> 3;
+    for (int j = c; j < npages; j += kTmaConsumers) {
+      const int st = j % S::STAGES;
+      if (!tmb_wait(full(st), (uint32_t)(j / S::STAGES) & 1u)) {
+        s_abort = 1;
+        atomicExch(err, 2u);
+        break;
+      }
+      const uint32_t kbase = base + (uint32_t)st * S::STAGE, vbase = kbase + S::PLANE;
+      const int t0 = k_begin + j * kTmaPage;
+      const int valid = min(kTmaPage, k_end - t0);
+      if (valid < kTmaPage) {
+        // rows past the context: zero V (whole 128-byte lines, any swizzle)
+        unsigned char* vg = gb + ((size_t)st * S::STAGE + S::PLANE);
+        for (int i = lane; i < (kTmaPage - valid) * S::CHUNKS * 8; i += 32) {
+          const int r = valid + i / (S::CHUNKS * 8), rest = i % (S::CHUNKS * 8), ch = rest / 8, u = rest % 8;
+          *reinterpret_cast<uint4*>(vg + ch * (kTmaPage * 128) + r * 128 + u * 16) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      // S = Q K^T (2 n-tiles of 8 positions)
+      float sacc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
+#pragma unroll
+      for (int ks_ = 0; ks_ < KSTEPS; ++ks_) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldsm_x4(qaddr0 + (uint32_t)((lr + 8 * (lm & 1)) * S::QST + 16 * ks_ + 8 * (lm >> 1)) * 2, a0, a1, a2, a3);
+        ldsm_x4(kbase + sw_off(8 * (lm >> 1) + lr, 16 * ks_ + 8 * (lm & 1)), b0, b1, b2, b3);
+        mma_bf16_16816(sacc[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(sacc[1], a0, a1, a2, a3, b2, b3);
+      }
+      // online softmax of row rA over this page (4 lanes share a row)
+      float pa[2][2];
+      float mp = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = t0 + nt * 8 + (lane & 3) * 2 + e;
+          const bool ok = (key < k_end) && (key <= prow);
+          pa[nt][e] = ok ? sacc[nt][e] * scale : -INFINITY;
+          mp = fmaxf(mp, pa[nt][e]);
+        }
+      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 1));
+      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 2));
+      const float m_new = fmaxf(m_run, mp);
+      const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+      float lp = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float pv = (m_new == -INFINITY || pa[nt][e] == -INFINITY) ? 0.f : expf(pa[nt][e] - m_new);
+          pa[nt][e] = pv;
+          lp += pv;
+        }
+      lp += __shfl_xor_sync(0xffffffffu, lp, 1);
+      lp += __shfl_xor_sync(0xffffffffu, lp, 2);
+      l_run = l_run * alpha + lp;
+      m_run = m_new;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        oacc[nt][0] *= alpha;
+        oacc[nt][1] *= alpha;
+      }
+      const uint32_t pa0 = pack_bf16(pa[0][0], pa[0][1]), pa2 = pack_bf16(pa[1][0], pa[1][1]);
+      // O += P V
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + sw_off(8 * (lm & 1) + lr, 16 * np + 8 * (lm >> 1)), b0, b1, b2, b3);
+        mma_bf16_16816(oacc[2 * np], pa0, 0u, pa2, 0u, b0, b1);
+        mma_bf16_16816(oacc[2 * np + 1], pa0, 0u, pa2, 0u, b2, b3);
+      }
+      // stage free: generic writes (zeroing) before the next TMA fill of it
+      if (valid < kTmaPage) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) tmb_arrive(empty(st));
+    }
+    // this consumer's state -> shared memory (after every consumer is done with the ring)
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kTmaConsumers) : "memory");
+    if ((lane & 3) == 0 && rA < kRows) mls[c * kRows + rA] = make_float2(m_run, l_run);
+    float* ow = os + c * kRows * D;
+    if (rA < nrows) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        ow[rA * D + nt * 8 + (lane & 3) * 2] = oacc[nt][0];
+        ow[rA * D + nt * 8 + (lane & 3) * 2 + 1] = oacc[nt][1];
+      }
+    }
+  }
+  __syncthreads();
+  if (s_abort) {
+    // a bounded wait gave up (error recorded): let the copies still in flight land, then leave
+    if (tid == 0)
+      for (int j = max(0, issued - S::STAGES); j < issued; ++j) tmb_wait(full(j % S::STAGES), (uint32_t)(j / S::STAGES) & 1u);
+    return;
+  }
+
+  // ---- combine the consumers in warp order
+  const bool direct = (ns == 1);
+  if (direct && split != 0) {  // the group's context fits split 0, which writes the output
+    pdl_trigger();
+    return;
+  }
+  const int64_t pbase = (grp_id * nsplit + split) * kRows;
+  for (int i = tid; i < nrows * D; i += kTmaThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, mls[w * kRows + r].x);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kTmaConsumers; ++w) {
+        const float2 ml = mls[w * kRows + r];
+        const float wt = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
+        L += ml.y * wt;
+        O += os[(w * kRows + r) * D + d] * wt;
+      }
+    }
+    if (direct) {
+      // one split: the fold would weight it by exp(0) = 1, so this is its result exactly
+      const int gr = row0 + r, t = gr / G, g = gr % G;
+      out[(((int64_t)b * T + t) * hq + kvh * G + g) * D + d] = from_f<bf16>((L > 0.f) ? O / L : 0.f);
+    } else {
+      ws_o[(pbase + r) * D + d] = O;
+      if (d == 0) ws_ml[pbase + r] = make_float2(M, L);
+    }
+  }
+  pdl_trigger();
+  if (direct) return;
+  if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+  attention_fold<bf16, D, kTmaChunk, kTmaThreads>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T,
+                                                  hq, kvh, b, os);
+}
+
 // ---------------------------------------------------------------- K2
 template <typename KV>
 __global__ void kv_write_kernel(KV* pages, int num_layers, int num_blocks, int block_size, int hkv,
@@ -663,6 +1005,9 @@ struct AttnLayout {
   size_t groups, off_cnt, off_o, off_ml, total;
 };
 
+// Workspace: ticket counters, an error word, split partials.  Sized for the
+// 128-position splits of the CUDA-core / mma kernels, which covers the TMA
+// kernel's 256-position splits too.
 inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_len) {
   AttnLayout L;
   const int G = hq / hkv;
@@ -673,7 +1018,7 @@ inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_
   const size_t rows = groups * L.nsplit * kRows;
   L.groups = groups;
   L.off_cnt = 0;
-  L.off_o = kCounterBytes;
+  L.off_o = kCounterBytes + 256;  // error word at kCounterBytes
   L.off_ml = L.off_o + align256(sizeof(float) * rows * D);
   L.total = L.off_ml + align256(sizeof(float2) * rows);
   return L;
@@ -695,6 +1040,54 @@ int launch_attention_tc(cudaStream_t st, const void* q, const void* pages, int n
           seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups, L.nsplit,
           reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
           reinterpret_cast<unsigned int*>(w + L.off_cnt));
+  return SSD_OK;
+}
+
+bool kv_map_cached(CUtensorMap* out, const void* pages, int plane_pages, int hkv, int D) {
+  struct Key {
+    const void* p;
+    int n, h, d;
+    bool operator==(const Key& o) const { return p == o.p && n == o.n && h == o.h && d == o.d; }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.p) ^ ((size_t)k.n * 0x9E3779B97F4A7C15ull) ^ ((size_t)k.h << 20) ^ (size_t)k.d;
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  std::lock_guard<std::mutex> g(mu);
+  const Key key{pages, plane_pages, hkv, D};
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return true;
+  }
+  if (!make_kv_page_map(out, pages, plane_pages, kTmaPage, hkv, D)) return false;
+  if (cache.size() > 1024) cache.clear();
+  cache.emplace(key, *out);
+  return true;
+}
+
+template <int D>
+int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks, int hkv,
+                         int layer, const int32_t* tables, int max_blocks, const int32_t* seq_lens,
+                         const int32_t* q_lens, void* out, float scale, int B, int T, int hq, int max_seq_len,
+                         const AttnLayout& L, void* ws) {
+  using S = TmaSmem<D>;
+  CUtensorMap map;
+  if (!kv_map_cached(&map, pages, 2 * num_layers * num_blocks, hkv, D)) return SSD_ERR_LAUNCH;
+  auto kern = paged_attention_tma_kernel<D>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total) != cudaSuccess)
+    return SSD_ERR_LAUNCH;
+  char* w = reinterpret_cast<char*>(ws);
+  const int nsplit = (max_seq_len + kTmaChunk - 1) / kTmaChunk;  // <= L.nsplit: fits the workspace
+  dim3 grid(nsplit, hkv * L.row_groups, B);
+  SSD_PDL(kern, grid, kTmaThreads, S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
+          layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups,
+          nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
+          reinterpret_cast<unsigned int*>(w + L.off_cnt), reinterpret_cast<unsigned int*>(w + kCounterBytes));
+  SSD_CHECK_LAUNCH();
   return SSD_OK;
 }
 
@@ -757,6 +1150,16 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
                                  block_tables, max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, L,  \
                                  workspace)
   const bool aligned16 = !(reinterpret_cast<uintptr_t>(q) & 15) && !(reinterpret_cast<uintptr_t>(pages) & 15);
+#define SSD_ATTN_TMA(DD)                                                                                        \
+  return launch_attention_tma<DD>(st, q, pages, num_layers, num_blocks, num_kv_heads, layer, block_tables,      \
+                                  max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, max_seq_len, L,    \
+                                  workspace)
+  if (dtype == SSD_DTYPE_BF16 && aligned16 && block_size == kTmaPage && (int64_t)2 * num_layers * num_blocks < (1ll << 31)) {
+    if (head_dim == 256) SSD_ATTN_TMA(256);
+    if (head_dim == 128) SSD_ATTN_TMA(128);
+    if (head_dim == 64) SSD_ATTN_TMA(64);
+  }
+#undef SSD_ATTN_TMA
   if (dtype == SSD_DTYPE_BF16 && aligned16) {
     if (head_dim == 256) SSD_ATTN_TC(256);
     if (head_dim == 128) SSD_ATTN_TC(128);

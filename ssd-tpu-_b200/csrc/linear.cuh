@@ -1,5 +1,7 @@
 // Internal interface of the projection kernels (not part of the C ABI).
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace ssd {
@@ -56,6 +58,10 @@ size_t linear_tc_workspace(int M, int N, int K);
 int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
               size_t ws_bytes, int rowscale = 0, float eps = 0.f);
 bool linear_tc_supported(int M, int N, int K);
+
+// TMA map over a bf16 KV cache plane stack [plane_pages][block_size][hkv][D]: box = one
+// page of one head, 64 dims wide (128-byte swizzle); D % 64 == 0.
+bool make_kv_page_map(CUtensorMap* m, const void* pages, int plane_pages, int block_size, int hkv, int D);
 
 // ---- tensor-parallel collectives fused into the tcgen05 projection epilogue
 constexpr int kMaxTP = 8;

@@ -747,6 +747,20 @@ int launch_any(int M, A... a) {
 
 }  // namespace tc
 
+bool make_kv_page_map(CUtensorMap* m, const void* pages, int plane_pages, int block_size, int hkv, int D) {
+  // pages [plane_pages][block_size][hkv][D] bf16 viewed as 5-D (d % 64, d / 64, head, row, page):
+  // one box = 16 rows x 64 dims (128 B per row, 128-byte swizzle) of one head of one page
+  tc::EncodeFn fn = tc::encode_fn();
+  if (!fn || D % 64 || block_size > 256) return false;
+  cuuint64_t dims[5] = {64, (cuuint64_t)(D / 64), (cuuint64_t)hkv, (cuuint64_t)block_size, (cuuint64_t)plane_pages};
+  cuuint64_t strides[4] = {128, (cuuint64_t)D * 2, (cuuint64_t)hkv * D * 2, (cuuint64_t)block_size * hkv * D * 2};
+  cuuint32_t box[5] = {64, 1, 1, (cuuint32_t)block_size, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(pages), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool linear_tc_supported(int M, int N, int K) {
   return M >= 1 && M <= 256 && N >= 1 && K >= 64 && (K % 8) == 0 && (N + tc::BM - 1) / tc::BM <= kCounterCap &&
          tc::encode_fn() != nullptr;

@@ -25,10 +25,15 @@ def load_weights(model_path: str | None, *, use_toy: bool = False, seed: int = 0
                  device="cuda") -> GemmaWeights:
     name = model_path if model_path in PRESETS else default_preset(role, use_toy)
     dtype = torch.float32 if name.startswith("toy") else torch.bfloat16
-    key = (name, seed, str(device))
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    key = (name, seed, str(dev))
     w = _SHARED.get(key)
     if w is None:
-        w = GemmaWeights.random(PRESETS[name], seed=seed, dtype=dtype, device=device)
+        with torch.cuda.device(dev):  # the init kernels run on that GPU's current stream
+            w = GemmaWeights.random(PRESETS[name], seed=seed, dtype=dtype, device=dev)
+            torch.cuda.current_stream(dev).synchronize()
         _SHARED[key] = w
     return w
 

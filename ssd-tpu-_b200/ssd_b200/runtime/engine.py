@@ -52,12 +52,18 @@ class LLMEngine:
         self.draft: GemmaAdapter | None = None
         if config.mode != DecodeMode.AR:
             same = config.draft_model_path is not None and config.draft_model_path == config.target_model_path
+            async_draft = config.mode in (DecodeMode.SSD, DecodeMode.INSTANCE)
+            ddev = torch.device(config.draft_device) if (async_draft and config.draft_device) else \
+                torch.device("cuda", torch.cuda.current_device())
             self.draft_w = load_weights(config.draft_model_path, use_toy=config.use_toy_model,
-                                        seed=config.seed if same else config.seed + 1, role="draft")
+                                        seed=config.seed if same else config.seed + 1, role="draft", device=ddev)
         if config.mode in (DecodeMode.SSD, DecodeMode.INSTANCE):
-            self.draft = GemmaAdapter(self.draft_w, max_model_len=config.max_model_len, name="draft")
-            self.draft_worker = DraftWorker(config, self.draft)
-            self.draft_worker.start()
+            # the draft adapter and its worker live on the draft's GPU (its own GPU when
+            # config.draft_device names one); only token ids cross between the GPUs
+            with torch.cuda.device(self.draft_w.device):
+                self.draft = GemmaAdapter(self.draft_w, max_model_len=config.max_model_len, name="draft")
+                self.draft_worker = DraftWorker(config, self.draft)
+                self.draft_worker.start()
 
     # ------------------------------------------------------------ public
     def generate(self, prompts: list[list[int]], sampling: SamplingParams, *,

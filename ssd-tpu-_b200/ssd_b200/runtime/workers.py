@@ -53,7 +53,7 @@ class DraftWorker:
         dev = torch.device(self.model.dev)
         self._device = dev.index if dev.index is not None else torch.cuda.current_device()
         self.stream = torch.cuda.Stream(device=self._device)
-        with torch.cuda.stream(self.stream):
+        with torch.cuda.device(self._device), torch.cuda.stream(self.stream):
             self.cache = SpecCache.create(num_branches=max(1, self.config.mq_len), k=self.config.speculate_k,
                                           vocab=self.model.vocab_size, device=self.model.dev, with_logits=False)
         self.stream.synchronize()

@@ -141,3 +141,21 @@ def test_adapter_verify_commit_matches_prefill(cuda):
     c = GemmaAdapter(w, max_model_len=256)
     c.prefill(torch.tensor(prompt))
     torch.testing.assert_close(c.decode(r).logits[0], lg[0], rtol=0, atol=0)
+
+
+def test_ssd_draft_on_its_own_gpu(cuda):
+    """ssd mode with the draft model and its worker on a second GPU: same stream as AR."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from ssd_b200 import LLM, DecodeMode, SamplingParams, SSDConfig
+
+    prompt = list(range(7, 30))
+    sampling = SamplingParams(max_new_tokens=16)
+    ar = LLM.from_mode(DecodeMode.AR)
+    ref, _ = ar.generate([prompt], sampling)
+    ar.shutdown()
+    llm = LLM(SSDConfig(mode=DecodeMode.SSD, use_toy_model=True, draft_device="cuda:1"))
+    assert llm._engine.draft_w.device == torch.device("cuda", 1)
+    out, m = llm.generate([prompt], sampling)
+    llm.shutdown()
+    assert out[0] == ref[0] and m.total_tokens >= 16

@@ -60,6 +60,12 @@ def parse():
     ap.add_argument("--rows", "--m", dest="m", type=int, default=5)
     ap.add_argument("--cols", "--n", dest="n", type=int, default=49152)
     ap.add_argument("--depth", "--kdim", dest="kdim", type=int, default=3072)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="> 0: batched serving workload (B sequences, --k drafts, --temperature, contexts "
+                         "U[--ctx-min, --ctx-max]); prints its own JSON line instead of the decode-loop line")
+    ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--ctx-min", type=int, default=1024)
+    ap.add_argument("--ctx-max", type=int, default=8192)
     ap.add_argument("--attn", choices=["2a", "decode7b", "decode2b"], default="2a",
                     help="--op attention shape: op config 2a (B=8, ctx U[512,4096]) or one decode step")
     return ap.parse_args()
@@ -536,10 +542,112 @@ def run_op(args):
     print(json.dumps(line), flush=True)
 
 
+def run_batched(args):
+    """Batched serving (B sequences, k drafts, sampling): Gemma-7B target + Gemma-2B draft, random-init
+    bf16, contexts ~ U[ctx_min, ctx_max] stood in by seeded N(0, 1) K/V in both caches (a prefill of
+    ~150 K tokens would take minutes and is not what the step measures).  One step = k draft forwards
+    over B rows + one verify forward over B*(k+1) rows + rejection sampling + rollbacks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from ssd_b200.models.gemma import PRESETS, GemmaWeights
+    from ssd_b200.runtime.batched import BatchedSpeculativeDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    B, k = args.batch, args.k
+    st_, sd_ = PRESETS["gemma-7b"], PRESETS["gemma-2b"]
+    comm = None
+    if world > 1:
+        from ssd_b200.runtime.tensor_parallel import TPComm, shard_weights
+
+        target = shard_weights(GemmaWeights.random(st_, seed=1000, max_pos=args.ctx_max + 512), rank, world)
+        draft = shard_weights(GemmaWeights.random(sd_, seed=2000, max_pos=args.ctx_max + 512), rank, world)
+        torch.cuda.empty_cache()
+        comm = TPComm(heap_bytes=1 << 30, max_m=max(256, B * (k + 1)), max_n=max(st_.d_model, sd_.d_model))
+    else:
+        target = GemmaWeights.random(st_, seed=1000, max_pos=args.ctx_max + 512)
+        draft = GemmaWeights.random(sd_, seed=2000, max_pos=args.ctx_max + 512)
+    rng = np.random.default_rng(0)
+    ctx = [int(x) for x in rng.integers(args.ctx_min, args.ctx_max + 1, B)]
+    steps = args.warmup + args.steps
+    grow = (steps + 2) * (k + 1)
+    max_seq = args.ctx_max + grow + 16
+    blocks = sum((c + grow + 15) // 16 + 1 for c in ctx) + 2
+    dec = BatchedSpeculativeDecoder(target, draft, batch=B, k=k, max_seq_len=max_seq,
+                                    temperature=args.temperature, seed=7, comm=comm, num_blocks=blocks)
+    dec.start_synthetic(ctx, np.random.default_rng(1))
+    for _ in range(args.warmup):
+        dec.step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0.record(stream)
+    tokens = 0
+    verify_ms = []
+    ctx_sum = 0.0
+    for _ in range(args.steps):
+        ctx_sum += float(dec.t.n.sum())
+        new = dec.step()
+        tokens += sum(len(x) for x in new)
+        verify_ms.append(dec.last_verify_ms)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    hbm, kind = peaks()
+    lt, ld = target.shape, draft.shape
+    mean_ctx = ctx_sum / args.steps / B
+    w_t = lt.layer_weight_bytes() * lt.num_layers + (st_.vocab // world) * st_.d_model * 2
+    w_d = ld.layer_weight_bytes() * ld.num_layers + (sd_.vocab // world) * sd_.d_model * 2
+    kv_t = B * mean_ctx * lt.kv_bytes_per_token()
+    kv_d = B * mean_ctx * ld.kv_bytes_per_token()
+    step_bytes = w_t + kv_t + k * (w_d + kv_d)
+    step_s = ms / 1000.0 / args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": "batched sd tokens/s (Gemma-7B/2B, B sequences, k drafts, sampling)",
+            "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "n/a", "dtype": "bf16",
+            "data": "synthetic (random-init weights; contexts stood in by seeded N(0,1) K/V)",
+            "config": {"workload": f"batched serving B={B}, k={k}, T={args.temperature}, ctx U[{args.ctx_min}, "
+                                   f"{args.ctx_max}]", "parallelism": f"tp{world}", "top_p": None},
+            "tokens_per_step": tokens / args.steps, "accept_rate": None,
+            "verify_ms": statistics.mean(verify_ms),
+            "step_bytes_per_rank": step_bytes, "step_hbm_gbs": step_bytes / step_s / 1e9,
+            "step_roofline_frac": step_bytes / step_s / 1e9 / hbm, "peak_kind": kind,
+            "clocks": clk,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.op is not None:
         run_op(args)
+        return
+    if args.batch > 0 and args.impl == "ours":
+        run_batched(args)
         return
     if args.impl == "reference":
         run_reference(args)

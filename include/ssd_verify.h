@@ -98,6 +98,18 @@ int ssd_verify_greedy_noalloc(ssd_stream_t stream, const float* logits_p,
 int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, int32_t* out,
                     void* workspace, size_t workspace_bytes);
 
+/*
+ * Row-wise sample from softmax(x[r] / temperature) (temperature > 0), e.g. the
+ * draft token of sampled speculative decoding (the reference drafts greedily,
+ * jax_ssd/models/gemma_adapter.py:127; sampled drafting is what verify_sample,
+ * jax_ssd/algorithm/verify.py:68-120, assumes).  Gumbel-max: out[r] = argmax_j
+ * (x[r][j] / temperature - log(-log(u))), u from a counter hash at
+ * (seed, offset + r * V + j), so the draw is reproducible and no noise buffer
+ * is read.  rows <= 16384.  Uses the ssd_verify_greedy workspace sizing with B=rows, K=0.
+ */
+int ssd_sample_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, float temperature,
+                    uint64_t seed, uint64_t offset, int32_t* out, void* workspace, size_t workspace_bytes);
+
 /* Workspace bytes for ssd_verify_sample. */
 size_t ssd_verify_sample_workspace_size(int B, int K, int V);
 

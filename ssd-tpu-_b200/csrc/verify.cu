@@ -121,7 +121,7 @@ greedy_scan_kernel(const float* x, int64_t ld, int V, int kp1, int nchunks,
       k = v > k ? v : k;
     }
     k = block_reduce(k, red, OpMax());
-    if (threadIdx.x == 0) tt[r] = (int)argmax_key_index(k);
+    if (threadIdx.x == 0) tt[r] = k == 0ull ? 0 : (int)argmax_key_index(k);  // all-NaN row: token 0
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
@@ -224,6 +224,7 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   int acc = 0;
   for (int j = 0; j < K; ++j) {
     const int tok = spec[(int64_t)b * (K + 1) + j + 1];
+    if ((unsigned)tok >= (unsigned)V) break;  // not a token id: reject (never index with it)
     const float2 pst = stats[j];  // target row j+off is stored at index j
     const float2 qst = stats[nP + j];
     const float pv = prob_of(__ldcg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok), tp, pst.x, pst.y);
@@ -319,7 +320,7 @@ sample_draw_kernel(const float* lp, const float* lq,
       k = v > k ? v : k;
     }
     accept_until[b] = d.acc;
-    recovery[b] = (int32_t)argmax_key_index(k);
+    recovery[b] = k == 0ull ? 0 : (int32_t)argmax_key_index(k);
     if (mask) {
       mask[(int64_t)b * (K + 1)] = 0;
       for (int j = 0; j < K; ++j) mask[(int64_t)b * (K + 1) + j + 1] = (j < d.acc) ? 1 : 0;
@@ -338,6 +339,46 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t i) {
   const uint64_t h = mix64(seed ^ mix64(i));
   return ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0,1), 24-bit grid
+}
+
+// ---------------------------------------------------------------- row sampling
+// token[r] = argmax_j (x[r][j] / T + G[r][j]), G = -log(-log(u)), u from the
+// counter hash at (seed, offset + r * V + j): a draw from softmax(x[r] / T)
+// (Gumbel-max), with no noise buffer in HBM.  Same chunked scan and ordered
+// fold as the greedy kernels, so a row's draw is deterministic for a seed.
+__global__ void __launch_bounds__(kScanThreads)
+sample_rows_kernel(const float* x, int64_t ld, int V, int nchunks, float inv_t, uint64_t seed, uint64_t offset,
+                   unsigned int* counters, unsigned long long* partial, int32_t* out) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool is_last;
+  pdl_wait();
+  const int row = blockIdx.y, c = blockIdx.x;
+  int lo, hi;
+  chunk_bounds(V, nchunks, c, lo, hi);
+  const float* xr = x + (int64_t)row * ld;
+  const uint64_t base = offset + (uint64_t)row * (uint64_t)V;
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
+    const float u = hash_uniform(seed, base + (uint64_t)j);
+    const float v = __ldcg(xr + j) * inv_t - logf(-logf(u));
+    if (v > best) {
+      best = v;
+      bidx = j;
+    }
+  }
+  unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
+  if (threadIdx.x == 0) partial[(int64_t)row * nchunks + c] = key;
+  pdl_trigger();
+  if (!last_block_of(&counters[row], (unsigned)nchunks, &is_last)) return;
+  unsigned long long k = 0ull;
+  for (int i = threadIdx.x; i < nchunks; i += blockDim.x) {
+    const unsigned long long v = __ldcg(&partial[(int64_t)row * nchunks + i]);
+    k = v > k ? v : k;
+  }
+  k = block_reduce(k, red, OpMax());
+  // no finite candidate in the row (all logits NaN): emit token 0 rather than an invalid id
+  if (threadIdx.x == 0) out[row] = k == 0ull ? 0 : (int32_t)argmax_key_index(k);
 }
 
 __global__ void uniform_fill_kernel(float* out, int64_t n, uint64_t seed, uint64_t offset) {
@@ -464,6 +505,24 @@ extern "C" int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, 
   if (rows <= 0 || rows > 65535 || V <= 0 || ld < V || !x || !out) return SSD_ERR_INVALID;
   return launch_greedy((cudaStream_t)stream, x, ld, rows, 1, V, nullptr, nullptr, nullptr, nullptr, nullptr, out,
                        workspace, workspace_bytes);
+}
+
+extern "C" int ssd_sample_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, float temperature,
+                               uint64_t seed, uint64_t offset, int32_t* out, void* workspace,
+                               size_t workspace_bytes) {
+  if (rows <= 0 || rows > 65535 || V <= 0 || ld < V || !x || !out || !(temperature > 0.f)) return SSD_ERR_INVALID;
+  const int nch = scan_chunks(rows, V);
+  const size_t need = kCounterBytes + sizeof(unsigned long long) * (size_t)rows * nch;
+  if (!workspace || workspace_bytes < need) return SSD_ERR_WORKSPACE;
+  if (rows > kCounterCap) return SSD_ERR_UNSUPPORTED;
+  unsigned int* counters = reinterpret_cast<unsigned int*>(workspace);
+  unsigned long long* part =
+      reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) + kCounterBytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  SSD_PDL(sample_rows_kernel, dim3(nch, rows), kScanThreads, 0, st, x, ld, V, nch, 1.0f / temperature, seed, offset,
+          counters, part, out);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
 }
 
 static void sample_layout(int B, int K, int V, int& nR, int& nch, size_t& off_part, size_t& off_dec,

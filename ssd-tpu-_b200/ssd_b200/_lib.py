@@ -36,6 +36,7 @@ SIGNATURES = {
     "ssd_verify_greedy": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i]),
     "ssd_verify_greedy_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i]),
     "ssd_argmax_rows": (_i, [_p, _p, _i64, _i, _i, _p, _p, _sz]),
+    "ssd_sample_rows": (_i, [_p, _p, _i64, _i, _i, _f, _u64, _u64, _p, _p, _sz]),
     "ssd_verify_sample_workspace_size": (_sz, [_i, _i, _i]),
     "ssd_verify_sample": (_i, [_p, _p, _p, _p, _p, _p, _f, _f, _f, _i, _p, _p, _p, _p, _sz, _i, _i, _i]),
     "ssd_uniform_fill": (_i, [_p, _p, _i64, _u64, _u64]),

@@ -120,3 +120,23 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     check(lib().ssd_argmax_rows(stream_ptr(), ptr(x), x.stride(0), rows, v, ptr(out), ptr(ws), ws.numel()),
           "ssd_argmax_rows")
     return out
+
+
+def sample_rows(x: torch.Tensor, temperature: float, seed: int, offset: int = 0,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """One draw per row from softmax(x / temperature) (``ssd_sample_rows``, Gumbel-max on a counter hash).
+
+    The draw for (seed, offset) is reproducible; callers advance ``offset`` by at
+    least rows * V between draws that must be independent.
+    """
+    if x.dim() != 2 or x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1:
+        raise ValueError("sample_rows wants a row-contiguous 2-D fp32 CUDA tensor")
+    rows, v = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    nbytes = lib().ssd_verify_greedy_workspace_size(rows, 0, v)
+    ws = workspace(x.device, "sample_rows", nbytes)
+    check(lib().ssd_sample_rows(stream_ptr(), ptr(x), x.stride(0), rows, v, float(temperature),
+                                int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), ptr(out), ptr(ws), ws.numel()),
+          "ssd_sample_rows")
+    return out

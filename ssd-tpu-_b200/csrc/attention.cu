@@ -594,23 +594,33 @@ paged_attention_tc_kernel(const bf16* q, const bf16* pages, int num_layers,
 //     each page's K and V rows into a ring of shared-memory stages with TMA
 //     (a 5-D tensor map over the cache, box = 16 rows x 64 dims, 128-byte
 //     swizzle, no multicast), one mbarrier per stage;
-//   * warps 1-4 are consumers: consumer c takes pages c, c+4, c+8, c+12 and
-//     keeps an online-softmax state per query row (running max, sum and the
-//     16 x D accumulator in registers) across its pages: S = Q K^T and O += P V
-//     with mma.sync m16n8k16 (bf16 in, fp32 accumulate), fragments via
-//     ldmatrix from the swizzled stages;
-//   * the four consumers' states are combined in warp order; a group whose
-//     context fits one split writes its output directly, otherwise the split
-//     writes a partial and the group's last split folds them in split order.
+//   * the other warps are consumers (3 at D = 256, 4 otherwise): consumer c
+//     takes pages c, c+C, c+2C, ... and keeps an online-softmax state per query
+//     row (running max, sum and the 16 x D accumulator in registers) across
+//     its pages: S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
+//     accumulate), fragments via ldmatrix from the swizzled stages.  The stage
+//     count is a multiple of C, so every stage belongs to one consumer, which
+//     waits on it exactly one phase after its previous use (an mbarrier wait
+//     only tells phases apart modulo 2);
+//   * the consumers' states are combined in warp order; a group whose context
+//     fits one split writes its output directly, otherwise the split writes a
+//     partial and the group's last split folds them in split order.
 // Rows of a page past the end of the context are zeroed in the stage before
 // P.V (masked probabilities are exact zeros, stale rows must not be NaN).
-// 160 threads and ~106 KB of shared memory: two CTAs per SM, up to 12 pages
-// (192 KB) of K/V in flight per SM.  Batch invariance as for the other
+// At D = 256: 128 threads and ~106 KB of shared memory, two CTAs per SM, up
+// to 12 pages (192 KB) of K/V in flight per SM.  Batch invariance as for the other
 // kernels: splits, page ownership and every reduction order are fixed.
 constexpr int kTmaChunk = 256;                  // positions per split
 constexpr int kTmaPage = 16;                    // rows per page (TMA box height)
-constexpr int kTmaConsumers = 4;
-constexpr int kTmaThreads = 32 * (1 + kTmaConsumers);
+// consumer warps per CTA for head size D; the stage count is a multiple of it
+template <int D>
+constexpr int tma_consumers() {
+  return D == 256 ? 3 : 4;
+}
+template <int D>
+constexpr int tma_threads() {
+  return 32 * (1 + tma_consumers<D>());
+}
 constexpr uint32_t kTmaWaitLimit = 1u << 24;
 
 __device__ __forceinline__ void tmb_init(uint32_t bar, uint32_t count) {
@@ -650,18 +660,20 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
 
 template <int D>
 struct TmaSmem {
+  static constexpr int CONS = tma_consumers<D>();
   static constexpr int CHUNKS = D / 64;                          // 128-byte swizzle rows per page row
   static constexpr uint32_t PLANE = kTmaPage * D * 2;            // K (or V) of one page: 16 x D bf16
   static constexpr uint32_t STAGE = 2 * PLANE;
   static constexpr int STAGES = D == 256 ? 6 : D == 128 ? 12 : 16;
+  static_assert(STAGES % CONS == 0, "every stage must belong to one consumer (mbarrier parity)");
   static constexpr int QST = D + 8;                              // padded Q rows (ldmatrix conflict-free)
   static constexpr size_t ring = (size_t)STAGES * STAGE;
   static constexpr size_t q_off = ring;
   static constexpr size_t q_bytes = 2ull * 16 * QST;
   static constexpr size_t bar_off = q_off + q_bytes;
   static constexpr size_t ml_off = bar_off + 8 * 2 * STAGES + 16;
-  static constexpr size_t total = 1024 + ml_off + sizeof(float2) * kTmaConsumers * kRows;
-  static constexpr size_t o_bytes = sizeof(float) * kTmaConsumers * kRows * D;   // aliases the ring
+  static constexpr size_t total = 1024 + ml_off + sizeof(float2) * CONS * kRows;
+  static constexpr size_t o_bytes = sizeof(float) * CONS * kRows * D;   // aliases the ring
   static_assert(o_bytes <= ring, "consumer outputs must fit in the ring");
 };
 
@@ -672,7 +684,7 @@ __device__ __forceinline__ uint32_t sw_off(int row, int dim) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kTmaThreads, 2)
+__global__ void __launch_bounds__(tma_threads<D>(), 2)
 paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16* q, int num_layers, int num_blocks,
                            int hkv, int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
                            const int32_t* q_lens, bf16* out, float scale, int T, int hq, int row_groups, int nsplit,
@@ -680,6 +692,8 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   using S = TmaSmem<D>;
   constexpr int KSTEPS = D / 16;
   constexpr int NT = D / 8;
+  constexpr int NCONS = S::CONS;
+  constexpr int NTHREADS = tma_threads<D>();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -766,7 +780,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
     // ------------------------------------------------------------ consumers
     const int c = warp - 1;
     // Q rows (bf16, zero padding rows) -- consumers share this work
-    for (int i = tid - 32; i < 16 * (D / 8); i += 32 * kTmaConsumers) {
+    for (int i = tid - 32; i < 16 * (D / 8); i += 32 * NCONS) {
       const int r = i / (D / 8), cc = i % (D / 8);
       uint4 v = make_uint4(0, 0, 0, 0);
       if (r < nrows && ri.pos[r] >= 0) {
@@ -775,7 +789,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
       }
       *reinterpret_cast<uint4*>(qs + r * S::QST + cc * 8) = v;
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kTmaConsumers) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCONS) : "memory");
     const int rA = lane >> 2;
     const int prow = (rA < nrows) ? ri.pos[rA] : -1;
     float m_run = -INFINITY, l_run = 0.f;
@@ -786,7 +800,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
       for (int e = 0; e < 4; ++e) oacc[nt][e] = 0.f;
     const uint32_t qaddr0 = (uint32_t)__cvta_generic_to_shared(qs);
     const int lr = lane & 7, lm = lane >> 3;
-    for (int j = c; j < npages; j += kTmaConsumers) {
+    for (int j = c; j < npages; j += NCONS) {
       const int st = j % S::STAGES;
       if (!tmb_wait(full(st), (uint32_t)(j / S::STAGES) & 1u)) {
         s_abort = 1;
@@ -868,7 +882,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
       if (lane == 0) tmb_arrive(empty(st));
     }
     // this consumer's state -> shared memory (after every consumer is done with the ring)
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kTmaConsumers) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCONS) : "memory");
     if ((lane & 3) == 0 && rA < kRows) mls[c * kRows + rA] = make_float2(m_run, l_run);
     float* ow = os + c * kRows * D;
     if (rA < nrows) {
@@ -894,15 +908,15 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
     return;
   }
   const int64_t pbase = (grp_id * nsplit + split) * kRows;
-  for (int i = tid; i < nrows * D; i += kTmaThreads) {
+  for (int i = tid; i < nrows * D; i += NTHREADS) {
     const int r = i / D, d = i % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, mls[w * kRows + r].x);
+    for (int w = 0; w < NCONS; ++w) M = fmaxf(M, mls[w * kRows + r].x);
     float O = 0.f, L = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kTmaConsumers; ++w) {
+      for (int w = 0; w < NCONS; ++w) {
         const float2 ml = mls[w * kRows + r];
         const float wt = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
         L += ml.y * wt;
@@ -921,8 +935,8 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   pdl_trigger();
   if (direct) return;
   if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
-  attention_fold<bf16, D, kTmaChunk, kTmaThreads>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T,
-                                                  hq, kvh, b, os);
+  attention_fold<bf16, D, kTmaChunk, NTHREADS>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq,
+                                               kvh, b, os);
 }
 
 // ---------------------------------------------------------------- K2
@@ -1083,7 +1097,7 @@ int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int 
   char* w = reinterpret_cast<char*>(ws);
   const int nsplit = (max_seq_len + kTmaChunk - 1) / kTmaChunk;  // <= L.nsplit: fits the workspace
   dim3 grid(nsplit, hkv * L.row_groups, B);
-  SSD_PDL(kern, grid, kTmaThreads, S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
+  SSD_PDL(kern, grid, tma_threads<D>(), S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
           layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups,
           nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
           reinterpret_cast<unsigned int*>(w + L.off_cnt), reinterpret_cast<unsigned int*>(w + kCounterBytes));

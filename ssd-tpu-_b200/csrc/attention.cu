@@ -743,6 +743,10 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   const int k_end = min(min(min(k_begin + kTmaChunk, kmax), seq_len), max_blocks * kTmaPage);
   const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
   const int ns = max(1, min(nsplit, (seq_len + kTmaChunk - 1) / kTmaChunk));
+  if (split >= ns) {  // past this sequence's context: the fold neither waits for nor reads this split
+    pdl_trigger();
+    return;
+  }
   const int npages = k_end > k_begin ? (k_end - k_begin + kTmaPage - 1) / kTmaPage : 0;
 
   int issued = 0;  // pages the producer lane has put in flight
@@ -902,11 +906,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   }
 
   // ---- combine the consumers in warp order
-  const bool direct = (ns == 1);
-  if (direct && split != 0) {  // the group's context fits split 0, which writes the output
-    pdl_trigger();
-    return;
-  }
+  const bool direct = (ns == 1);  // the group's context fits split 0, which writes the output
   const int64_t pbase = (grp_id * nsplit + split) * kRows;
   for (int i = tid; i < nrows * D; i += NTHREADS) {
     const int r = i / D, d = i % D;
@@ -934,7 +934,8 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   }
   pdl_trigger();
   if (direct) return;
-  if (!last_block_of(&counters[grp_id], (unsigned)nsplit, &is_last)) return;
+  // the ns splits that hold context take a ticket; the last one folds them in split order
+  if (!last_block_of(&counters[grp_id], (unsigned)ns, &is_last)) return;
   attention_fold<bf16, D, kTmaChunk, NTHREADS>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq,
                                                kvh, b, os);
 }

@@ -174,6 +174,25 @@ int ssd_page_free(ssd_stream_t stream, int32_t* block_tables, int32_t* table_len
                   int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks,
                   const uint8_t* release, int B);
 
+/*
+ * Fork for branch decoding (async SSD fan-out; the reference builds dense branch
+ * masks instead, jax_ssd/kernels/masks.py:8-30, pallas_attention.py:16-35):
+ * rows dst_row0 .. dst_row0+n-1 (empty tables, n <= 1024) take the first
+ * num_tokens tokens of row src_row.  Its full blocks are shared (ref count + 1
+ * per sharer, absent counting as 1, as page_manager.py:66-70 reads it); when the
+ * last block is partial each row gets a fresh block popped from the free-list top
+ * in row order, and (kv_pages != NULL) the partial block's first num_tokens %
+ * block_size rows are copied into it for every layer and both planes.  A row that
+ * cannot get its block is left empty with ok[i] = 0 (ok is required with kv_pages).
+ * Paged attention over the forked rows then sees the trunk plus each branch's own
+ * tokens -- the branch mask -- with no trunk copy.  Releasing a forked row with
+ * ssd_page_free decrements the shared counts.
+ */
+int ssd_page_fork(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens, int max_blocks,
+                  int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks,
+                  int src_row, int dst_row0, int n, int num_tokens, int block_size, uint8_t* ok,
+                  void* kv_pages, int dtype, int num_layers, int num_kv_heads, int head_dim);
+
 /* ------------------------------------------------------------ speculation cache */
 /*
  * SpecCache.lookup (jax_ssd/algorithm/spec_cache.py:43-66) on the device.

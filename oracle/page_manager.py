@@ -78,6 +78,28 @@ class OraclePageManager:
         seq.block_table.clear()
         seq.draft_block_table.clear()
 
+    def fork(self, src: OracleSeq, dsts: list, num_tokens: int) -> list:
+        """Branch fork (no reference counterpart; the device ``ssd_page_fork``): each empty
+        dst takes src's first num_tokens tokens -- full blocks shared with ref counts
+        ``get(b, 1) + 1`` (the reading of page_manager.py:66-70), a fresh LIFO-popped block
+        for a partial last block.  Returns ok per dst (False: left empty, nothing popped)."""
+        full, part = divmod(num_tokens, self.block_size)
+        need = full + (1 if part else 0)
+        oks = []
+        for d in dsts:
+            fits = len(src.block_table) >= need and (not part or len(self.free_blocks) > 0)
+            oks.append(fits)
+            if not fits:
+                continue
+            d.block_table = list(src.block_table[:full])
+            for blk in d.block_table:
+                self.ref_counts[blk] = self.ref_counts.get(blk, 1) + 1
+            if part:
+                blk = self.free_blocks.pop()
+                d.block_table.append(blk)
+                self.ref_counts[blk] = self.ref_counts.get(blk, 0) + 1
+        return oks
+
     def _free_block(self, blk: int) -> None:
         rc = self.ref_counts.get(blk, 1) - 1
         self.ref_counts[blk] = rc

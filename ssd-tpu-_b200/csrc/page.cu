@@ -194,10 +194,113 @@ page_release_kernel(int mode, int32_t* tables, int32_t* lens, int max_blocks, in
   pdl_trigger();
 }
 
+// Fork: dst rows dst_row0 .. dst_row0+n-1 (empty tables) take the first
+// num_tokens tokens of row src_row -- its full blocks shared (ref count + 1 per
+// sharer, absent counting as 1) and, when the last block is partial, a fresh
+// block of their own popped from the free-list top in row order.  A row that
+// would need a fresh block when none is left is left empty (ok = 0).
+__global__ void __launch_bounds__(kPageThreads)
+page_fork_kernel(int32_t* tables, int32_t* lens, int max_blocks, int32_t* free_list, int32_t* free_top,
+                 int32_t* ref_counts, int num_blocks, int src_row, int dst_row0, int n, int num_tokens,
+                 int block_size, uint8_t* ok) {
+  __shared__ int s_nok;
+  __shared__ uint8_t s_ok[kPageThreads];
+  pdl_wait();
+  const int full = num_tokens / block_size;
+  const bool part = (num_tokens % block_size) != 0;
+  const int need = full + (part ? 1 : 0);
+  if (threadIdx.x == 0) {
+    int top = *free_top;
+    int nok = 0;
+    for (int i = 0; i < n; ++i) {
+      const int d = dst_row0 + i;
+      const bool fits = need <= max_blocks && lens[src_row] >= need && (!part || top > 0);
+      s_ok[i] = fits ? 1 : 0;
+      if (ok) ok[i] = fits ? 1 : 0;
+      if (!fits) continue;
+      if (part) {
+        const int blk = free_list[--top];
+        free_list[top] = -1;
+        tables[(int64_t)d * max_blocks + full] = blk;
+        if (blk >= 0 && blk < num_blocks) ref_counts[blk] += 1;
+      }
+      lens[d] = need;
+      ++nok;
+    }
+    *free_top = top;
+    s_nok = nok;
+  }
+  __syncthreads();
+  const int nok = s_nok;
+  // shared full blocks: copy the table prefix into every row that forked, count the sharers
+  for (int j = threadIdx.x; j < full && j < max_blocks; j += blockDim.x) {
+    const int blk = tables[(int64_t)src_row * max_blocks + j];
+    for (int i = 0; i < n; ++i)
+      if (s_ok[i]) tables[(int64_t)(dst_row0 + i) * max_blocks + j] = blk;
+    if (nok > 0 && blk >= 0 && blk < num_blocks) ref_counts[blk] = max(ref_counts[blk], 1) + nok;
+  }
+  pdl_trigger();
+}
+
+// Copy rows [0, rows) of row src_row's block `full` into each forked row's own
+// block `full`, every layer and both planes of pages [2][L][NB][BS][Hkv][D].
+template <typename KV>
+__global__ void kv_fork_copy_kernel(KV* pages, int num_layers, int num_blocks, int block_size, int hkv, int D,
+                                    const int32_t* tables, int max_blocks, int src_row, int dst_row0, int n, int full,
+                                    int rows, const uint8_t* ok) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x;       // forked row
+  const int lp = blockIdx.y;      // plane * num_layers + layer
+  if (ok && !ok[i]) return;
+  const int sblk = tables[(int64_t)src_row * max_blocks + full];
+  const int dblk = tables[(int64_t)(dst_row0 + i) * max_blocks + full];
+  if ((unsigned)sblk >= (unsigned)num_blocks || (unsigned)dblk >= (unsigned)num_blocks) return;
+  const int64_t page = (int64_t)block_size * hkv * D;
+  const KV* src = pages + ((int64_t)lp * num_blocks + sblk) * page;
+  KV* dst = pages + ((int64_t)lp * num_blocks + dblk) * page;
+  const int64_t count = (int64_t)rows * hkv * D;
+  for (int64_t e = threadIdx.x; e < count; e += blockDim.x) dst[e] = src[e];
+}
+
 }  // namespace
 }  // namespace ssd
 
 using namespace ssd;
+
+extern "C" int ssd_page_fork(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens, int max_blocks,
+                             int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks, int src_row,
+                             int dst_row0, int n, int num_tokens, int block_size, uint8_t* ok, void* kv_pages,
+                             int dtype, int num_layers, int num_kv_heads, int head_dim) {
+  if (n < 0 || max_blocks <= 0 || num_blocks <= 0 || block_size <= 0 || num_tokens < 0 || src_row < 0 ||
+      dst_row0 < 0 || (src_row >= dst_row0 && src_row < dst_row0 + n))
+    return SSD_ERR_INVALID;
+  if (n == 0) return SSD_OK;
+  if (!block_tables || !table_lens || !free_list || !free_top || !ref_counts) return SSD_ERR_INVALID;
+  if (kv_pages && (num_layers <= 0 || num_kv_heads <= 0 || head_dim <= 0 || !ok)) return SSD_ERR_INVALID;
+  if (n > kPageThreads) return SSD_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  SSD_PDL(page_fork_kernel, 1, kPageThreads, 0, st, block_tables, table_lens, max_blocks, free_list, free_top,
+          ref_counts, num_blocks, src_row, dst_row0, n, num_tokens, block_size, ok);
+  SSD_CHECK_LAUNCH();
+  const int rows = num_tokens % block_size;
+  if (kv_pages && rows > 0) {
+    const int full = num_tokens / block_size;
+    dim3 grid(n, 2 * num_layers);
+    if (dtype == SSD_DTYPE_BF16)
+      SSD_PDL(kv_fork_copy_kernel<bf16>, grid, 256, 0, st, reinterpret_cast<bf16*>(kv_pages), num_layers,
+              num_blocks, block_size, num_kv_heads, head_dim, block_tables, max_blocks, src_row, dst_row0, n, full,
+              rows, ok);
+    else if (dtype == SSD_DTYPE_F32)
+      SSD_PDL(kv_fork_copy_kernel<float>, grid, 256, 0, st, reinterpret_cast<float*>(kv_pages), num_layers,
+              num_blocks, block_size, num_kv_heads, head_dim, block_tables, max_blocks, src_row, dst_row0, n, full,
+              rows, ok);
+    else
+      return SSD_ERR_INVALID;
+    SSD_CHECK_LAUNCH();
+  }
+  return SSD_OK;
+}
 
 extern "C" int ssd_page_allocate(ssd_stream_t stream, int32_t* block_tables, int32_t* table_lens, int max_blocks,
                                  int32_t* free_list, int32_t* free_top, int32_t* ref_counts, int num_blocks,

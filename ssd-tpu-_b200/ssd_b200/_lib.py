@@ -43,6 +43,7 @@ SIGNATURES = {
     "ssd_page_allocate": (_i, [_p, _p, _p, _i, _p, _p, _p, _i, _p, _p, _p, _i, _i]),
     "ssd_page_rollback": (_i, [_p, _p, _p, _i, _p, _p, _p, _i, _p, _p, _p, _i, _i]),
     "ssd_page_free": (_i, [_p, _p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _p, _i]),
+    "ssd_page_fork": (_i, [_p, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p, _i, _i, _i, _i]),
     "ssd_spec_cache_lookup": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _p, _i, _p, _p, _p, _p]),
     "ssd_kv_write": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p, _p, _p, _i, _i]),
     "ssd_paged_attention_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),

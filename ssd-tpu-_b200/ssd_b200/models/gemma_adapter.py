@@ -32,20 +32,25 @@ from .gemma import GemmaRunner, GemmaWeights
 
 class GemmaAdapter:
     def __init__(self, weights: GemmaWeights, max_model_len: int = 4096, block_size: int = 16,
-                 max_tokens: int = 64, name: str = "gemma") -> None:
+                 max_tokens: int = 64, name: str = "gemma", max_branches: int = 0) -> None:
         s = weights.shape
         self.w = weights
         self.name = name
         self.vocab_size = s.vocab
         self.max_model_len = max_model_len
         self.block_size = block_size
-        self.num_blocks = (max_model_len + block_size - 1) // block_size + 2
+        self.max_branches = int(max_branches)
+        per_seq = (max_model_len + block_size - 1) // block_size + 2
+        # row 0 holds the sequence; rows 1.. are branch rows forked from it (shared trunk pages
+        # plus one private block each for the partial trunk page and the branch tokens)
+        self.num_blocks = per_seq + self.max_branches * 4
         self.dev = weights.device
         self.chunk = min(64, max_tokens_per_forward(weights.dtype))
-        self.runner = GemmaRunner(weights, 1, max(self.chunk, max_tokens), max_model_len)
+        self.runner = GemmaRunner(weights, 1 + self.max_branches, max(self.chunk, max_tokens), max_model_len)
         self.cache = KVCacheState.allocate(s.num_layers, self.num_blocks, block_size, s.num_kv_heads, s.head_dim,
                                            dtype=weights.dtype, device=self.dev)
-        self.pm = PageManager(block_size, self.num_blocks, max_seqs=1, device=self.dev)
+        self.pm = PageManager(block_size, self.num_blocks, max_seqs=1 + self.max_branches,
+                              max_blocks_per_seq=per_seq, device=self.dev)
         self.cached: list[int] = []   # tokens whose K/V rows are valid in the cache
         self.pending: list[int] = []  # tokens of the last verify (written, not yet committed)
         self._lg1 = torch.empty((1, s.vocab), dtype=torch.float32, device=self.dev)
@@ -145,6 +150,67 @@ class GemmaAdapter:
             spec.append(int(nxt.item()))
             feed = [spec[-1]]
         return spec, logits
+
+    def draft_branches(self, prefix_tokens: list[int], feeds: list[list[int]], k: int) -> list[list[int]]:
+        """k greedy draft tokens for each branch ``prefix + feeds[i]``, all branches at once.
+
+        Row 0 is brought to hold exactly the prefix (common-prefix reuse, as in
+        ``draft_speculate``); branch rows are forked from it (``ssd_page_fork``: trunk
+        pages shared, the partial page copied), then one forward over every branch's
+        feed (ragged) and k-1 one-token forwards run over all branch rows, and the
+        branch rows are released.  Each branch's tokens equal
+        ``draft_speculate(prefix + feeds[i], k)[0]`` (batch invariance); branch
+        attention is the paged attention over the forked tables.
+        """
+        prefix = [int(t) for t in prefix_tokens]
+        n_all = len(feeds)
+        if n_all == 0:
+            return []
+        if self.max_branches <= 0 or any(len(f) == 0 for f in feeds):
+            return [self.draft_speculate(prefix + list(f), k)[0] for f in feeds]
+        common = 0
+        for a, b in zip(self.cached, prefix):
+            if a != b:
+                break
+            common += 1
+        self._truncate(common)
+        if len(prefix) > common:
+            self._run(prefix[common:], None, last_only=True)
+        n0 = len(prefix)
+        out: list[list[int]] = []
+        cap = max_tokens_per_forward(self.w.dtype)
+        tmax = max(len(f) for f in feeds)
+        group = max(1, min(self.max_branches, cap // max(tmax, 1)))
+        for g0 in range(0, n_all, group):
+            fs = [list(f) for f in feeds[g0:g0 + group]]
+            n = len(fs)
+            ok = self.pm.fork_rows(0, 1, n, n0, self.cache)
+            if not bool(ok.all()):
+                self.pm.free_rows(1, n)
+                out.extend(self.draft_speculate(prefix + f, k)[0] for f in fs)
+                continue
+            ql = [len(f) for f in fs]
+            t = max(ql)
+            toks = torch.zeros((n, t), dtype=torch.int32)
+            for i, f in enumerate(fs):
+                toks[i, :len(f)] = torch.tensor(f, dtype=torch.int32)
+            toks = toks.to(self.dev)
+            qlen = torch.tensor(ql, dtype=torch.int32, device=self.dev)
+            base = torch.full((n,), n0, dtype=torch.int32, device=self.dev)
+            self.pm.allocate_rows(1, n, base, qlen + (k - 1), None)
+            lg = torch.empty((n, self.vocab_size), dtype=torch.float32, device=self.dev)
+            nxt = torch.empty((k, n), dtype=torch.int32, device=self.dev)
+            tables = self.pm.tables[1:1 + n]
+            self.runner.forward(toks, base, self.cache.pages, tables, lg, q_lens=qlen, last_only=True)
+            argmax_rows(lg, nxt[0])
+            for i in range(1, k):
+                self.runner.forward(nxt[i - 1].view(n, 1), base + qlen + (i - 1), self.cache.pages, tables, lg,
+                                    last_only=True)
+                argmax_rows(lg, nxt[i])
+            self.pm.free_rows(1, n)
+            host = nxt.t().cpu().tolist()
+            out.extend([int(x) for x in row] for row in host)
+        return out
 
     def tokenize(self, text: str) -> list[int]:
         return [b % self.vocab_size for b in text.encode("utf-8")]

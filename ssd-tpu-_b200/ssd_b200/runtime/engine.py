@@ -61,7 +61,8 @@ class LLMEngine:
             # the draft adapter and its worker live on the draft's GPU (its own GPU when
             # config.draft_device names one); only token ids cross between the GPUs
             with torch.cuda.device(self.draft_w.device):
-                self.draft = GemmaAdapter(self.draft_w, max_model_len=config.max_model_len, name="draft")
+                self.draft = GemmaAdapter(self.draft_w, max_model_len=config.max_model_len, name="draft",
+                                          max_branches=max(1, config.mq_len))
                 self.draft_worker = DraftWorker(config, self.draft)
                 self.draft_worker.start()
 

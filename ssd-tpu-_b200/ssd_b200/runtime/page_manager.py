@@ -137,6 +137,31 @@ class PageManager:
                                       self.num_blocks, ptr(num_tokens), ptr(accepted), ptr(kv_lens),
                                       self.block_size, n), "ssd_page_rollback")
 
+    def fork_rows(self, src_row: int, dst_row0: int, n: int, num_tokens: int, cache=None) -> torch.Tensor:
+        """Rows dst_row0.. (empty) take src_row's first num_tokens tokens: full blocks shared,
+        the partial block copied (K/V rows too when ``cache`` -- a ``KVCacheState`` -- is given).
+        Returns ok [n] uint8 (device)."""
+        ok = torch.zeros(max(n, 1), dtype=torch.uint8, device=self.device)
+        kv, dt, nl, hkv, hd = None, 0, 0, 0, 0
+        if cache is not None:
+            p = cache.pages
+            kv = ptr(p)
+            dt = 0 if p.dtype == torch.bfloat16 else 1
+            nl, hkv, hd = p.shape[1], p.shape[4], p.shape[5]
+        check(lib().ssd_page_fork(stream_ptr(), ptr(self.tables), ptr(self.lens), self.max_blocks,
+                                  ptr(self.free_list), ptr(self.free_top), ptr(self.ref_counts_dev), self.num_blocks,
+                                  src_row, dst_row0, n, int(num_tokens), self.block_size, ptr(ok), kv, dt, nl, hkv,
+                                  hd), "ssd_page_fork")
+        return ok[:n]
+
+    def free_rows(self, row0: int, n: int) -> None:
+        """Release rows row0 .. row0+n-1 (their blocks' ref counts drop; freed blocks return)."""
+        rel = torch.zeros(self.max_seqs, dtype=torch.uint8, device=self.device)
+        rel[row0:row0 + n] = 1
+        check(lib().ssd_page_free(stream_ptr(), ptr(self.tables), ptr(self.lens), self.max_blocks, None, None, 0,
+                                  ptr(self.free_list), ptr(self.free_top), ptr(self.ref_counts_dev),
+                                  self.num_blocks, ptr(rel), self.max_seqs), "ssd_page_free")
+
     def release(self, seq: Sequence) -> None:
         """Forget the slot of a freed sequence."""
         self._rows.pop(seq.seq_id, None)

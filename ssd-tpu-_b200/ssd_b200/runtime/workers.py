@@ -14,10 +14,14 @@ stream:
    position ``a`` with the drafted token removed (a rejected draft is never the
    recovery token; at ``a = k`` the bonus distribution is used as is).  Each
    branch is drafted from ``prefix + spec[:a] + [candidate]``, so a hit serves
-   exactly the tokens a miss would draft.  The rebuild finishes before the
-   next request is served (as in the reference, which rebuilds inside
-   ``_handle``); it overlaps the target's verify when the engine runs the draft
-   on another device or stream.  The reference builds the same keys
+   exactly the tokens a miss would draft.  All branches of a request are
+   drafted together (``GemmaAdapter.draft_branches``: the committed prefix is
+   forked into branch rows that share its KV pages, then k batched forwards --
+   the paged attention over forked tables is the reference's branch mask,
+   jax_ssd/kernels/masks.py:8-30).  The rebuild finishes before the next request
+   is served (as in the reference, which rebuilds inside ``_handle``); it
+   overlaps the target's verify when the engine runs the draft on another device
+   or stream.  The reference builds the same keys
    (workers.py:119-145) from top-F of all-zero glue logits, i.e. candidates
    ``0..F-1``, and drafts them from the candidate alone.
 """
@@ -149,12 +153,22 @@ class DraftWorker:
                     top = torch.topk(row, fan[a])
                     for c, pc in zip(top.indices.tolist(), top.values.tolist()):
                         # reach * (1 - q_a(s_a)) * q_a(c) / (1 - q_a(s_a)) = reach * q_a(c)
-                        branches.append((reach * pc, int(key[0]), a, int(c), prefix + spec[:a] + [int(c)]))
+                        branches.append((reach * pc, int(key[0]), a, int(c), spec[:a] + [int(c)], prefix))
                 if a < k:
                     reach *= q_spec[a]
         branches.sort(key=lambda b: -b[0])
-        for slot, (_, sid, a, c, branch) in enumerate(branches[: self.cache.keys.shape[0]]):
-            s, _ = self.model.draft_speculate(branch, k)
-            self.cache.insert(slot, [sid, a, c], s)
-            self.branches_drafted += 1
+        chosen = branches[: self.cache.keys.shape[0]]
+        by_prefix: dict[int, list] = {}
+        for slot, br in enumerate(chosen):
+            by_prefix.setdefault(id(br[5]), []).append((slot, br))
+        for group in by_prefix.values():
+            prefix = group[0][1][5]
+            if hasattr(self.model, "draft_branches"):
+                # every branch of one request at once: forked trunk pages, batched draft forwards
+                specs = self.model.draft_branches(prefix, [br[4] for _, br in group], k)
+            else:
+                specs = [self.model.draft_speculate(prefix + br[4], k)[0] for _, br in group]
+            for (slot, (_, sid, a, c, _feed, _p)), sp in zip(group, specs):
+                self.cache.insert(slot, [sid, a, c], sp)
+                self.branches_drafted += 1
         self.stream.synchronize()

@@ -269,3 +269,28 @@ def test_oracle_folded_norm_formulation_matches_textbook_fp32():
     la = a.forward(ids, pa, table, [0])
     lb = b.forward(ids, pb, table, [0])
     np.testing.assert_allclose(la, lb, rtol=1e-4, atol=1e-5)
+
+
+def test_oracle_fork_shares_and_frees():
+    """Branch fork: full trunk blocks shared (ref counts), a private block per branch for the
+    partial page; freeing every row returns all blocks to the free list."""
+    from oracle.page_manager import OraclePageManager, OracleSeq
+
+    pm = OraclePageManager(block_size=16, num_blocks=32)
+    src = OracleSeq(num_tokens=40)
+    assert pm.allocate(src, 0) and len(src.block_table) == 3
+    dsts = [OracleSeq(num_tokens=40) for _ in range(3)]
+    assert pm.fork(src, dsts, 40) == [True, True, True]
+    for d in dsts:
+        assert d.block_table[:2] == src.block_table[:2] and d.block_table[2] not in src.block_table
+    assert pm.ref_counts[src.block_table[0]] == 4 and pm.ref_counts[src.block_table[2]] == 1
+    for q in dsts + [src]:
+        pm.free_sequence(q)
+    assert sorted(pm.free_blocks) == list(range(32)) and pm.ref_counts == {}
+    # page-aligned trunk: nothing popped
+    pm2 = OraclePageManager(block_size=16, num_blocks=8)
+    s2 = OracleSeq(num_tokens=32)
+    pm2.allocate(s2, 0)
+    top = len(pm2.free_blocks)
+    d2 = OracleSeq(num_tokens=32)
+    assert pm2.fork(s2, [d2], 32) == [True] and len(pm2.free_blocks) == top and d2.block_table == s2.block_table

@@ -19,6 +19,10 @@
 //     (atomic ticket), which sums the fp32 partials in CTA (= K) order, so the
 //     result is deterministic and, because the unit split depends on (N, K) and
 //     the SM count only, independent of M.
+//   * shapes with at most half as many tiles as SMs use a tile-split plan
+//     instead: G CTAs per tile, each one contiguous part of its k-blocks; for
+//     M <= 16 they run as one thread-block cluster and fold in distributed
+//     shared memory (see linear_tc_kernel's CLU parameter).
 // Every mbarrier wait is bounded: on timeout the kernel records an error code,
 // stops issuing work, drains what it issued and releases its TMEM.
 //
@@ -71,6 +75,7 @@ struct Params {
   int KB;        // k-blocks per tile
   int U;         // total units = tiles * KB
   int base, rem; // units per CTA; the first `rem` CTAs take one more
+  int G;         // tile-split plan: each tile's k-blocks cut into G parts, CTA c = tile * G + part (0: stream-K)
   float* part;   // [grid][2][M][BM] partial tiles
   unsigned int* counters;  // per tile (self-resetting)
   unsigned int* err;       // error word
@@ -80,8 +85,23 @@ struct Params {
   size_t ctrl_off, dst_off;
 };
 
-__host__ __device__ inline int unit_begin(const Params& p, int c) { return c * p.base + (c < p.rem ? c : p.rem); }
+// First unit of CTA c.  Stream-K: contiguous ranges of base or base + 1 units.
+// Tile-split: part j of a tile takes KB / G k-blocks, the first KB % G parts one
+// more -- the same contiguous, K-ordered ranges, aligned to tiles.
+__host__ __device__ inline int unit_begin(const Params& p, int c) {
+  if (p.G) {
+    const int tile = c / p.G, part = c - tile * p.G;
+    const int b = p.KB / p.G, r = p.KB % p.G;
+    return tile * p.KB + part * b + (part < r ? part : r);
+  }
+  return c * p.base + (c < p.rem ? c : p.rem);
+}
 __device__ inline int cta_of_unit(const Params& p, int u) {
+  if (p.G) {
+    const int tile = u / p.KB, kb = u - tile * p.KB;
+    const int b = p.KB / p.G, r = p.KB % p.G, big = r * (b + 1);
+    return tile * p.G + (kb < big ? kb / (b + 1) : r + (kb - big) / b);
+  }
   const int big = p.rem * (p.base + 1);
   return u < big ? u / (p.base + 1) : p.rem + (u - big) / p.base;
 }
@@ -119,6 +139,44 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
   }
   *abort_flag = 1;
   atomicExch(err, code);
+  return false;
+}
+
+// ---- thread-block cluster (distributed shared memory) helpers
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+// the same shared-memory offset in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t caddr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+// bounded wait that acquires what other CTAs of the cluster released with their arrivals
+__device__ __forceinline__ bool wait_cluster_bounded(uint32_t bar, uint32_t parity, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
   return false;
 }
 
@@ -231,7 +289,7 @@ struct Cfg {
   // share the SM and prefetch its weights while this one drains (PDL).
   static constexpr int STAGES = MP <= 16 ? 6 : MP <= 32 ? 5 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
   static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;
-  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4) + 16 + 4 * 256;  // + row scales
+  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16 + 4 * 256;  // + row scales
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
 };
 
@@ -239,7 +297,13 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 
 // COLL: instantiate the fused-collective epilogue (p.coll != COLL_NONE); the
 // plain projection is compiled without it so that its code stays small.
-template <int MP, bool COLL>
+// CLU: launched as clusters of p.G CTAs over the tile-split plan (one tile per
+// cluster, one segment per CTA).  The parts of a tile meet in distributed
+// shared memory instead of the global partial buffer: every non-leader leaves
+// its fp32 partial in its own (idle) ring and arrives on the leader's mbarrier;
+// the leader folds its own accumulator and the peers' partials in part (= K)
+// order -- the same sums as the global fold, with no ticket and no L2 round trips.
+template <int MP, bool COLL, bool CLU>
 __global__ void __launch_bounds__(kThreads)
 linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const Params p) {
@@ -254,7 +318,8 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   auto empty = [&](int s) { return bars + 8u * (S + s); };
   auto accf = [&](int b) { return bars + 8u * (2 * S + b); };
   auto acce = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * C::STAGE + 8 * (2 * S + 4));
+  const uint32_t red_bar = bars + 8u * (2 * S + 4);  // CLU: the non-leaders' partials are ready
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * C::STAGE + 8 * (2 * S + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* inv_s = reinterpret_cast<float*>(tmem_slot + 4);  // [M] row scales
@@ -272,6 +337,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       mbar_init(accf(b), 1);
       mbar_init(acce(b), kEpiThreads);
     }
+    if (CLU) mbar_init(red_bar, (uint32_t)(p.G - 1));
     *abort_flag = 0;
     *last_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -287,6 +353,9 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // CLU: split-phase cluster barrier -- arrive now, wait before the first remote
+  // access, so that the peers' mbarrier inits are visible by then.
+  if (CLU) cluster_arrive();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -477,7 +546,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         }
       }
     };
-    if (p.rowscale) {
+    if (p.rowscale && (!CLU || cluster_ctarank() == 0)) {
       // RMS of each token row (the (1 + w) factor is folded into the weights):
       // warp (q) takes rows m = q, q+4, ...; lanes stride K in 8-element vectors,
       // xor-tree sum -- a fixed order, identical in every CTA and for any M.
@@ -498,8 +567,73 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       }
       epi_bar();
     }
+    if constexpr (CLU) {
+      // ------------------------------------------------ cluster fold (one tile)
+      cluster_wait();  // startup phase: every CTA of the cluster has initialised its barriers
+      const uint32_t crank = cluster_ctarank();
+      const int tile = cta / p.G;
+      const int n = tile * BM + row;
+      float v[16];
+      if (wait_bounded(accf(0), 0u, abort_flag, p.err, 4)) {
+        tc_fence_after();
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+      }
+      // [M][BM] fp32 partial in ring stage 0: every MMA of this CTA has completed
+      // (accf), so no operand lives there any more
+      float* red = reinterpret_cast<float*>(gbase);
+      if (crank != 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < p.M) red[j * BM + row] = v[j];
+        // the barrier orders all epilogue threads' stores before thread 64's
+        // cluster-scope release (cumulativity)
+        epi_bar();
+        if (threadIdx.x == 64) mbar_arrive_remote(mapa(red_bar, 0));
+      } else {
+        if (!wait_cluster_bounded(red_bar, 0u, 4u * kWaitLimit)) {
+          *abort_flag = 1;
+          atomicExch(p.err, 6u);
+        }
+        // fold in part (= K) order, 4 peers' loads in flight at a time: the sums
+        // of the global fold (0 + part 0 + part 1 + ...)
+        float s[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s[j] = 0.f + v[j];
+        const uint32_t red_s = smem_u32(red) + 4u * (uint32_t)row;
+        for (int c = 1; c < p.G; c += 4) {
+          float r[4][16];
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint32_t rb = mapa(red_s, (uint32_t)min(c + cc, p.G - 1));
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              r[cc][j] = (c + cc < p.G && j < p.M) ? ld_dsmem(rb + 4u * (uint32_t)(j * BM)) : 0.f;
+          }
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s[j] += r[cc][j];
+        }
+        const uint32_t jt = COLL ? tile_count(tile) : 0u;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (p.rowscale && j < p.M) s[j] = __fmul_rn(s[j], inv_s[j]);
+          const float up = __shfl_down_sync(0xffffffffu, s[j], 1);
+          if constexpr (COLL) {
+            if (j < p.M && n < p.N) push(jt, tile, j, n, s[j]);
+          } else if (j < p.M && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
+            epilogue_store<bf16>(p.epi, p.y, p.N, j, n, s[j], up);
+          }
+        }
+        if constexpr (COLL) coll_finish(jt, tile);
+      }
+    }
     int seg = 0;
-    int u = u0;
+    int u = CLU ? u1 : u0;  // CLU: the tile was finished above
     const int first_tile = u0 / p.KB;
     while (u < u1) {
       const int tile = u / p.KB;
@@ -603,11 +737,16 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     }
   }
 
+  if (CLU && warp < 2) cluster_wait();  // startup phase (the epilogue waited before its remote accesses)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+  if (CLU) {  // no CTA leaves while the leader may still read its shared memory
+    cluster_arrive();
+    cluster_wait();
   }
 }
 
@@ -676,21 +815,91 @@ int num_sms() {
   return n;
 }
 
+constexpr int kMaxParts = 16;  // cluster size limit (non-portable sizes above 8)
+
+// Kernel attributes, set once per instantiation and device (not on every launch).
+template <int MP, bool COLL, bool CLU>
+cudaError_t prepare_kernel() {
+  static std::mutex mu;
+  static uint64_t done = 0;  // bit d: attributes set on device d
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (done >> dev & 1ull) return cudaSuccess;
+  auto kern = linear_tc_kernel<MP, COLL, CLU>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<MP>::SMEM);
+  if (e == cudaSuccess && CLU) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) done |= 1ull << dev;
+  return e;
+}
+
+// True when `tiles` clusters of G CTAs of the M <= 16 kernel can all be resident
+// at once on this device (so the tile-split plan runs in one wave).
+bool clusters_fit(int G, int tiles) {
+  static std::mutex mu;
+  static std::unordered_map<int, int> cache;  // device * 32 + G -> max active clusters
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(dev * 32 + G);
+  if (it == cache.end()) {
+    int n = 0;
+    if (prepare_kernel<16, false, true>() == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(G * tiles);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = Cfg<16>::SMEM;
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = G;
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = 1;
+      cfg.attrs = a;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel<16, false, true>, &cfg) != cudaSuccess) n = 0;
+    }
+    (void)cudaGetLastError();
+    it = cache.emplace(dev * 32 + G, n).first;
+  }
+  return it->second >= tiles;
+}
+
+// Tile-split plan for shapes with at most half as many tiles as SMs: G parts per
+// tile (the largest G whose clusters all fit at once, else the arithmetic
+// choice through the global fold).  Depends on (N, K) and the device only, never
+// on M, so every M sums the same partials in the same order.
+int split_parts(int tiles, int KB, int sms) {
+  if (tiles * 2 > sms || KB < 2) return 0;
+  int G = sms / tiles;
+  if (G > KB) G = KB;
+  if (G > kMaxParts) G = kMaxParts;
+  for (int g = G; g >= 2; --g)
+    if (clusters_fit(g, tiles)) return g;
+  return G;
+}
+
 void plan(int M, int N, int K, int sms, Params& p, int& grid) {
   const int tiles = (N + BM - 1) / BM;
   p.KB = (K + BK - 1) / BK;
   p.U = tiles * p.KB;
+  p.G = split_parts(tiles, p.KB, sms);
+  if (p.G) {
+    grid = tiles * p.G;
+    p.base = p.rem = 0;
+    return;
+  }
   grid = p.U < sms ? p.U : sms;
   p.base = p.U / grid;
   p.rem = p.U % grid;
   (void)M;
 }
 
+// Both plans launch at most one CTA per SM, so the partial buffer is sized for
+// the SM count.
 size_t workspace_bytes(int M, int N, int K) {
-  Params p{};
-  int grid;
-  plan(M, N, K, num_sms(), p, grid);
-  return kCounterBytes + 256 + sizeof(float) * (size_t)grid * 2 * M * BM;
+  (void)N;
+  (void)K;
+  return kCounterBytes + 256 + sizeof(float) * (size_t)num_sms() * 2 * M * BM;
 }
 
 template <int MP>
@@ -728,8 +937,23 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
     p.recv_rows = ca->recv_rows;
     p.recv_tiles = ca->recv_tiles;
   }
-  auto kern = p.coll != COLL_NONE ? linear_tc_kernel<MP, true> : linear_tc_kernel<MP, false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
+  if constexpr (MP == 16) {
+    if (p.G >= 2 && clusters_fit(p.G, grid / p.G)) {
+      const bool coll = p.coll != COLL_NONE;
+      if ((coll ? prepare_kernel<16, true, true>() : prepare_kernel<16, false, true>()) != cudaSuccess)
+        return SSD_ERR_LAUNCH;
+      auto kern = coll ? linear_tc_kernel<16, true, true> : linear_tc_kernel<16, false, true>;
+      if (launch_pdl_cluster(kern, dim3(grid), dim3(kThreads), C::SMEM, st, (unsigned)p.G, wm, xm, p) !=
+          cudaSuccess) {
+        (void)cudaGetLastError();
+        return SSD_ERR_LAUNCH;
+      }
+      return SSD_OK;
+    }
+  }
+  const bool coll = p.coll != COLL_NONE;
+  auto kern = coll ? linear_tc_kernel<MP, true, false> : linear_tc_kernel<MP, false, false>;
+  if ((coll ? prepare_kernel<MP, true, false>() : prepare_kernel<MP, false, false>()) != cudaSuccess)
     return SSD_ERR_LAUNCH;
   SSD_PDL(kern, grid, kThreads, C::SMEM, st, wm, xm, p);
   SSD_CHECK_LAUNCH();

@@ -155,3 +155,36 @@ def test_rownorm_projection(cuda, dtype_name, m, n, k, epi):
         ref = acc
     tol = 2e-2 if dt == torch.bfloat16 else 1e-5
     torch.testing.assert_close(y.float(), ref, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("n,k", [(3072, 4096), (2048, 2048), (2560, 2048), (2048, 16384), (768, 2048), (3072, 128)])
+def test_tile_split_rows_match_across_m(cuda, n, k):
+    """Shapes with at most half as many 128-row output tiles as SMs cut every tile's K range into G
+    parts: for M <= 16 the G CTAs of a tile form one thread-block cluster and fold their partials in
+    distributed shared memory, for larger M the same parts go through the global ticket fold.  Every
+    row is bit-identical for M = 1, 5, 16 and 40 (plain, row-norm and residual epilogues)."""
+    import torch
+
+    from ssd_b200.kernels.ops import linear
+    from ssd_b200.workspace import workspace
+
+    g = torch.Generator(device="cuda").manual_seed(n + k)
+    x = (2.0 * torch.randn((40, k), device="cuda", generator=g)).bfloat16()
+    w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).bfloat16()
+    res = torch.randn((40, n), device="cuda", generator=g).bfloat16()
+    full = linear(x, w, "store_f32", ws_key="split_test")
+    torch.testing.assert_close(full, x.float() @ w.float().T, rtol=1e-4, atol=1e-4)
+    full_norm = linear(x, w, "store", rownorm_eps=1e-6, ws_key="split_test")
+    full_res = res.clone()
+    linear(x, w, "residual", out=full_res, ws_key="split_test")
+    for m in (1, 5, 16):
+        assert torch.equal(linear(x[:m].contiguous(), w, "store_f32", ws_key="split_test"), full[:m])
+        assert torch.equal(linear(x[:m].contiguous(), w, "store", rownorm_eps=1e-6, ws_key="split_test"),
+                           full_norm[:m])
+        r = res[:m].clone()
+        linear(x[:m].contiguous(), w, "residual", out=r, ws_key="split_test")
+        assert torch.equal(r, full_res[:m])
+    torch.cuda.synchronize()
+    head = workspace(x.device, "split_test", 0)[: 16384 * 4 + 4].view(torch.int32)
+    assert int(head[:16384].abs().sum()) == 0      # ticket counters reset
+    assert int(head[16384]) == 0                   # no device-side wait gave up

@@ -688,7 +688,7 @@ __global__ void __launch_bounds__(tma_threads<D>(), 2)
 paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16* q, int num_layers, int num_blocks,
                            int hkv, int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
                            const int32_t* q_lens, bf16* out, float scale, int T, int hq, int row_groups, int nsplit,
-                           float* ws_o, float2* ws_ml, unsigned int* counters, unsigned int* err) {
+                           float* ws_o, float2* ws_ml, unsigned int* counters, unsigned int* err, int early) {
   using S = TmaSmem<D>;
   constexpr int KSTEPS = D / 16;
   constexpr int NT = D / 8;
@@ -722,7 +722,11 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&kvmap) : "memory");
   }
-  pdl_wait();
+  // early != 0: the caller guarantees that the previous kernel in the stream
+  // writes neither the sequence lengths, q_lens, the page tables nor any K/V row
+  // below seq_len - q_len (it writes only q and this step's new rows).  Those are
+  // then read, and the pages below the new rows streamed, before waiting for it.
+  if (!early) pdl_wait();
   const int seq_len = ld_act(seq_lens + b);
   const int ql = q_lens ? ld_act(q_lens + b) : T;
   const int total_rows = G * T;
@@ -760,7 +764,13 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
     }
     __syncwarp();
     if (lane == 0 && npages > 0) {
+      const int stable_end = early ? seq_len - ql : 0;  // rows below it are not the previous kernel's
+      bool waited = !early;
       for (int j = 0; j < npages; ++j, ++issued) {
+        if (!waited && k_begin + (j + 1) * kTmaPage > stable_end) {
+          pdl_wait();
+          waited = true;
+        }
         const int st = j % S::STAGES;
         if (j >= S::STAGES && !tmb_wait(empty(st), (uint32_t)((j / S::STAGES) - 1) & 1u)) {
           s_abort = 1;
@@ -783,6 +793,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   } else {
     // ------------------------------------------------------------ consumers
     const int c = warp - 1;
+    if (early) pdl_wait();  // q (and the new K/V rows) are the previous kernel's output
     // Q rows (bf16, zero padding rows) -- consumers share this work
     for (int i = tid - 32; i < 16 * (D / 8); i += 32 * NCONS) {
       const int r = i / (D / 8), cc = i % (D / 8);
@@ -1088,20 +1099,24 @@ template <int D>
 int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks, int hkv,
                          int layer, const int32_t* tables, int max_blocks, const int32_t* seq_lens,
                          const int32_t* q_lens, void* out, float scale, int B, int T, int hq, int max_seq_len,
-                         const AttnLayout& L, void* ws) {
+                         const AttnLayout& L, void* ws, int early) {
   using S = TmaSmem<D>;
   CUtensorMap map;
   if (!kv_map_cached(&map, pages, 2 * num_layers * num_blocks, hkv, D)) return SSD_ERR_LAUNCH;
   auto kern = paged_attention_tma_kernel<D>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total) != cudaSuccess)
-    return SSD_ERR_LAUNCH;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+  });
+  if (attr_err != cudaSuccess) return SSD_ERR_LAUNCH;
   char* w = reinterpret_cast<char*>(ws);
   const int nsplit = (max_seq_len + kTmaChunk - 1) / kTmaChunk;  // <= L.nsplit: fits the workspace
   dim3 grid(nsplit, hkv * L.row_groups, B);
   SSD_PDL(kern, grid, tma_threads<D>(), S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
           layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups,
           nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
-          reinterpret_cast<unsigned int*>(w + L.off_cnt), reinterpret_cast<unsigned int*>(w + kCounterBytes));
+          reinterpret_cast<unsigned int*>(w + L.off_cnt), reinterpret_cast<unsigned int*>(w + kCounterBytes), early);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }
@@ -1144,6 +1159,16 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
                                           const int32_t* seq_lens, const int32_t* q_lens, void* out, float scale,
                                           int B, int T, int num_heads, int max_seq_len, void* workspace,
                                           size_t workspace_bytes) {
+  return ssd::paged_verify_attention_impl(stream, q, pages, dtype, num_layers, num_blocks, block_size, num_kv_heads,
+                                          head_dim, layer, block_tables, max_blocks, seq_lens, q_lens, out, scale, B,
+                                          T, num_heads, max_seq_len, workspace, workspace_bytes, 0);
+}
+
+int ssd::paged_verify_attention_impl(ssd_stream_t stream, const void* q, const void* pages, int dtype,
+                                     int num_layers, int num_blocks, int block_size, int num_kv_heads, int head_dim,
+                                     int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
+                                     const int32_t* q_lens, void* out, float scale, int B, int T, int num_heads,
+                                     int max_seq_len, void* workspace, size_t workspace_bytes, int early) {
   if (B <= 0 || T <= 0 || num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads || layer < 0 ||
       layer >= num_layers || block_size <= 0 || max_blocks <= 0 || max_seq_len <= 0 || !q || !pages || !out ||
       !block_tables || !seq_lens)
@@ -1168,7 +1193,7 @@ extern "C" int ssd_paged_verify_attention(ssd_stream_t stream, const void* q, co
 #define SSD_ATTN_TMA(DD)                                                                                        \
   return launch_attention_tma<DD>(st, q, pages, num_layers, num_blocks, num_kv_heads, layer, block_tables,      \
                                   max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, max_seq_len, L,    \
-                                  workspace)
+                                  workspace, early)
   if (dtype == SSD_DTYPE_BF16 && aligned16 && block_size == kTmaPage && (int64_t)2 * num_layers * num_blocks < (1ll << 31)) {
     if (head_dim == 256) SSD_ATTN_TMA(256);
     if (head_dim == 128) SSD_ATTN_TMA(128);

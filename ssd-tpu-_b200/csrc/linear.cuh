@@ -63,6 +63,16 @@ bool linear_tc_supported(int M, int N, int K);
 // page of one head, 64 dims wide (128-byte swizzle); D % 64 == 0.
 bool make_kv_page_map(CUtensorMap* m, const void* pages, int plane_pages, int block_size, int hkv, int D);
 
+// ssd_paged_verify_attention with `early`: nonzero when the previous kernel in
+// the stream writes only q and this step's new K/V rows (the decoder forward),
+// so that the TMA kernel may read the tables and stream the older pages before
+// waiting for it (programmatic dependent launch).
+int paged_verify_attention_impl(ssd_stream_t stream, const void* q, const void* pages, int dtype, int num_layers,
+                                int num_blocks, int block_size, int num_kv_heads, int head_dim, int layer,
+                                const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
+                                const int32_t* q_lens, void* out, float scale, int B, int T, int num_heads,
+                                int max_seq_len, void* workspace, size_t workspace_bytes, int early);
+
 // ---- tensor-parallel collectives fused into the tcgen05 projection epilogue
 constexpr int kMaxTP = 8;
 constexpr int kFlagTiles = 2048;  // output tiles (128 rows of W) per collective

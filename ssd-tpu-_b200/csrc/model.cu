@@ -381,9 +381,10 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
     SSD_TRY(ssd_rope_kv_write(stream, s.qkv, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hq, hkv, D, l,
                               bt->block_tables, bt->max_blocks, s.pos, w->rope_cos, w->rope_sin, w->rope_max_pos, B,
                               T));
-    SSD_TRY(ssd_paged_verify_attention(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
+    // early = 1: the kernel before it (RoPE + K/V write) writes only q and the new rows
+    SSD_TRY(paged_verify_attention_impl(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
                                        bt->block_tables, bt->max_blocks, s.seq_after, s.qlen, s.attn, scale, B, T,
-                                       hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes));
+                                       hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes, 1));
     SSD_TRY(proj_rowpar(1, s.attn, w->w_o[l], s.x, M, d, hq * D));
     SSD_TRY(proj(2, s.x, w->w_gate_up[l], s.act, SSD_EPI_GEGLU, M, 2 * F, d, 1));  // mlp_norm folded likewise
     SSD_TRY(proj_rowpar(3, s.act, w->w_down[l], s.x, M, d, F));

@@ -377,6 +377,12 @@ typedef struct {
    * the full vocabulary and embed the full (replicated) table, whose rows
    * [tp_rank*vocab/tp_world, ...) are this rank's LM-head block. */
   int tp_rank, tp_world;
+  /* 1: within every q and k head of w_qkv the rows are stored as rotation
+   * pairs -- row 2i holds dimension i, row 2i+1 dimension i + D/2 (v rows
+   * unchanged) -- and the forward applies RoPE and writes the K/V rows in the
+   * QKV projection's epilogue (bf16 weights only).  0: canonical row order and
+   * the separate ssd_rope_kv_write step. */
+  int qk_pairs;
 } ssd_gemma_weights;
 
 typedef struct {

@@ -96,6 +96,25 @@ struct CollArgs {
   int recv_rows, recv_tiles;  // all-reduce: receive slots [2][recv_tiles][world][recv_rows][128] (fp32 | count << 32)
 };
 
+// QKV projection epilogue with RoPE and the K/V page write (weights with q/k
+// rows stored as rotation pairs, see ssd_gemma_weights.qk_pairs): the rounded
+// q values are rotated into q_out [M, hq, D], k rotated and v copied into the
+// token's page slot, exactly as ssd_rope_kv_write does from a stored qkv row.
+struct RopeArgs {
+  bf16* q_out;
+  bf16* pages;
+  const int32_t* pos;     // [M] token positions (-1: no K/V write)
+  const int32_t* tables;  // [B, max_blocks]
+  const float* cos_t;     // [rope_max_pos, D/2]
+  const float* sin_t;
+  int64_t plane;          // elements of one K (or V) plane: layers * blocks * block_size * hkv * D
+  int layer, num_blocks, block_size, max_blocks, hq, hkv, D, T, rope_max_pos;
+};
+constexpr int kEpiRopeQkv = 100;  // internal epilogue code (not part of the C ABI)
+
+int linear_tc_rope(cudaStream_t st, const void* x, const void* w, int M, int N, int K, void* ws, size_t ws_bytes,
+                   float eps, const RopeArgs& ra);
+
 // mode ALLREDUCE: y[M,N] (bf16, residual in/out) += round(sum over ranks of x_r w_r^T)
 // mode ALLGATHER: out[M, col_off .. col_off+N) = x w^T (fp32), written on every rank
 int linear_tc_coll(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,

@@ -19,8 +19,8 @@
 //     (atomic ticket), which sums the fp32 partials in CTA (= K) order, so the
 //     result is deterministic and, because the unit split depends on (N, K) and
 //     the SM count only, independent of M.
-//   * shapes with at most half as many tiles as SMs use a tile-split plan
-//     instead: G CTAs per tile, each one contiguous part of its k-blocks; for
+//   * shapes with at most as many tiles as SMs use a tile-split plan instead:
+//     G CTAs per tile (up to two per SM), each one contiguous part of its k-blocks; for
 //     M <= 16 they run as one thread-block cluster and fold in distributed
 //     shared memory (see linear_tc_kernel's CLU parameter).
 // Every mbarrier wait is bounded: on timeout the kernel records an error code,
@@ -83,6 +83,7 @@ struct Params {
   int coll, rank, world, ldy, col_off, recv_rows, recv_tiles;
   char* heaps[kMaxTP];
   size_t ctrl_off, dst_off;
+  RopeArgs rope;  // epi == kEpiRopeQkv
 };
 
 // First unit of CTA c.  Stream-K: contiguous ranges of base or base + 1 units.
@@ -289,11 +290,55 @@ struct Cfg {
   // share the SM and prefetch its weights while this one drains (PDL).
   static constexpr int STAGES = MP <= 16 ? 6 : MP <= 32 ? 5 : MP <= 64 ? 8 : MP <= 128 ? 6 : 4;
   static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;
-  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16 + 4 * 256;  // + row scales
+  // barriers, TMEM slot and flags, row scales [256], RoPE row info [MP] (int + int64)
+  static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16 + 4 * 256 + 12 * MP;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// kEpiRopeQkv: output (m, n) of the QKV projection with rotation-paired q/k rows;
+// `pair` is the accumulator of row n ^ 1 (the other half of the rotation pair).
+// Row m's table position (clamped) and the element offset of its K row in the
+// pages (-1: no K/V write), computed once per CTA into shared memory.
+__device__ __forceinline__ void rope_row_info(const RopeArgs& r, int m, int* pc, long long* off) {
+  const int p = ld_act(r.pos + m);
+  long long o = -1;
+  if (p >= 0 && p / r.block_size < r.max_blocks) {
+    const int blk = ld_act(r.tables + (int64_t)(m / r.T) * r.max_blocks + p / r.block_size);
+    if ((unsigned)blk < (unsigned)r.num_blocks)
+      o = (((long long)r.layer * r.num_blocks + blk) * r.block_size + p % r.block_size) * r.hkv * r.D;
+  }
+  pc[m] = p < 0 ? 0 : min(p, r.rope_max_pos - 1);
+  off[m] = o;
+}
+
+__device__ __forceinline__ void rope_qkv_store(const RopeArgs& r, int m, int n, float acc, float pair, int pc,
+                                               long long off) {
+  const int D = r.D, half = D >> 1, qk = (r.hq + r.hkv) * D;
+  if (n < qk) {
+    const int h = n / D, rr = n - h * D, i = rr >> 1;
+    const bool odd = rr & 1;
+    // the stored (bf16) q/k values, as the separate RoPE step reads them
+    const float self = store_round<bf16>(acc), other = store_round<bf16>(pair);
+    const float x1 = odd ? other : self, x2 = odd ? self : other;
+    const float c = __ldg(r.cos_t + (int64_t)pc * half + i), sn = __ldg(r.sin_t + (int64_t)pc * half + i);
+    const float y = odd ? __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn)) : __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+    const int dim = i + (odd ? half : 0);
+    if (h < r.hq) r.q_out[((int64_t)m * r.hq + h) * D + dim] = from_f<bf16>(y);
+    else if (off >= 0) r.pages[off + (long long)(h - r.hq) * D + dim] = from_f<bf16>(y);
+  } else if (off >= 0) {
+    r.pages[r.plane + off + (n - qk)] = from_f<bf16>(acc);
+  }
+}
+
+// every non-collective output store of the kernel
+template <bool ROPE>
+__device__ __forceinline__ void store_out(const Params& p, int m, int n, float acc, float pair, const int* rpc,
+                                          const long long* roff) {
+  if constexpr (ROPE) rope_qkv_store(p.rope, m, n, acc, pair, rpc[m], roff[m]);
+  else if (!(p.epi == SSD_EPI_GEGLU && (n & 1))) epilogue_store<bf16>(p.epi, p.y, p.N, m, n, acc, pair);
+}
 
 // COLL: instantiate the fused-collective epilogue (p.coll != COLL_NONE); the
 // plain projection is compiled without it so that its code stays small.
@@ -303,8 +348,12 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // its fp32 partial in its own (idle) ring and arrives on the leader's mbarrier;
 // the leader folds its own accumulator and the peers' partials in part (= K)
 // order -- the same sums as the global fold, with no ticket and no L2 round trips.
-template <int MP, bool COLL, bool CLU>
-__global__ void __launch_bounds__(kThreads)
+// ROPE: the QKV projection's epilogue applies RoPE and writes the K/V rows
+// (epi == kEpiRopeQkv); its own instantiation, so the plain kernels stay small.
+// The collective and RoPE instantiations declare one resident CTA per SM as the
+// minimum (two still fit): without it ptxas held them to 96 registers and spilled.
+template <int MP, bool COLL, bool CLU, bool ROPE>
+__global__ void __launch_bounds__(kThreads, (COLL || ROPE) ? 1 : 0)
 linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const Params p) {
   using C = Cfg<MP>;
@@ -323,6 +372,8 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* inv_s = reinterpret_cast<float*>(tmem_slot + 4);  // [M] row scales
+  int* rope_pc = reinterpret_cast<int*>(inv_s + 256);      // ROPE: [MP] positions, then [MP] K-row offsets
+  long long* rope_off = reinterpret_cast<long long*>(rope_pc + MP);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -567,6 +618,12 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       }
       epi_bar();
     }
+    if constexpr (ROPE) {
+      if (!CLU || cluster_ctarank() == 0) {  // the CTAs that store outputs
+        for (int m = (int)threadIdx.x - 64; m < p.M; m += kEpiThreads) rope_row_info(p.rope, m, rope_pc, rope_off);
+        epi_bar();
+      }
+    }
     if constexpr (CLU) {
       // ------------------------------------------------ cluster fold (one tile)
       cluster_wait();  // startup phase: every CTA of the cluster has initialised its barriers
@@ -622,11 +679,11 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           if (p.rowscale && j < p.M) s[j] = __fmul_rn(s[j], inv_s[j]);
-          const float up = __shfl_down_sync(0xffffffffu, s[j], 1);
+          const float up = __shfl_xor_sync(0xffffffffu, s[j], 1);  // row n ^ 1 (GeGLU up, RoPE pair)
           if constexpr (COLL) {
             if (j < p.M && n < p.N) push(jt, tile, j, n, s[j]);
-          } else if (j < p.M && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
-            epilogue_store<bf16>(p.epi, p.y, p.N, j, n, s[j], up);
+          } else if (j < p.M && n < p.N) {
+            store_out<ROPE>(p, j, n, s[j], up, rope_pc, rope_off);
           }
         }
         if constexpr (COLL) coll_finish(jt, tile);
@@ -661,13 +718,13 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         for (int j = 0; j < 16; ++j) {
           const int m = c0 + j;
           if (whole && p.rowscale && m < p.M) v[j] = __fmul_rn(v[j], inv_s[m]);
-          const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
+          const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);  // row n ^ 1 (GeGLU up, RoPE pair)
           if (m >= p.M) continue;
           if (whole) {
             if constexpr (COLL) {
               if (n < p.N) push(jt_whole, tile, m, n, v[j]);
-            } else if (n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
-              epilogue_store<bf16>(p.epi, p.y, p.N, m, n, v[j], up);
+            } else if (n < p.N) {
+              store_out<ROPE>(p, m, n, v[j], up, rope_pc, rope_off);
             }
           } else {
             mine[(size_t)m * BM + row] = v[j];
@@ -725,11 +782,11 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           if (p.rowscale && i < mn) s[i] = __fmul_rn(s[i], inv_s[m0 + i]);
-          const float up = __shfl_down_sync(0xffffffffu, s[i], 1);
+          const float up = __shfl_xor_sync(0xffffffffu, s[i], 1);  // row n ^ 1 (GeGLU up, RoPE pair)
           if constexpr (COLL) {
             if (i < mn && n < p.N) push(jt, tile, m0 + i, n, s[i]);
-          } else if (i < mn && n < p.N && !(p.epi == SSD_EPI_GEGLU && (n & 1))) {
-            epilogue_store<bf16>(p.epi, p.y, p.N, m0 + i, n, s[i], up);
+          } else if (i < mn && n < p.N) {
+            store_out<ROPE>(p, m0 + i, n, s[i], up, rope_pc, rope_off);
           }
         }
       }
@@ -818,7 +875,7 @@ int num_sms() {
 constexpr int kMaxParts = 16;  // cluster size limit (non-portable sizes above 8)
 
 // Kernel attributes, set once per instantiation and device (not on every launch).
-template <int MP, bool COLL, bool CLU>
+template <int MP, bool COLL, bool CLU, bool ROPE>
 cudaError_t prepare_kernel() {
   static std::mutex mu;
   static uint64_t done = 0;  // bit d: attributes set on device d
@@ -826,7 +883,7 @@ cudaError_t prepare_kernel() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> g(mu);
   if (done >> dev & 1ull) return cudaSuccess;
-  auto kern = linear_tc_kernel<MP, COLL, CLU>;
+  auto kern = linear_tc_kernel<MP, COLL, CLU, ROPE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<MP>::SMEM);
   if (e == cudaSuccess && CLU) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e == cudaSuccess) done |= 1ull << dev;
@@ -844,7 +901,7 @@ bool clusters_fit(int G, int tiles) {
   auto it = cache.find(dev * 32 + G);
   if (it == cache.end()) {
     int n = 0;
-    if (prepare_kernel<16, false, true>() == cudaSuccess) {
+    if (prepare_kernel<16, false, true, false>() == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(G * tiles);
       cfg.blockDim = dim3(kThreads);
@@ -856,7 +913,7 @@ bool clusters_fit(int G, int tiles) {
       a[0].val.clusterDim.z = 1;
       cfg.attrs = a;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel<16, false, true>, &cfg) != cudaSuccess) n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel<16, false, true, false>, &cfg) != cudaSuccess) n = 0;
     }
     (void)cudaGetLastError();
     it = cache.emplace(dev * 32 + G, n).first;
@@ -864,13 +921,13 @@ bool clusters_fit(int G, int tiles) {
   return it->second >= tiles;
 }
 
-// Tile-split plan for shapes with at most half as many tiles as SMs: G parts per
-// tile (the largest G whose clusters all fit at once, else the arithmetic
-// choice through the global fold).  Depends on (N, K) and the device only, never
+// Tile-split plan for shapes with at most as many tiles as SMs: G parts per tile,
+// up to two CTAs per SM (the largest G whose clusters all fit at once, else the
+// arithmetic choice through the global fold).  Depends on (N, K) and the device only, never
 // on M, so every M sums the same partials in the same order.
 int split_parts(int tiles, int KB, int sms) {
-  if (tiles * 2 > sms || KB < 2) return 0;
-  int G = sms / tiles;
+  if (tiles > sms || KB < 2) return 0;
+  int G = (2 * sms) / tiles;
   if (G > KB) G = KB;
   if (G > kMaxParts) G = kMaxParts;
   for (int g = G; g >= 2; --g)
@@ -894,17 +951,17 @@ void plan(int M, int N, int K, int sms, Params& p, int& grid) {
   (void)M;
 }
 
-// Both plans launch at most one CTA per SM, so the partial buffer is sized for
-// the SM count.
+// Stream-K launches one CTA per SM, the tile-split plan up to two: the partial
+// buffer [grid][2][M][BM] is sized for twice the SM count.
 size_t workspace_bytes(int M, int N, int K) {
   (void)N;
   (void)K;
-  return kCounterBytes + 256 + sizeof(float) * (size_t)num_sms() * 2 * M * BM;
+  return kCounterBytes + 256 + sizeof(float) * (size_t)num_sms() * 4 * M * BM;
 }
 
 template <int MP>
 int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int M, int N, int K, void* ws,
-           int rowscale, float eps, const CollArgs* ca) {
+           int rowscale, float eps, const CollArgs* ca, const RopeArgs* ra) {
   using C = Cfg<MP>;
   CUtensorMap wm, xm;
   if (!weight_map(&wm, w, N, K)) return SSD_ERR_LAUNCH;
@@ -925,6 +982,7 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   p.err = reinterpret_cast<unsigned int*>(wsb + kCounterBytes);
   p.part = reinterpret_cast<float*>(wsb + kCounterBytes + 256);
   p.coll = COLL_NONE;
+  if (ra) p.rope = *ra;
   if (ca && ca->mode != COLL_NONE) {
     p.coll = ca->mode;
     p.rank = ca->rank;
@@ -939,10 +997,13 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   }
   if constexpr (MP == 16) {
     if (p.G >= 2 && clusters_fit(p.G, grid / p.G)) {
-      const bool coll = p.coll != COLL_NONE;
-      if ((coll ? prepare_kernel<16, true, true>() : prepare_kernel<16, false, true>()) != cudaSuccess)
+      const bool coll = p.coll != COLL_NONE, rope = epi == kEpiRopeQkv;
+      if ((coll ? prepare_kernel<16, true, true, false>()
+                : rope ? prepare_kernel<16, false, true, true>() : prepare_kernel<16, false, true, false>()) !=
+          cudaSuccess)
         return SSD_ERR_LAUNCH;
-      auto kern = coll ? linear_tc_kernel<16, true, true> : linear_tc_kernel<16, false, true>;
+      auto kern = coll ? linear_tc_kernel<16, true, true, false>
+                       : rope ? linear_tc_kernel<16, false, true, true> : linear_tc_kernel<16, false, true, false>;
       if (launch_pdl_cluster(kern, dim3(grid), dim3(kThreads), C::SMEM, st, (unsigned)p.G, wm, xm, p) !=
           cudaSuccess) {
         (void)cudaGetLastError();
@@ -951,9 +1012,12 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
       return SSD_OK;
     }
   }
-  const bool coll = p.coll != COLL_NONE;
-  auto kern = coll ? linear_tc_kernel<MP, true, false> : linear_tc_kernel<MP, false, false>;
-  if ((coll ? prepare_kernel<MP, true, false>() : prepare_kernel<MP, false, false>()) != cudaSuccess)
+  const bool coll = p.coll != COLL_NONE, rope = epi == kEpiRopeQkv;
+  auto kern = coll ? linear_tc_kernel<MP, true, false, false>
+                   : rope ? linear_tc_kernel<MP, false, false, true> : linear_tc_kernel<MP, false, false, false>;
+  if ((coll ? prepare_kernel<MP, true, false, false>()
+            : rope ? prepare_kernel<MP, false, false, true> () : prepare_kernel<MP, false, false, false>()) !=
+      cudaSuccess)
     return SSD_ERR_LAUNCH;
   SSD_PDL(kern, grid, kThreads, C::SMEM, st, wm, xm, p);
   SSD_CHECK_LAUNCH();
@@ -996,7 +1060,17 @@ int linear_tc(cudaStream_t st, const void* x, const void* w, void* y, int epi, i
               size_t ws_bytes, int rowscale, float eps) {
   if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
-  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, rowscale, eps, (const CollArgs*)nullptr);
+  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, rowscale, eps, (const CollArgs*)nullptr,
+                        (const RopeArgs*)nullptr);
+}
+
+int linear_tc_rope(cudaStream_t st, const void* x, const void* w, int M, int N, int K, void* ws, size_t ws_bytes,
+                   float eps, const RopeArgs& ra) {
+  if (!linear_tc_supported(M, N, K)) return SSD_ERR_UNSUPPORTED;
+  if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
+  if (ra.D <= 0 || (ra.D & 1) || N != (ra.hq + 2 * ra.hkv) * ra.D || ra.T <= 0 || M % ra.T) return SSD_ERR_INVALID;
+  return tc::launch_any(M, st, x, w, nullptr, kEpiRopeQkv, M, N, K, ws, 1, eps, (const CollArgs*)nullptr, &ra);
 }
 
 int linear_tc_coll(cudaStream_t st, const void* x, const void* w, void* y, int M, int N, int K, void* ws,
@@ -1006,7 +1080,7 @@ int linear_tc_coll(cudaStream_t st, const void* x, const void* w, void* y, int M
   if (!ws || ws_bytes < tc::workspace_bytes(M, N, K)) return SSD_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return SSD_ERR_UNSUPPORTED;
   const int epi = ca.mode == COLL_ALLREDUCE ? SSD_EPI_RESIDUAL : SSD_EPI_STORE_F32;
-  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, 0, 0.f, &ca);
+  return tc::launch_any(M, st, x, w, y, epi, M, N, K, ws, 0, 0.f, &ca, (const RopeArgs*)nullptr);
 }
 
 }  // namespace ssd

@@ -289,6 +289,9 @@ static bool weights_ok(const ssd_gemma_weights* w) {
     if (!w->w_qkv[l] || !w->w_o[l] || !w->w_gate_up[l] || !w->w_down[l]) return false;
   if (w->tp_world < 0 || w->tp_world > SSD_MAX_TP || w->tp_rank < 0 || (w->tp_world > 1 && w->tp_rank >= w->tp_world))
     return false;
+  if (w->qk_pairs && (w->dtype != SSD_DTYPE_BF16 || (w->head_dim & 1) ||
+                      !linear_tc_supported(max_m(), (w->num_heads + 2 * w->num_kv_heads) * w->head_dim, w->d_model)))
+    return false;
   return true;
 }
 
@@ -377,11 +380,36 @@ extern "C" int ssd_gemma_forward(ssd_stream_t stream, const ssd_gemma_weights* w
   for (int l = 0; l < L; ++l) {
     // RMSNorm folded: w_qkv carries (1 + attn_norm) in its columns, the projection
     // scales each token row by its rsqrt(mean(x^2) + eps)
-    SSD_TRY(proj(0, s.x, w->w_qkv[l], s.qkv, SSD_EPI_STORE, M, (hq + 2 * hkv) * D, d, 1));
-    SSD_TRY(ssd_rope_kv_write(stream, s.qkv, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hq, hkv, D, l,
-                              bt->block_tables, bt->max_blocks, s.pos, w->rope_cos, w->rope_sin, w->rope_max_pos, B,
-                              T));
-    // early = 1: the kernel before it (RoPE + K/V write) writes only q and the new rows
+    if (w->qk_pairs) {
+      // RoPE and the K/V page write in the projection's epilogue (q/k rows stored as rotation pairs)
+      RopeArgs ra;
+      ra.q_out = reinterpret_cast<bf16*>(s.q);
+      ra.pages = reinterpret_cast<bf16*>(bt->kv_pages);
+      ra.pos = s.pos;
+      ra.tables = bt->block_tables;
+      ra.cos_t = w->rope_cos;
+      ra.sin_t = w->rope_sin;
+      ra.plane = (int64_t)L * bt->num_blocks * bt->block_size * hkv * D;
+      ra.layer = l;
+      ra.num_blocks = bt->num_blocks;
+      ra.block_size = bt->block_size;
+      ra.max_blocks = bt->max_blocks;
+      ra.hq = hq;
+      ra.hkv = hkv;
+      ra.D = D;
+      ra.T = T;
+      ra.rope_max_pos = w->rope_max_pos;
+      SSD_TRY(timed(0, [&] {
+        return linear_tc_rope(st, s.x, w->w_qkv[l], M, (hq + 2 * hkv) * D, d, s.lin_ws, s.lin_ws_bytes, w->eps, ra);
+      }));
+    } else {
+      SSD_TRY(proj(0, s.x, w->w_qkv[l], s.qkv, SSD_EPI_STORE, M, (hq + 2 * hkv) * D, d, 1));
+      SSD_TRY(ssd_rope_kv_write(stream, s.qkv, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hq, hkv, D,
+                                l, bt->block_tables, bt->max_blocks, s.pos, w->rope_cos, w->rope_sin,
+                                w->rope_max_pos, B, T));
+    }
+    // early = 1: the kernel before it (RoPE + K/V write, or the QKV projection that
+    // does them) writes only q and the new rows
     SSD_TRY(paged_verify_attention_impl(stream, s.q, bt->kv_pages, dt, L, bt->num_blocks, bt->block_size, hkv, D, l,
                                        bt->block_tables, bt->max_blocks, s.seq_after, s.qlen, s.attn, scale, B, T,
                                        hq, bt->max_seq_len, s.attn_ws, s.attn_ws_bytes, 1));

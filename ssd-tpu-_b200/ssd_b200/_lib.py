@@ -90,7 +90,7 @@ class GemmaWeightsC(C.Structure):
         ("embed", _p), ("final_norm", _p),
         ("w_qkv", C.POINTER(_p)), ("w_o", C.POINTER(_p)), ("w_gate_up", C.POINTER(_p)), ("w_down", C.POINTER(_p)),
         ("rope_cos", _p), ("rope_sin", _p), ("rope_max_pos", _i),
-        ("tp_rank", _i), ("tp_world", _i),
+        ("tp_rank", _i), ("tp_world", _i), ("qk_pairs", _i),
     ]
 
 

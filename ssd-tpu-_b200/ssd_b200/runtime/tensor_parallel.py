@@ -169,4 +169,5 @@ def shard_weights(full, rank: int, world: int):
         w.mlp_norm[l] = full.mlp_norm[l]
     w.rope_cos, w.rope_sin = full.rope_cos, full.rope_sin
     w.tp_rank, w.tp_world = rank, world
+    w.qk_pairs = full.qk_pairs  # head blocks of rotation-paired rows stay paired
     return w

@@ -157,9 +157,10 @@ def test_rownorm_projection(cuda, dtype_name, m, n, k, epi):
     torch.testing.assert_close(y.float(), ref, rtol=tol, atol=tol)
 
 
-@pytest.mark.parametrize("n,k", [(3072, 4096), (2048, 2048), (2560, 2048), (2048, 16384), (768, 2048), (3072, 128)])
+@pytest.mark.parametrize("n,k", [(3072, 4096), (2048, 2048), (2560, 2048), (2048, 16384), (768, 2048), (3072, 128),
+                                 (12288, 3072)])
 def test_tile_split_rows_match_across_m(cuda, n, k):
-    """Shapes with at most half as many 128-row output tiles as SMs cut every tile's K range into G
+    """Shapes with at most as many 128-row output tiles as SMs cut every tile's K range into G
     parts: for M <= 16 the G CTAs of a tile form one thread-block cluster and fold their partials in
     distributed shared memory, for larger M the same parts go through the global ticket fold.  Every
     row is bit-identical for M = 1, 5, 16 and 40 (plain, row-norm and residual epilogues)."""

@@ -64,6 +64,8 @@ def parse():
                     help="> 0: batched serving workload (B sequences, --k drafts, --temperature, contexts "
                          "U[--ctx-min, --ctx-max]); prints its own JSON line instead of the decode-loop line")
     ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--top-p", dest="top_p", type=float, default=0.95,
+                    help="batched mode: top-p nucleus of the draft and target distributions (1 = off)")
     ap.add_argument("--ctx-min", type=int, default=1024)
     ap.add_argument("--ctx-max", type=int, default=8192)
     ap.add_argument("--attn", choices=["2a", "decode7b", "decode2b"], default="2a",
@@ -582,7 +584,8 @@ def run_batched(args):
     max_seq = args.ctx_max + grow + 16
     blocks = sum((c + grow + 15) // 16 + 1 for c in ctx) + 2
     dec = BatchedSpeculativeDecoder(target, draft, batch=B, k=k, max_seq_len=max_seq,
-                                    temperature=args.temperature, seed=7, comm=comm, num_blocks=blocks)
+                                    temperature=args.temperature, top_p=args.top_p, seed=7, comm=comm,
+                                    num_blocks=blocks)
     dec.start_synthetic(ctx, np.random.default_rng(1))
     for _ in range(args.warmup):
         dec.step()
@@ -627,7 +630,8 @@ def run_batched(args):
             "scaling": "strong" if world > 1 else "n/a", "dtype": "bf16",
             "data": "synthetic (random-init weights; contexts stood in by seeded N(0,1) K/V)",
             "config": {"workload": f"batched serving B={B}, k={k}, T={args.temperature}, ctx U[{args.ctx_min}, "
-                                   f"{args.ctx_max}]", "parallelism": f"tp{world}", "top_p": None},
+                                   f"{args.ctx_max}]", "parallelism": f"tp{world}",
+                       "top_p": args.top_p if args.temperature > 0 and args.top_p < 1 else None},
             "tokens_per_step": tokens / args.steps, "accept_rate": None,
             "verify_ms": statistics.mean(verify_ms),
             "step_bytes_per_rank": step_bytes, "step_hbm_gbs": step_bytes / step_s / 1e9,

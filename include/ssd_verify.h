@@ -110,6 +110,18 @@ int ssd_argmax_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, i
 int ssd_sample_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, int V, float temperature,
                     uint64_t seed, uint64_t offset, int32_t* out, void* workspace, size_t workspace_bytes);
 
+/*
+ * Top-p (nucleus) filter of softmax(x[r] / temperature), in place: every
+ * logit below the row's cutoff t* (and every NaN) becomes -inf, so the
+ * sampling and acceptance kernels above see the renormalised nucleus.  t* is
+ * the largest logit value whose cumulative mass -- over all logits >= it,
+ * ties included, fp64 masses exp((x - max) / temperature) -- reaches
+ * top_p * Z.  top_p >= 1 leaves the rows untouched.  Not in the reference (its
+ * SamplingParams has no top-p); the batched serving workload (T = 1.0,
+ * top-p 0.95) asks for it.  No workspace.
+ */
+int ssd_top_p_mask(ssd_stream_t stream, float* x, int64_t ld, int rows, int V, float temperature, float top_p);
+
 /* Workspace bytes for ssd_verify_sample. */
 size_t ssd_verify_sample_workspace_size(int B, int K, int V);
 

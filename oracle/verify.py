@@ -42,6 +42,45 @@ def softmax(x: np.ndarray) -> np.ndarray:
     return (e / e.sum(axis=-1, keepdims=True, dtype=np.float32)).astype(np.float32)
 
 
+def top_p_threshold(x: np.ndarray, temperature: float, top_p: float):
+    """Cutoff of the top-p nucleus of softmax(x / T) for one row (fp32 logits).
+
+    Not in the reference (its SamplingParams has no top-p); restates the
+    definition ``ssd_top_p_mask`` implements: fp64 masses w = exp(-(m - x) / T)
+    over the finite logits, sorted by value (descending); the cutoff is the
+    value at which the running mass first reaches top_p * Z, so every logit
+    >= it (ties included) is kept.  None: no finite logit.
+    """
+    v = np.asarray(x, dtype=np.float32)
+    fin = v > -np.inf  # False for -inf and NaN
+    if not fin.any():
+        return None
+    vals = v[fin].astype(np.float64)
+    m = vals.max()
+    inv_t = 1.0 / float(np.float32(temperature))
+    w = np.exp(-((m - vals) * inv_t))
+    order = np.argsort(-vals, kind="stable")
+    cum = np.cumsum(w[order])
+    i = int(np.searchsorted(cum, top_p * w.sum(), side="left"))
+    if i >= len(vals):
+        return np.float32(-np.inf)
+    return np.float32(vals[order][i])
+
+
+def top_p_mask(x: np.ndarray, temperature: float, top_p: float) -> np.ndarray:
+    """Copy of logits [..., V] with every value below its row's top-p cutoff (and NaN) set to -inf."""
+    out = np.array(x, dtype=np.float32, copy=True)
+    if top_p >= 1.0:
+        return out
+    rows = out.reshape(-1, out.shape[-1])
+    for r in rows:
+        t = top_p_threshold(r, temperature, top_p)
+        if t is None:
+            continue
+        r[~(r >= t)] = -np.inf
+    return out
+
+
 def verify_sample(
     logits_p: np.ndarray,
     logits_q: np.ndarray,

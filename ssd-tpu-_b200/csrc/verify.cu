@@ -185,7 +185,7 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   auto push = [&](float x) {
     const float v = __fdiv_rn(x, temp);
     if (v > m) { s = (m == -INFINITY ? 0.f : s * expf(__fsub_rn(m, v))) + 1.f; m = v; }
-    else s += expf(__fsub_rn(v, m));
+    else if (v > -INFINITY) s += expf(__fsub_rn(v, m));  // a masked (-inf) logit adds nothing
   };
   if (vec_ok) {
     const int nv = (hi - lo) >> 2;
@@ -326,6 +326,143 @@ sample_draw_kernel(const float* lp, const float* lq,
       for (int j = 0; j < K; ++j) mask[(int64_t)b * (K + 1) + j + 1] = (j < d.acc) ? 1 : 0;
     }
   }
+}
+
+// ---------------------------------------------------------------- top-p (nucleus) mask
+// One CTA per row.  The nucleus of softmax(x / T) at mass p is {x >= t*}, t* the
+// largest logit value whose cumulative mass (all logits >= it, ties included)
+// reaches p * Z.  Masses are fp64: w = exp(-(m - x) / T), m the row max.
+//   1. m;
+//   2. histogram of d = (m - x) / T over [0, 32) nats in 2048 bins of 1/64 nat
+//      (counts and fp64 masses); logits further down add to a tail sum only;
+//   3. the cutoff bin: the first bin, walking down from the max, at which the
+//      running mass reaches p * Z;
+//   4. its logits are compacted into shared memory and sorted (descending); the
+//      walk continues through them to the exact t*;
+//   5. every logit below t* (and every NaN) becomes -inf, in place.
+// A cutoff in the tail (p within e^-32 * V / Z of 1) keeps every finite logit;
+// a cutoff bin holding more than kTopPCap logits is kept whole.
+constexpr int kTopPThreads = 1024;
+constexpr int kTopPBins = 2048;
+constexpr double kTopPBinsPerNat = 64.0;
+constexpr int kTopPCap = 4096;
+
+__global__ void __launch_bounds__(kTopPThreads)
+top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
+  __shared__ unsigned int cnt[kTopPBins];
+  __shared__ double mass[kTopPBins];
+  __shared__ float cand[kTopPCap];
+  __shared__ float redf[32];
+  __shared__ double redd[32];
+  __shared__ int s_bin, s_ncand;
+  __shared__ double s_above, s_target;
+  __shared__ float s_t;
+  pdl_wait();
+  float* row = x + (int64_t)blockIdx.x * ld;
+  float mloc = -INFINITY;
+  for (int j = threadIdx.x; j < V; j += kTopPThreads) mloc = fmaxf(mloc, __ldcg(row + j));  // fmaxf skips NaN
+  const float m = block_reduce(mloc, redf, OpMax());
+  if (!(m > -INFINITY)) {  // no finite logit: nothing to rank
+    pdl_trigger();
+    return;
+  }
+  const double md = (double)m;
+  for (int i = threadIdx.x; i < kTopPBins; i += kTopPThreads) {
+    cnt[i] = 0u;
+    mass[i] = 0.0;
+  }
+  if (threadIdx.x == 0) s_ncand = 0;
+  __syncthreads();
+  double tail = 0.0;
+  for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+    const float v = __ldcg(row + j);
+    if (!(v > -INFINITY)) continue;  // -inf and NaN carry no mass
+    const double d = (md - (double)v) * inv_t;
+    const double w = exp(-d);
+    const int bin = (int)(d * kTopPBinsPerNat);
+    if (bin < kTopPBins) {
+      atomicAdd(&cnt[bin], 1u);
+      atomicAdd(&mass[bin], w);
+    } else {
+      tail += w;
+    }
+  }
+  tail = block_reduce(tail, redd, OpSum());
+  if (threadIdx.x == 0) {
+    double Z = tail;
+    for (int i = kTopPBins - 1; i >= 0; --i) Z += mass[i];
+    const double target = top_p * Z;
+    double cum = 0.0;
+    int b = 0;
+    for (; b < kTopPBins; ++b) {
+      if (cum + mass[b] >= target) break;
+      cum += mass[b];
+    }
+    s_bin = b < kTopPBins ? b : -1;
+    s_above = cum;
+    s_target = target;
+    s_t = -INFINITY;  // cutoff in the tail: keep every finite logit
+  }
+  __syncthreads();
+  const int b = s_bin;
+  if (b >= 0) {
+    const unsigned int n = cnt[b];
+    if (n > (unsigned)kTopPCap) {
+      // too many logits near the cutoff to sort here: keep the whole bin
+      if (threadIdx.x == 0) s_t = (float)(md - ((double)(b + 1) / kTopPBinsPerNat) / inv_t);
+    } else {
+      for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+        const float v = __ldcg(row + j);
+        if (!(v > -INFINITY)) continue;
+        const double d = (md - (double)v) * inv_t;
+        if ((int)(d * kTopPBinsPerNat) == b) {
+          const int k = atomicAdd(&s_ncand, 1);
+          if (k < kTopPCap) cand[k] = v;
+        }
+      }
+      __syncthreads();
+      int np2 = 1;
+      while (np2 < (int)n) np2 <<= 1;
+      for (int i = (int)n + threadIdx.x; i < np2; i += kTopPThreads) cand[i] = -INFINITY;
+      __syncthreads();
+      // bitonic sort, descending
+      for (int size = 2; size <= np2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int i = threadIdx.x; i < np2; i += kTopPThreads) {
+            const int jx = i ^ stride;
+            if (jx > i) {
+              const bool desc = (i & size) == 0;
+              const float a = cand[i], c = cand[jx];
+              if (desc ? (a < c) : (a > c)) {
+                cand[i] = c;
+                cand[jx] = a;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+      if (threadIdx.x == 0) {
+        double cum = s_above;
+        float t = n > 0 ? cand[n - 1] : -INFINITY;
+        for (unsigned int i = 0; i < n; ++i) {
+          cum += exp(-(md - (double)cand[i]) * inv_t);
+          if (cum >= s_target) {
+            t = cand[i];
+            break;
+          }
+        }
+        s_t = t;
+      }
+    }
+  }
+  __syncthreads();
+  const float t = s_t;
+  for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+    const float v = __ldcg(row + j);
+    if (!(v >= t)) row[j] = -INFINITY;
+  }
+  pdl_trigger();
 }
 
 // ---------------------------------------------------------------- RNG fills
@@ -521,6 +658,16 @@ extern "C" int ssd_sample_rows(ssd_stream_t stream, const float* x, int64_t ld, 
   cudaStream_t st = (cudaStream_t)stream;
   SSD_PDL(sample_rows_kernel, dim3(nch, rows), kScanThreads, 0, st, x, ld, V, nch, 1.0f / temperature, seed, offset,
           counters, part, out);
+  SSD_CHECK_LAUNCH();
+  return SSD_OK;
+}
+
+extern "C" int ssd_top_p_mask(ssd_stream_t stream, float* x, int64_t ld, int rows, int V, float temperature,
+                              float top_p) {
+  if (rows <= 0 || V <= 0 || ld < V || !x || !(temperature > 0.f) || !(top_p > 0.f)) return SSD_ERR_INVALID;
+  if (top_p >= 1.0f) return SSD_OK;  // the whole distribution
+  cudaStream_t st = (cudaStream_t)stream;
+  SSD_PDL(top_p_mask_kernel, dim3(rows), kTopPThreads, 0, st, x, ld, V, 1.0 / (double)temperature, (double)top_p);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }

@@ -37,6 +37,7 @@ SIGNATURES = {
     "ssd_verify_greedy_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i]),
     "ssd_argmax_rows": (_i, [_p, _p, _i64, _i, _i, _p, _p, _sz]),
     "ssd_sample_rows": (_i, [_p, _p, _i64, _i, _i, _f, _u64, _u64, _p, _p, _sz]),
+    "ssd_top_p_mask": (_i, [_p, _p, _i64, _i, _i, _f, _f]),
     "ssd_verify_sample_workspace_size": (_sz, [_i, _i, _i]),
     "ssd_verify_sample": (_i, [_p, _p, _p, _p, _p, _p, _f, _f, _f, _i, _p, _p, _p, _p, _sz, _i, _i, _i]),
     "ssd_uniform_fill": (_i, [_p, _p, _i64, _u64, _u64]),

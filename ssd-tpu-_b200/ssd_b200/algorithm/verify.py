@@ -73,17 +73,39 @@ def uniforms_from_seed(seed: int, b: int, k: int, v: int, device) -> tuple[torch
     return ua, ug
 
 
+def top_p_mask_(x: torch.Tensor, temperature: float, top_p: float) -> torch.Tensor:
+    """In place: every logit of each row of ``x`` below the top-p cutoff of softmax(x / temperature)
+    becomes -inf (``ssd_top_p_mask``; ties at the cutoff are kept, NaN is masked).  ``x`` is a 2-D
+    (or [..., V] contiguous) fp32 CUDA tensor; top_p >= 1 leaves it untouched."""
+    if x.dtype != torch.float32 or not x.is_cuda or x.stride(-1) != 1:
+        raise ValueError("top_p_mask_ wants a row-contiguous fp32 CUDA tensor")
+    v = x.shape[-1]
+    rows = x.numel() // v if x.dim() != 2 else x.shape[0]
+    ld = x.stride(0) if x.dim() == 2 else v
+    if x.dim() != 2 and not x.is_contiguous():
+        raise ValueError("top_p_mask_ wants a contiguous tensor when it is not 2-D")
+    check(lib().ssd_top_p_mask(stream_ptr(), ptr(x), ld, rows, v, float(temperature), float(top_p)),
+          "ssd_top_p_mask")
+    return x
+
+
 def verify_sample(logits_p, logits_q, speculations, key, *, temperature_p: float = 1.0,
-                  temperature_q: float = 1.0, sampler_x: float = 0.5, alignment: str = "reference"):
+                  temperature_q: float = 1.0, sampler_x: float = 0.5, alignment: str = "reference",
+                  top_p: float = 1.0):
     """verify.py:68-120: rejection sampling with bonus token and residual draw.
 
     logits_p [B, K+1, V], logits_q [B, K, V] fp32; speculations [B, K+1].
     ``key``: int seed or ``(u_accept[B,K], u_gumbel[B,V])``.
     ``alignment="reference"`` judges draft token j+1 with target row j+1, as
     verify.py:103 does; ``"standard"`` uses row j (the textbook rule).
+    ``top_p < 1`` (not in the reference) runs the test on the top-p nuclei of
+    both distributions (``top_p_mask_`` on copies of the logits).
     """
     lp = _dev(logits_p, torch.float32)
     lq = _dev(logits_q, torch.float32)
+    if top_p < 1.0:
+        lp = top_p_mask_(lp.clone(), temperature_p, top_p)
+        lq = top_p_mask_(lq.clone(), temperature_q, top_p)
     spec = _dev(speculations, torch.int32)
     b, kp1, v = lp.shape
     k = kp1 - 1
@@ -123,14 +145,17 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
 
 
 def sample_rows(x: torch.Tensor, temperature: float, seed: int, offset: int = 0,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, top_p: float = 1.0) -> torch.Tensor:
     """One draw per row from softmax(x / temperature) (``ssd_sample_rows``, Gumbel-max on a counter hash).
 
     The draw for (seed, offset) is reproducible; callers advance ``offset`` by at
-    least rows * V between draws that must be independent.
+    least rows * V between draws that must be independent.  ``top_p < 1`` draws
+    from the top-p nucleus (``top_p_mask_`` on a copy of ``x``).
     """
     if x.dim() != 2 or x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1:
         raise ValueError("sample_rows wants a row-contiguous 2-D fp32 CUDA tensor")
+    if top_p < 1.0:
+        x = top_p_mask_(x.clone(), temperature, top_p)
     rows, v = x.shape
     if out is None:
         out = torch.empty(rows, dtype=torch.int32, device=x.device)

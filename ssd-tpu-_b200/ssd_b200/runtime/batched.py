@@ -12,9 +12,11 @@ Per step, for all B sequences (all device work stream-ordered, one host sync):
 2. draft: one forward over each sequence's 1-2 not yet drafted tokens (ragged
    ``q_lens``), then k-1 one-token forwards; each draft token is the argmax
    (temperature 0) or a Gumbel-max draw from softmax(logits / T)
-   (``ssd_sample_rows``); in sampling mode the draft rows are kept for the
-   acceptance test;
-3. verify: one target forward over B x (k+1) tokens;
+   (``ssd_sample_rows``), restricted to the top-p nucleus when ``top_p < 1``
+   (``ssd_top_p_mask`` on the draft rows in place); in sampling mode the
+   (masked) draft rows are kept for the acceptance test;
+3. verify: one target forward over B x (k+1) tokens (its rows top-p masked
+   likewise in sampling mode);
 4. acceptance: ``ssd_verify_greedy`` or ``ssd_verify_sample`` (rejection
    sampling with bonus / residual draw, the textbook row alignment) over the B
    rows;
@@ -30,7 +32,7 @@ import numpy as np
 import torch
 
 from .._lib import check, lib, ptr, stream_ptr
-from ..algorithm.verify import argmax_rows, sample_rows, verify_sample
+from ..algorithm.verify import argmax_rows, sample_rows, top_p_mask_, verify_sample
 from ..kernels.kv_cache import KVCacheState
 from ..kernels.ops import max_tokens_per_forward
 from ..models.gemma import GemmaRunner, GemmaWeights
@@ -57,10 +59,13 @@ class _BatchModel:
 class BatchedSpeculativeDecoder:
     def __init__(self, target: GemmaWeights, draft: GemmaWeights, batch: int, k: int = 4, max_seq_len: int = 1024,
                  block_size: int = 16, temperature: float = 0.0, sampler_x: float = 0.5, seed: int = 0, comm=None,
-                 num_blocks: int | None = None):
+                 num_blocks: int | None = None, top_p: float = 1.0):
         B = self.B = int(batch)
         self.k = k
         self.temperature = float(temperature)
+        self.top_p = float(top_p)
+        if not 0.0 < self.top_p <= 1.0:
+            raise ValueError("top_p must be in (0, 1]")
         self.sampler_x = float(sampler_x)
         self.seed = int(seed)
         self.dev = target.device
@@ -196,6 +201,8 @@ class BatchedSpeculativeDecoder:
                 d.runner.forward(self.dtok[i - 1].view(B, 1), ds[11 + i], d.cache.pages, d.pm.tables, self.logits_d,
                                  last_only=True)
             if self.sampling:
+                if self.top_p < 1.0:
+                    top_p_mask_(self.logits_d, self.temperature, self.top_p)
                 sample_rows(self.logits_d, self.temperature, self.seed, self._draws * B * self.V, out=self.dtok[i])
                 self._draws += 1
                 self.logits_q[:, i].copy_(self.logits_d)
@@ -207,6 +214,8 @@ class BatchedSpeculativeDecoder:
         self.ev[0].record(st)
         t.pm.allocate_rows(0, B, ds[10], ds[11], None)
         t.runner.forward(self.vt, ds[10], t.cache.pages, t.pm.tables, self.logits_t, last_only=False)
+        if self.sampling and self.top_p < 1.0:
+            top_p_mask_(self.logits_t.view(B * (k + 1), self.V), self.temperature, self.top_p)
         if self.sampling:
             for u in (self.u_accept, self.u_gumbel):
                 check(lib().ssd_uniform_fill(stream_ptr(), ptr(u), u.numel(), self.seed ^ 0x5D5D,

@@ -90,3 +90,21 @@ def test_batched_synthetic_long_context_step(cuda):
     for _ in range(3):
         dec.step()
     assert (dec.t.n > n0).all() and (dec.t.n - n0 <= 3 * 7).all()
+
+
+def test_top_p_to_zero_sampling_equals_greedy(cuda):
+    """With top_p -> 0 every nucleus is the argmax alone: sampled drafting, rejection sampling on the
+    nuclei and the residual draw all collapse to greedy decoding, token for token."""
+    from ssd_b200.runtime.batched import BatchedSpeculativeDecoder
+
+    t, d = _pair(cuda)
+    rng = np.random.default_rng(4)
+    prompts = [[int(x) for x in rng.integers(0, 2048, n)] for n in (9, 33, 70)]
+    greedy = BatchedSpeculativeDecoder(t, d, batch=3, k=6, max_seq_len=512).generate(prompts, 20)
+    nucleus = BatchedSpeculativeDecoder(t, d, batch=3, k=6, max_seq_len=512, temperature=1.0, top_p=1e-6,
+                                        seed=3).generate(prompts, 20)
+    assert nucleus == greedy
+    # a real nucleus still samples: p = 0.95 at T = 1 runs and stays inside the vocabulary
+    out = BatchedSpeculativeDecoder(t, d, batch=3, k=6, max_seq_len=512, temperature=1.0, top_p=0.95,
+                                    seed=3).generate(prompts, 12)
+    assert all(0 <= tok < t.shape.vocab for o in out for tok in o)

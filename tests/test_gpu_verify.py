@@ -147,3 +147,53 @@ def test_sample_seeded_key_is_deterministic(cuda):
     assert (u > 0).all() and (u < 1).all() and abs(u.mean() - 0.5) < 0.01
     r3 = verify_sample(lp, lq, spec, (ua, ug))
     assert r3.recovery_tokens.tolist() == r1.recovery_tokens.tolist()
+
+
+def _top_p_rows(v, seed):
+    rng = np.random.default_rng(seed)
+    rows = (3.0 * rng.standard_normal((6, v))).astype(np.float32)
+    rows[1] = np.round(rows[1] * 4) / 4                 # many ties
+    rows[2, ::7] = -np.inf                              # already masked entries
+    rows[2, 5] = np.nan
+    rows[3] = np.float32(0.5)                           # all equal
+    rows[4, 17] = 40.0                                  # one dominant logit
+    return rows
+
+
+@pytest.mark.parametrize("v,t,p", [(256000, 1.0, 0.95), (256000, 0.7, 0.5), (32000, 1.3, 0.9), (4099, 1.0, 1e-4)])
+def test_top_p_mask_matches_oracle(cuda, v, t, p):
+    """ssd_top_p_mask keeps exactly the oracle's nucleus (same values, everything else -inf)."""
+    import torch
+
+    from oracle.verify import top_p_mask as o_mask
+    from ssd_b200.algorithm.verify import top_p_mask_
+
+    rows = _top_p_rows(v, seed=v + int(100 * p))
+    got = top_p_mask_(torch.from_numpy(rows).cuda(), t, p).cpu().numpy()
+    want = o_mask(rows, t, p)
+    np.testing.assert_array_equal(got, want)
+    kept = np.isfinite(want).sum(-1)
+    assert (kept >= 1).all() and kept[3] == v  # ties: the all-equal row keeps every logit
+
+
+@pytest.mark.parametrize("b,k,v", [(6, 6, 32000), (4, 4, 256000)])
+def test_sample_with_top_p_matches_oracle(cuda, b, k, v):
+    """Rejection sampling on the top-p nuclei (standard alignment, T = 1, p = 0.95) equals the oracle run
+    on the oracle-masked logits with the same uniforms (near-ties excepted, as for plain sampling)."""
+    from oracle.verify import top_p_mask as o_mask
+    from ssd_b200.algorithm.verify import verify_sample
+
+    lp, lq, spec, ua, ug = _sample_inputs(b, k, v, seed=7 * b + v)
+    res = verify_sample(lp, lq, spec, (ua, ug), alignment="standard", top_p=0.95)
+    acc, rec, mask, (am, gap) = o_sample(o_mask(lp, 1.0, 0.95), o_mask(lq, 1.0, 0.95), spec, ua, ug,
+                                         alignment="standard", return_margins=True)
+    ga = res.accept_until.cpu().numpy()
+    gr = res.recovery_tokens.cpu().numpy()
+    assert np.all((ga == acc) | (am < 1e-5)), (ga, acc, am)
+    ok_rows = ga == acc
+    assert np.all((gr == rec) | (gap < 1e-4) | ~ok_rows), (gr, rec, gap)
+    # the recovery token lies inside the target's nucleus, or the draft's when every draft token was accepted
+    lpm = o_mask(lp, 1.0, 0.95)
+    for i in range(b):
+        row = lpm[i, k] if ga[i] == k else lpm[i, ga[i]]
+        assert np.isfinite(row[gr[i]])

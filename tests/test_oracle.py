@@ -294,3 +294,20 @@ def test_oracle_fork_shares_and_frees():
     top = len(pm2.free_blocks)
     d2 = OracleSeq(num_tokens=32)
     assert pm2.fork(s2, [d2], 32) == [True] and len(pm2.free_blocks) == top and d2.block_table == s2.block_table
+
+
+def test_top_p_threshold_definition():
+    """Nucleus cutoff of softmax(x / T): the value at which the running mass (descending, fp64) first
+    reaches p * Z; ties at the cutoff stay, NaN and -inf go."""
+    from oracle.verify import top_p_mask, top_p_threshold
+
+    x = np.array([2, 1, 1, 0], np.float32)  # masses 1, e^-1, e^-1, e^-2 (Z = 1.871)
+    assert top_p_threshold(x, 1.0, 0.5) == 2.0       # 1 >= 0.936
+    assert top_p_threshold(x, 1.0, 0.6) == 1.0       # 1 < 1.123 <= 1.368: both tied 1s kept
+    assert top_p_threshold(x, 1.0, 0.99) == 0.0
+    assert top_p_threshold(x, 1.0, 1e-9) == 2.0
+    assert top_p_threshold(x, 0.25, 0.9) == 2.0      # sharper: e^-4 tails
+    got = top_p_mask(np.array([[2, 1, 1, 0, np.nan, -np.inf]], np.float32), 1.0, 0.6)
+    np.testing.assert_array_equal(got, [[2, 1, 1, -np.inf, -np.inf, -np.inf]])
+    assert top_p_threshold(np.array([np.nan, -np.inf], np.float32), 1.0, 0.9) is None
+    np.testing.assert_array_equal(top_p_mask(x[None], 1.0, 1.0), x[None])  # p >= 1: untouched

@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
                     help="N > 1: tensor-parallel pair (one sequence) or independent replicas")
-    ap.add_argument("--op", choices=["linear", "attention", "verify", "sample", "allreduce", "allgather"],
+    ap.add_argument("--op", choices=["linear", "attention", "verify", "sample", "topp", "allreduce", "allgather"],
                     default=None,
                     help="time one kernel family on its op-level workload instead of the decode loop")
     ap.add_argument("--rows", "--m", dest="m", type=int, default=5)
@@ -524,7 +524,7 @@ def run_op(args):
         line = {"op": "paged_attention", "shape": args.attn, "B": b, "T": t, "Hq": hq, "Hkv": hkv, "ctx": ctx.tolist(), "us": ms * 1000, "gbs": nbytes / ms / 1e6,
                 "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind, "kv_bytes": nbytes,
                 "note": "KV pages (302 MB expected) exceed L2; one layer"}
-    else:
+    elif args.op in ("verify", "sample"):
         b, k, v = 8, 4, 256000
         nrot = 4
         lps = [3.0 * torch.randn((b, k + 1, v), device="cuda", generator=g) for _ in range(nrot)]
@@ -541,6 +541,30 @@ def run_op(args):
         line = {"op": "verify_" + ("greedy" if args.op == "verify" else "sample"), "B": b, "K": k, "V": v,
                 "us": ms * 1000, "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind,
                 "algorithmic_bytes": nbytes}
+    elif args.op == "topp":
+        # top-p 0.95 at T = 1 over --rows rows of 256000 N(0, 3^2) logits; the mask works in place, so
+        # every timed call gets a fresh copy (the copy is outside the events)
+        from ssd_b200.algorithm.verify import top_p_mask_
+
+        rows, v = args.m, 256000
+        src = 3.0 * torch.randn((rows, v), device="cuda", generator=g)
+        x = torch.empty_like(src)
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for i in range(args.warmup + reps):
+            x.copy_(src)
+            e0.record(st)
+            top_p_mask_(x, 1.0, 0.95)
+            e1.record(st)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+        ms = float(np.median(times))
+        nbytes = rows * v * 4 * 2  # one read and one write of every logit
+        line = {"op": "top_p_mask", "rows": rows, "V": v, "top_p": 0.95, "us": ms * 1000,
+                "gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm, "peak_kind": kind,
+                "algorithmic_bytes": nbytes, "note": "rows copied fresh before each call (L2-warm when small)"}
     print(json.dumps(line), flush=True)
 
 

@@ -116,7 +116,7 @@ int ssd_sample_rows(ssd_stream_t stream, const float* x, int64_t ld, int rows, i
  * sampling and acceptance kernels above see the renormalised nucleus.  t* is
  * the largest logit value whose cumulative mass -- over all logits >= it,
  * ties included, fp64 masses exp((x - max) / temperature) -- reaches
- * top_p * Z.  top_p >= 1 leaves the rows untouched.  Not in the reference (its
+ * top_p * Z.  top_p >= 1 leaves the rows untouched; V < 524288.  Not in the reference (its
  * SamplingParams has no top-p); the batched serving workload (T = 1.0,
  * top-p 0.95) asks for it.  No workspace.
  */

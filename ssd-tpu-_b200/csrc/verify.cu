@@ -333,24 +333,27 @@ sample_draw_kernel(const float* lp, const float* lq,
 // largest logit value whose cumulative mass (all logits >= it, ties included)
 // reaches p * Z.  Masses are fp64: w = exp(-(m - x) / T), m the row max.
 //   1. m;
-//   2. histogram of d = (m - x) / T over [0, 32) nats in 2048 bins of 1/64 nat
-//      (counts and fp64 masses); logits further down add to a tail sum only;
+//   2. histogram of d = (m - x) / T over the near range [0, 8) nats in 2048 bins
+//      of 1/256 nat; each mass is rounded to a multiple of 2^-44 and added with a
+//      64-bit integer atomic (native in shared memory, order-independent, so the
+//      bin sums are deterministic).  Logits further down only add to an fp64
+//      register sum, so most of a row costs no atomic at all;
 //   3. the cutoff bin: the first bin, walking down from the max, at which the
-//      running mass reaches p * Z;
-//   4. its logits are compacted into shared memory and sorted (descending); the
-//      walk continues through them to the exact t*;
+//      running mass reaches p * Z.  If the near range holds less than p * Z, a
+//      second histogram covers [8, 40) nats in 1/64-nat bins the same way;
+//   4. the cutoff bin's logits are compacted into shared memory and sorted
+//      (descending); the walk continues through them to the exact t*;
 //   5. every logit below t* (and every NaN) becomes -inf, in place.
-// A cutoff in the tail (p within e^-32 * V / Z of 1) keeps every finite logit;
-// a cutoff bin holding more than kTopPCap logits is kept whole.
+// A cutoff beyond 40 nats (p within ~e^-40 * V / Z of 1) keeps every finite
+// logit; a cutoff bin holding more than kTopPCap logits is kept whole.
 constexpr int kTopPThreads = 1024;
 constexpr int kTopPBins = 2048;
-constexpr double kTopPBinsPerNat = 64.0;
 constexpr int kTopPCap = 4096;
+constexpr double kTopPFix = 17592186044416.0;  // 2^44: V * 2^44 stays below 2^63 for V < 2^19
 
 __global__ void __launch_bounds__(kTopPThreads)
 top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
-  __shared__ unsigned int cnt[kTopPBins];
-  __shared__ double mass[kTopPBins];
+  __shared__ unsigned long long massq[kTopPBins];  // bin masses in units of 2^-44
   __shared__ float cand[kTopPCap];
   __shared__ float redf[32];
   __shared__ double redd[32];
@@ -367,60 +370,71 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
     return;
   }
   const double md = (double)m;
-  for (int i = threadIdx.x; i < kTopPBins; i += kTopPThreads) {
-    cnt[i] = 0u;
-    mass[i] = 0.0;
-  }
-  if (threadIdx.x == 0) s_ncand = 0;
-  __syncthreads();
-  double tail = 0.0;
-  for (int j = threadIdx.x; j < V; j += kTopPThreads) {
-    const float v = __ldcg(row + j);
-    if (!(v > -INFINITY)) continue;  // -inf and NaN carry no mass
-    const double d = (md - (double)v) * inv_t;
-    const double w = exp(-d);
-    const int bin = (int)(d * kTopPBinsPerNat);
-    if (bin < kTopPBins) {
-      atomicAdd(&cnt[bin], 1u);
-      atomicAdd(&mass[bin], w);
-    } else {
-      tail += w;
+  double lo = 0.0, scale = 256.0;  // level 0: [0, 8) nats, 256 bins per nat
+  double above = 0.0;              // mass of the logits above the current range
+  double target = 0.0;
+  int b = -1;
+  for (int level = 0; level < 2 && b < 0; ++level) {
+    if (level == 1) {
+      lo = 8.0;
+      scale = 64.0;  // [8, 40) nats
+    }
+    const double hi = lo + kTopPBins / scale;
+    for (int i = threadIdx.x; i < kTopPBins; i += kTopPThreads) massq[i] = 0ull;
+    __syncthreads();
+    double below = 0.0;  // mass of the logits below the range (fp64, per thread)
+    for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+      const float v = __ldcg(row + j);
+      if (!(v > -INFINITY)) continue;  // -inf and NaN carry no mass
+      const double d = (md - (double)v) * inv_t;
+      if (d < lo) continue;  // counted at the previous level
+      const double w = exp(-d);
+      if (d < hi) atomicAdd(&massq[(int)((d - lo) * scale)], (unsigned long long)__double2ll_rn(w * kTopPFix));
+      else below += w;
+    }
+    below = block_reduce(below, redd, OpSum());
+    if (threadIdx.x == 0) {
+      unsigned long long inq = 0ull;
+      for (int i = 0; i < kTopPBins; ++i) inq += massq[i];
+      const double in_range = (double)inq / kTopPFix;
+      if (level == 0) target = top_p * (in_range + below);
+      unsigned long long cum = 0ull;
+      int bb = 0;
+      for (; bb < kTopPBins; ++bb) {
+        if (above + (double)(cum + massq[bb]) / kTopPFix >= target) break;
+        cum += massq[bb];
+      }
+      s_bin = bb < kTopPBins ? bb : -1;
+      s_above = above + (double)cum / kTopPFix;
+      s_target = target;
+      s_t = -INFINITY;  // cutoff below both ranges: keep every finite logit
+      if (bb >= kTopPBins) above += in_range;
+    }
+    __syncthreads();
+    b = s_bin;
+    if (threadIdx.x != 0) {
+      above = s_above;
+      target = s_target;
     }
   }
-  tail = block_reduce(tail, redd, OpSum());
-  if (threadIdx.x == 0) {
-    double Z = tail;
-    for (int i = kTopPBins - 1; i >= 0; --i) Z += mass[i];
-    const double target = top_p * Z;
-    double cum = 0.0;
-    int b = 0;
-    for (; b < kTopPBins; ++b) {
-      if (cum + mass[b] >= target) break;
-      cum += mass[b];
-    }
-    s_bin = b < kTopPBins ? b : -1;
-    s_above = cum;
-    s_target = target;
-    s_t = -INFINITY;  // cutoff in the tail: keep every finite logit
-  }
-  __syncthreads();
-  const int b = s_bin;
   if (b >= 0) {
-    const unsigned int n = cnt[b];
+    if (threadIdx.x == 0) s_ncand = 0;
+    __syncthreads();
+    for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+      const float v = __ldcg(row + j);
+      if (!(v > -INFINITY)) continue;
+      const double d = (md - (double)v) * inv_t;
+      if (d >= lo && (int)((d - lo) * scale) == b) {
+        const int k = atomicAdd(&s_ncand, 1);
+        if (k < kTopPCap) cand[k] = v;
+      }
+    }
+    __syncthreads();
+    const unsigned int n = (unsigned int)s_ncand;
     if (n > (unsigned)kTopPCap) {
       // too many logits near the cutoff to sort here: keep the whole bin
-      if (threadIdx.x == 0) s_t = (float)(md - ((double)(b + 1) / kTopPBinsPerNat) / inv_t);
+      if (threadIdx.x == 0) s_t = (float)(md - (lo + (double)(b + 1) / scale) / inv_t);
     } else {
-      for (int j = threadIdx.x; j < V; j += kTopPThreads) {
-        const float v = __ldcg(row + j);
-        if (!(v > -INFINITY)) continue;
-        const double d = (md - (double)v) * inv_t;
-        if ((int)(d * kTopPBinsPerNat) == b) {
-          const int k = atomicAdd(&s_ncand, 1);
-          if (k < kTopPCap) cand[k] = v;
-        }
-      }
-      __syncthreads();
       int np2 = 1;
       while (np2 < (int)n) np2 <<= 1;
       for (int i = (int)n + threadIdx.x; i < np2; i += kTopPThreads) cand[i] = -INFINITY;
@@ -666,6 +680,7 @@ extern "C" int ssd_top_p_mask(ssd_stream_t stream, float* x, int64_t ld, int row
                               float top_p) {
   if (rows <= 0 || V <= 0 || ld < V || !x || !(temperature > 0.f) || !(top_p > 0.f)) return SSD_ERR_INVALID;
   if (top_p >= 1.0f) return SSD_OK;  // the whole distribution
+  if (V >= (1 << 19)) return SSD_ERR_UNSUPPORTED;  // fixed-point bin masses would overflow
   cudaStream_t st = (cudaStream_t)stream;
   SSD_PDL(top_p_mask_kernel, dim3(rows), kTopPThreads, 0, st, x, ld, V, 1.0 / (double)temperature, (double)top_p);
   SSD_CHECK_LAUNCH();

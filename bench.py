@@ -40,6 +40,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Gemma-7B/2B sd tokens/sec at TP 1/2/4/8 B200; verify-step µs; HBM GB/s"
 WORKLOAD = "gemma-7b target + gemma-2b draft, random-init bf16, sd greedy k=4, batch 1, prompt 128"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
+TRAFFIC_RATIO = 309.07 / 302.52  # DRAM bytes / algorithmic bytes of one captured 7B gate/up launch
 
 
 def parse():
@@ -387,7 +388,12 @@ def run_ours(args):
             "tokens_per_step": tokens / args.steps,
             "roofline": {"bound": "hbm", "kernel": "skinny projections (QKV, O, gate/up, down, LM head), "
                          f"M = {M}", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                         # DRAM bytes per launch: the gate/up ncu capture's read + write over its
+                         # algorithmic bytes (309.07 / 302.52 MB), applied to the average launch
+                         "traffic": TRAFFIC_RATIO * proj_bytes / max(n_launch, 1) if not tp else None,
+                         "traffic_source": "ncu capture of the 7B gate/up launch (profiles/linear_tc_gate_up_m5.md): "
+                                           "309.07 MB DRAM per 302.52 MB algorithmic, scaled to the average launch",
                          "window": "event-timed projection launches of a separate profiled decode window",
                          "per_launch_bytes": proj_bytes / max(n_launch, 1), "per_kind": per_kind},
             "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": 16 * 4 + 8 * 4,

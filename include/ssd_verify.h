@@ -72,8 +72,8 @@ int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t*
 
 /*
  * ssd_verify_greedy without a workspace argument, for callers that cannot
- * allocate device memory (an XLA custom call handed only its operands, code
- * inside a CUDA graph capture, embedders with a fixed memory budget).  No
+ * allocate device memory (an XLA custom call handed only its operands,
+ * embedders with a fixed device-memory budget).  No
  * counterpart in the reference: it is an addition of this library.
  * Outputs and argument meaning are those of ssd_verify_greedy; it allocates
  * nothing.  Its scratch is a 34 KB array in the library's device data that

@@ -594,8 +594,8 @@ extern "C" int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, con
 
 // ------------------------------------------------------------------ no-allocation variant
 // Greedy acceptance for callers that cannot allocate device memory (an XLA
-// custom call that is handed only its operands, code running inside a CUDA
-// graph capture, embedders with a fixed memory budget).  Its scratch -- the
+// custom call that is handed only its operands and no allocator, embedders
+// with a fixed device-memory budget).  Its scratch -- the
 // ticket counters and the per-chunk argmax partials -- lives in this file-scope
 // device array instead of a caller workspace.  Every GPU that loads the library
 // holds these 34 KB until the process exits.  Host code must not use the array's

@@ -1,8 +1,8 @@
 """GPU: the allocation-free greedy acceptance entry point (ssd_verify_greedy_noalloc).
 
 Some callers of this library cannot call cudaMalloc: an XLA custom call is
-handed only its operands, code running inside a CUDA graph capture may not
-allocate, and some embedders run under a fixed device-memory budget.  For them
+handed only its operands and no allocator, and some embedders run under a
+fixed device-memory budget.  For them
 the library keeps the scratch of this one entry point in its own device data.
 This test calls it through the C ABI and checks that its outputs equal those
 of ssd_verify_greedy (which takes a caller workspace) on two calls in a row --

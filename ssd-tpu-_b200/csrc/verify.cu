@@ -31,6 +31,20 @@ inline int scan_chunks(int rows, int V) {
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// The statistics pass of the sampling verify (one exp per element over 2K rows
+// per sequence) is bound by instruction issue as much as by HBM: it gets twice
+// the CTAs.  The residual and draw passes, over one row pair per sequence, keep
+// scan_chunks (measured: twice the CTAs made both slower).
+inline int sample_chunks(int rows, int V) {
+  if (rows <= 0 || V <= 0) return 1;
+  int want = (2 * kTargetCtas + rows - 1) / rows;
+  int cap = (V + 1023) / 1024;  // at least 1K elements per CTA
+  if (cap < 1) cap = 1;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return want;
+}
+
 // Chunk [lo, hi) of a row of V elements; bounds are multiples of 4 except the end.
 __device__ __forceinline__ void chunk_bounds(int V, int nchunks, int c, int& lo, int& hi) {
   int per = (V + nchunks - 1) / nchunks;
@@ -155,8 +169,12 @@ struct SampleDecision {
 
 // fp32 ops written out so the compiler cannot contract them into FMAs: the
 // oracle evaluates the same expressions with separate roundings.
+// x / T; at T = 1 the quotient is x exactly, so the division is skipped.
+__device__ __forceinline__ float div_temp(float x, float temp) {
+  return temp == 1.f ? x : __fdiv_rn(x, temp);
+}
 __device__ __forceinline__ float prob_of(float logit, float temp, float m, float s) {
-  return __fdiv_rn(expf(__fsub_rn(__fdiv_rn(logit, temp), m)), s);
+  return __fdiv_rn(expf(__fsub_rn(div_temp(logit, temp), m)), s);
 }
 
 // Pass 1: per-row (max, sum exp) of x/T for the rows the acceptance test reads,
@@ -181,17 +199,50 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   int lo, hi;
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
   // One pass, online per thread: (m, s) with s = sum exp(v - m), v = x / T.
+  // Sixteen loaded values at a time: their max moves m once (one rescale), then
+  // each value adds exp(v - m) in four partial sums, without a branch per value.
+  // A NaN logit is skipped (fmaxf ignores it, the select drops it) and a masked
+  // (-inf) logit adds exp(-inf) = 0.
   float m = -INFINITY, s = 0.f;
   auto push = [&](float x) {
-    const float v = __fdiv_rn(x, temp);
+    const float v = div_temp(x, temp);
     if (v > m) { s = (m == -INFINITY ? 0.f : s * expf(__fsub_rn(m, v))) + 1.f; m = v; }
-    else if (v > -INFINITY) s += expf(__fsub_rn(v, m));  // a masked (-inf) logit adds nothing
+    else if (v > -INFINITY) s += expf(__fsub_rn(v, m));
   };
   if (vec_ok) {
     const int nv = (hi - lo) >> 2;
     const float4* p = reinterpret_cast<const float4*>(row + lo);
-    for (int i = threadIdx.x; i < nv; i += kScanThreads) {
-      float4 a = __ldcg(p + i);
+    int i = threadIdx.x;
+    // four independent 16-byte loads in flight per thread before any exp
+    for (; i + 3 * kScanThreads < nv; i += 4 * kScanThreads) {
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 a = __ldcg(p + i + u * kScanThreads);
+        v[4 * u] = a.x; v[4 * u + 1] = a.y; v[4 * u + 2] = a.z; v[4 * u + 3] = a.w;
+      }
+      float lm = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        v[e] = div_temp(v[e], temp);
+        lm = fmaxf(lm, v[e]);
+      }
+      if (lm > m) {
+        s = (m == -INFINITY) ? 0.f : s * expf(__fsub_rn(m, lm));
+        m = lm;
+      }
+      if (m != -INFINITY) {
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float ex = expf(__fsub_rn(v[e], m));
+          ps[e & 3] += (v[e] > -INFINITY) ? ex : 0.f;
+        }
+        s += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      }
+    }
+    for (; i < nv; i += kScanThreads) {
+      const float4 a = __ldcg(p + i);
       push(a.x); push(a.y); push(a.z); push(a.w);
     }
     for (int j = lo + 4 * nv + threadIdx.x; j < hi; j += kScanThreads) push(__ldcg(row + j));
@@ -219,16 +270,26 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
     }
     stats[rr] = make_float2(M, S);
   }
+  // the logits of the drafted tokens that the accept loop reads, all K in one go
+  // (not one dependent round trip per position)
+  __shared__ float s_xp[64], s_xq[64];
+  __shared__ int s_tok_ok[64];
+  for (int j = threadIdx.x; j < K; j += blockDim.x) {
+    const int tok = spec[(int64_t)b * (K + 1) + j + 1];
+    const bool ok = (unsigned)tok < (unsigned)V;  // not a token id: reject (never index with it)
+    s_tok_ok[j] = ok ? 1 : 0;
+    s_xp[j] = ok ? __ldcg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok) : 0.f;
+    s_xq[j] = ok ? __ldcg(lq + ((int64_t)b * K + j) * V + tok) : 0.f;
+  }
   __syncthreads();
   if (threadIdx.x != 0) return;
   int acc = 0;
   for (int j = 0; j < K; ++j) {
-    const int tok = spec[(int64_t)b * (K + 1) + j + 1];
-    if ((unsigned)tok >= (unsigned)V) break;  // not a token id: reject (never index with it)
+    if (!s_tok_ok[j]) break;
     const float2 pst = stats[j];  // target row j+off is stored at index j
     const float2 qst = stats[nP + j];
-    const float pv = prob_of(__ldcg(lp + ((int64_t)b * (K + 1) + j + off) * V + tok), tp, pst.x, pst.y);
-    const float qv = prob_of(__ldcg(lq + ((int64_t)b * K + j) * V + tok), tq, qst.x, qst.y);
+    const float pv = prob_of(s_xp[j], tp, pst.x, pst.y);
+    const float qv = prob_of(s_xq[j], tq, qst.x, qst.y);
     const float ratio = fminf(1.0f, __fdiv_rn(pv, fmaxf(qv, 1e-12f)));
     if (u_accept[(int64_t)b * K + j] < ratio) ++acc; else break;
   }
@@ -248,7 +309,7 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
 // Pass 2: residual mass sum_v max(p_v - x q_v, 0) (skipped for bonus rows).
 __global__ void __launch_bounds__(kScanThreads)
 sample_residual_kernel(const float* lp, const float* lq, int K, int V,
-                       int nchunks, float tp, float tq, float sx, unsigned int* counters,
+                       int nchunks, bool vec_ok, float tp, float tq, float sx, unsigned int* counters,
                        float* part, SampleDecision* dec) {
   __shared__ float redf[32];
   __shared__ bool is_last;
@@ -262,25 +323,45 @@ sample_residual_kernel(const float* lp, const float* lq, int K, int V,
   int lo, hi;
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
   float s = 0.f;
-  for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
-    const float p = prob_of(__ldcg(prow + j), tp, d.mp, d.sp);
-    const float q = prob_of(__ldcg(qrow + j), tq, d.mq, d.sq);
+  auto add = [&](float xp, float xq) {
+    const float p = prob_of(xp, tp, d.mp, d.sp);
+    const float q = prob_of(xq, tq, d.mq, d.sq);
     s += fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f);
+  };
+  int j0 = lo;
+  if (vec_ok) {
+    // two float4 of each row (four 16-byte loads) in flight per thread
+    const int nv = (hi - lo) >> 2;
+    const float4* pp = reinterpret_cast<const float4*>(prow + lo);
+    const float4* qq = reinterpret_cast<const float4*>(qrow + lo);
+    int i = threadIdx.x;
+    for (; i + kScanThreads < nv; i += 2 * kScanThreads) {
+      const float4 a0 = __ldcg(pp + i), a1 = __ldcg(pp + i + kScanThreads);
+      const float4 b0 = __ldcg(qq + i), b1 = __ldcg(qq + i + kScanThreads);
+      add(a0.x, b0.x); add(a0.y, b0.y); add(a0.z, b0.z); add(a0.w, b0.w);
+      add(a1.x, b1.x); add(a1.y, b1.y); add(a1.z, b1.z); add(a1.w, b1.w);
+    }
+    for (; i < nv; i += kScanThreads) {
+      const float4 a0 = __ldcg(pp + i), b0 = __ldcg(qq + i);
+      add(a0.x, b0.x); add(a0.y, b0.y); add(a0.z, b0.z); add(a0.w, b0.w);
+    }
+    j0 = lo + 4 * nv;
   }
+  for (int j = j0 + threadIdx.x; j < hi; j += kScanThreads) add(__ldcg(prow + j), __ldcg(qrow + j));
   s = block_reduce(s, redf, OpSum());
   if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = s;
   if (!last_block_of(&counters[b], (unsigned)nchunks, &is_last)) return;
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int i = 0; i < nchunks; ++i) tot += __ldcg(&part[(int64_t)b * nchunks + i]);
-    dec[b].rsum = fmaxf(tot, 1e-12f);
-  }
+  // fold the chunk sums: every thread loads its share, then one fixed-order tree
+  float tot = 0.f;
+  for (int i = threadIdx.x; i < nchunks; i += kScanThreads) tot += __ldcg(&part[(int64_t)b * nchunks + i]);
+  tot = block_reduce(tot, redf, OpSum());
+  if (threadIdx.x == 0) dec[b].rsum = fmaxf(tot, 1e-12f);
 }
 
 // Pass 3: Gumbel-max categorical draw over log(r + 1e-12).
 __global__ void __launch_bounds__(kScanThreads)
 sample_draw_kernel(const float* lp, const float* lq,
-                   const float* u_gumbel, int K, int V, int nchunks, float tp, float tq,
+                   const float* u_gumbel, int K, int V, int nchunks, bool vec_ok, float tp, float tq,
                    float sx, unsigned int* counters, unsigned long long* part,
                    const SampleDecision* dec, int32_t* accept_until,
                    int32_t* recovery, uint8_t* mask) {
@@ -296,29 +377,67 @@ sample_draw_kernel(const float* lp, const float* lq,
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
   float best = -INFINITY;
   int bidx = 0x7fffffff;
-  for (int j = lo + threadIdx.x; j < hi; j += kScanThreads) {
-    const float p = prob_of(__ldcg(prow + j), tp, d.mp, d.sp);
+  // element j with its target logit xp, draft logit xq (unused for a bonus draw), uniform u;
+  // a thread visits its elements in increasing j, so ties keep the first index
+  auto visit = [&](int j, float xp, float xq, float u) {
+    const float p = prob_of(xp, tp, d.mp, d.sp);
     float r;
     if (d.bonus) {
       r = p;
     } else {
-      const float q = prob_of(__ldcg(qrow + j), tq, d.mq, d.sq);
+      const float q = prob_of(xq, tq, d.mq, d.sq);
       r = __fdiv_rn(fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f), d.rsum);
     }
-    const float g = -logf(-logf(__ldcg(urow + j)));
+    const float g = -logf(-logf(u));
     const float score = __fadd_rn(logf(__fadd_rn(r, 1e-12f)), g);
     if (score > best) { best = score; bidx = j; }
+  };
+  int j0 = lo;
+  if (vec_ok) {
+    const int nv = (hi - lo) >> 2;
+    const float4* pp = reinterpret_cast<const float4*>(prow + lo);
+    const float4* qq = reinterpret_cast<const float4*>(qrow + lo);
+    const float4* uu = reinterpret_cast<const float4*>(urow + lo);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    int i = threadIdx.x;
+    // two float4 of each of the three rows (six 16-byte loads) in flight per thread
+    for (; i + kScanThreads < nv; i += 2 * kScanThreads) {
+      float4 a[2], c[2], u[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        a[e] = __ldcg(pp + i + e * kScanThreads);
+        c[e] = d.bonus ? zero : __ldcg(qq + i + e * kScanThreads);
+        u[e] = __ldcg(uu + i + e * kScanThreads);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = lo + 4 * (i + e * kScanThreads);
+        visit(j, a[e].x, c[e].x, u[e].x); visit(j + 1, a[e].y, c[e].y, u[e].y);
+        visit(j + 2, a[e].z, c[e].z, u[e].z); visit(j + 3, a[e].w, c[e].w, u[e].w);
+      }
+    }
+    for (; i < nv; i += kScanThreads) {
+      const float4 a = __ldcg(pp + i);
+      const float4 c = d.bonus ? zero : __ldcg(qq + i);
+      const float4 u = __ldcg(uu + i);
+      const int j = lo + 4 * i;
+      visit(j, a.x, c.x, u.x); visit(j + 1, a.y, c.y, u.y); visit(j + 2, a.z, c.z, u.z); visit(j + 3, a.w, c.w, u.w);
+    }
+    j0 = lo + 4 * nv;
   }
+  for (int j = j0 + threadIdx.x; j < hi; j += kScanThreads)
+    visit(j, __ldcg(prow + j), d.bonus ? 0.f : __ldcg(qrow + j), __ldcg(urow + j));
   unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
   if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = key;
   pdl_trigger();
   if (!last_block_of(&counters[b], (unsigned)nchunks, &is_last)) return;
+  unsigned long long k = 0ull;
+  for (int i = threadIdx.x; i < nchunks; i += kScanThreads) {
+    const unsigned long long v = __ldcg(&part[(int64_t)b * nchunks + i]);
+    k = v > k ? v : k;
+  }
+  k = block_reduce(k, red, OpMax());
   if (threadIdx.x == 0) {
-    unsigned long long k = 0ull;
-    for (int i = 0; i < nchunks; ++i) {
-      unsigned long long v = __ldcg(&part[(int64_t)b * nchunks + i]);
-      k = v > k ? v : k;
-    }
     accept_until[b] = d.acc;
     recovery[b] = k == 0ull ? 0 : (int32_t)argmax_key_index(k);
     if (mask) {
@@ -690,7 +809,7 @@ extern "C" int ssd_top_p_mask(ssd_stream_t stream, float* x, int64_t ld, int row
 static void sample_layout(int B, int K, int V, int& nR, int& nch, size_t& off_part, size_t& off_dec,
                           size_t& total) {
   nR = 2 * K + 1;  // upper bound over both alignments
-  nch = scan_chunks(B * nR, V);
+  nch = sample_chunks(B * nR, V);
   // the residual and draw passes scan B rows: give them the same chunk count
   off_part = kCounterBytes;
   const size_t p1 = sizeof(float2) * (size_t)B * nR * nch;
@@ -738,12 +857,12 @@ extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, con
                                                                 speculations, u_accept, dec);
   SSD_CHECK_LAUNCH();
   const int nch_b = scan_chunks(B, V);
-  SSD_PDL(sample_residual_kernel, dim3(nch_b, B), kScanThreads, 0, st, logits_p, logits_q, K, V, nch_b, temperature_p,
-                                                                  temperature_q, sampler_x, c1,
-                                                                  reinterpret_cast<float*>(part), dec);
+  const bool vec_b = vec_ok && ((reinterpret_cast<uintptr_t>(u_gumbel) & 15) == 0);
+  SSD_PDL(sample_residual_kernel, dim3(nch_b, B), kScanThreads, 0, st, logits_p, logits_q, K, V, nch_b, vec_ok,
+          temperature_p, temperature_q, sampler_x, c1, reinterpret_cast<float*>(part), dec);
   SSD_CHECK_LAUNCH();
   SSD_PDL(sample_draw_kernel, dim3(nch_b, B), kScanThreads, 0, st, 
-      logits_p, logits_q, u_gumbel, K, V, nch_b, temperature_p, temperature_q, sampler_x, c2,
+      logits_p, logits_q, u_gumbel, K, V, nch_b, vec_b, temperature_p, temperature_q, sampler_x, c2,
       reinterpret_cast<unsigned long long*>(part), dec, accept_until, recovery, accepted_mask);
   SSD_CHECK_LAUNCH();
   return SSD_OK;

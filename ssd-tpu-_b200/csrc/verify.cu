@@ -113,8 +113,14 @@ greedy_scan_kernel(const float* x, int64_t ld, int V, int kp1, int nchunks,
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
   __shared__ int tt[64];
+  __shared__ int s_spec[64];
   pdl_wait();
   const int row = blockIdx.y, c = blockIdx.x;
+  const int group = row / kp1;
+  // The drafted ids are read only by the group's last CTA, after the scan; every
+  // CTA issues their load now, so it lands while the slice streams in.
+  int my_spec = 0;
+  if (!argmax_out && threadIdx.x < kp1) my_spec = __ldcg(spec + (int64_t)group * kp1 + threadIdx.x);
   int lo, hi;
   chunk_bounds(V, nchunks, c, lo, hi);
   float best;
@@ -124,19 +130,21 @@ greedy_scan_kernel(const float* x, int64_t ld, int V, int kp1, int nchunks,
   if (threadIdx.x == 0) partial[(int64_t)row * nchunks + c] = key;
   pdl_trigger();
 
-  const int group = row / kp1;
   if (!last_block_of(&counters[group], (unsigned)(kp1 * nchunks), &is_last)) return;
 
-  // Fold the partials of every row of the group in chunk order.
-  for (int r = 0; r < kp1; ++r) {
+  // Fold the partials of every row of the group: one warp per row, all rows at
+  // once (the max of (value, index) keys does not depend on the order).
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = warp; r < kp1; r += kScanThreads / 32) {
     unsigned long long k = 0ull;
-    for (int i = threadIdx.x; i < nchunks; i += blockDim.x) {
-      unsigned long long v = __ldcg(&partial[(int64_t)(group * kp1 + r) * nchunks + i]);
+    for (int i = lane; i < nchunks; i += 32) {
+      const unsigned long long v = __ldcg(&partial[(int64_t)(group * kp1 + r) * nchunks + i]);
       k = v > k ? v : k;
     }
-    k = block_reduce(k, red, OpMax());
-    if (threadIdx.x == 0) tt[r] = k == 0ull ? 0 : (int)argmax_key_index(k);  // all-NaN row: token 0
+    k = warp_max_u64(k);
+    if (lane == 0) tt[r] = k == 0ull ? 0 : (int)argmax_key_index(k);  // all-NaN row: token 0
   }
+  if (threadIdx.x < kp1) s_spec[threadIdx.x] = my_spec;
   __syncthreads();
   if (threadIdx.x != 0) return;
   if (argmax_out) {  // argmax_rows: kp1 == 1
@@ -146,7 +154,7 @@ greedy_scan_kernel(const float* x, int64_t ld, int V, int kp1, int nchunks,
   const int K = kp1 - 1;
   const int b = group;
   int acc = 0;
-  while (acc < K && spec[(int64_t)b * kp1 + acc + 1] == tt[acc]) ++acc;
+  while (acc < K && s_spec[acc + 1] == tt[acc]) ++acc;
   accept_until[b] = acc;
   recovery[b] = tt[acc];  // == tt[K] when every draft token is accepted
   if (mask) {

@@ -266,17 +266,23 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   pdl_trigger();
 
   if (!last_block_of(&counters[b], (unsigned)(nR * nchunks), &is_last)) return;
-  // Fold chunk partials per row: M = max m_i, S = sum s_i * exp(m_i - M), chunk order.
-  for (int rr = threadIdx.x; rr < nR; rr += blockDim.x) {
-    const float2* pr = part + (int64_t)(b * nR + rr) * nchunks;
-    float M = -INFINITY;
-    for (int i = 0; i < nchunks; ++i) M = fmaxf(M, __ldcg(&pr[i].x));
-    float S = 0.f;
-    for (int i = 0; i < nchunks; ++i) {
-      float2 v = __ldcg(&pr[i]);
-      if (v.y > 0.f) S += v.y * expf(v.x - M);
+  // Fold chunk partials per row, one warp per row: M = max m_i, S = sum s_i * exp(m_i - M)
+  // (lane-strided over the chunks, then a fixed xor tree: deterministic).
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int rr = warp; rr < nR; rr += kScanThreads / 32) {
+      const float2* pr = part + (int64_t)(b * nR + rr) * nchunks;
+      float M = -INFINITY;
+      for (int i = lane; i < nchunks; i += 32) M = fmaxf(M, __ldcg(&pr[i].x));
+      M = warp_max(M);
+      float S = 0.f;
+      for (int i = lane; i < nchunks; i += 32) {
+        const float2 v = __ldcg(&pr[i]);
+        if (v.y > 0.f) S += v.y * expf(v.x - M);
+      }
+      S = warp_sum(S);
+      if (lane == 0) stats[rr] = make_float2(M, S);
     }
-    stats[rr] = make_float2(M, S);
   }
   // the logits of the drafted tokens that the accept loop reads, all K in one go
   // (not one dependent round trip per position)

@@ -30,7 +30,7 @@ def test_greedy_matches_reference_goldens(cuda, case):
     np.testing.assert_array_equal(res.accepted_mask.cpu().numpy(), mask)
 
 
-@pytest.mark.parametrize("b,k,v", [(8, 4, 256000), (32, 6, 32000), (3, 1, 4099), (1, 8, 7)])
+@pytest.mark.parametrize("b,k,v", [(8, 4, 256000), (32, 6, 32000), (3, 1, 4099), (1, 8, 7), (3, 63, 515)])
 def test_greedy_bit_exact_vs_oracle(cuda, b, k, v):
     from ssd_b200.algorithm.verify import verify_greedy
 
@@ -94,7 +94,8 @@ def _sample_inputs(b, k, v, seed, scale=3.0):
 
 
 @pytest.mark.parametrize("alignment", ["reference", "standard"])
-@pytest.mark.parametrize("b,k,v,tp,tq", [(8, 4, 256000, 1.0, 1.0), (6, 3, 4099, 0.7, 1.3), (16, 6, 1024, 1.0, 0.5)])
+@pytest.mark.parametrize("b,k,v,tp,tq", [(8, 4, 256000, 1.0, 1.0), (6, 3, 4099, 0.7, 1.3), (16, 6, 1024, 1.0, 0.5),
+                                          (2, 63, 300, 1.0, 1.0)])
 def test_sample_matches_oracle(cuda, alignment, b, k, v, tp, tq):
     from ssd_b200.algorithm.verify import verify_sample
 

@@ -1,6 +1,6 @@
 """CPU oracle for the speculative-decoding verify step — TEST INFRASTRUCTURE ONLY.
 
-This package is the checker, never the product: only ``tests/``,
+This package checks results and is never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm may
 import it.  The shipped path (``ssd_b200``) runs the CUDA library and fails
 loudly when that library is missing; it never routes through this code.

@@ -19,7 +19,7 @@ Usage (from the repository root, with the reference checkout available)::
     python tests/golden/make_golden.py /path/to/reference
 
 Writes ``tests/golden/verify_greedy.npz`` and ``tests/golden/page_manager.json``.
-The GPU box never runs this script; the committed fixtures travel instead.
+GPU test runs never execute this script; they read the committed fixtures.
 """
 
 from __future__ import annotations

@@ -1,4 +1,4 @@
-"""Tensor parallelism across GPUs: 2 ranks (and 4 / 8 when the box has them).
+"""Tensor parallelism across GPUs: 2 ranks (and 4 / 8 when the machine has them).
 
 Runs ``tests/tp_worker.py`` under torch.distributed.run; each rank compares its
 sharded forward with the unsharded forward of the same weights on its GPU

@@ -66,7 +66,7 @@ def test_oracle_page_manager_matches_reference_traces():
     assert len(scenarios) >= 8
     for scn in scenarios:
         _replay(scn)
-    # SURVEY-recorded answer of tests/test_page_rollback.py
+    # the reference's tests/test_page_rollback.py scenario, as its page manager answered it
     first = scenarios[0]["ops"]
     assert first[0]["after"]["block_tables"] == [[9, 8, 7, 6]]
     assert first[1]["after"]["block_tables"] == [[9, 8]]

@@ -63,7 +63,7 @@ size_t ssd_verify_greedy_workspace_size(int B, int K, int V);
  *   recovery      [B] int32 out: target argmax at position accept_until
  *   accepted_mask [B, K+1] uint8 out (may be NULL): [b,0]=0, [b,j+1]=(j<accept_until)
  *   target_tokens [B, K+1] int32 out (may be NULL): argmax of every row
- * argmax ties resolve to the first index.
+ * argmax ties resolve to the first index.  0 <= K <= 63 (else SSD_ERR_INVALID).
  */
 int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t* speculations,
                       int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
@@ -133,7 +133,7 @@ enum { SSD_ALIGN_REFERENCE = 0, SSD_ALIGN_STANDARD = 1 };
  * with the JAX threefry draws replaced by explicit uniforms:
  *   u_accept [B, K] in [0,1): draft token j is accepted iff u < min(1, p/max(q,1e-12))
  *   u_gumbel [B, V] in (0,1): categorical draw = argmax(log(r + 1e-12) - log(-log u))
- *   logits_q [B, K, V] fp32 draft logits; temperatures must be > 0.
+ *   logits_q [B, K, V] fp32 draft logits; temperatures must be > 0; 1 <= K <= 63.
  *   alignment SSD_ALIGN_REFERENCE judges draft token j+1 with target row j+1
  *   (verify.py:103 as written); SSD_ALIGN_STANDARD uses row j.
  */

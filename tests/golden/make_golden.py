@@ -14,11 +14,19 @@ Two pieces of the reference run without JAX and are executed here directly:
 The known answers of ``tests/test_spec_cache.py:6-20`` (JAX, not importable
 here) are transcribed as a small case list.
 
+``jax_ssd/models/toy_model.py`` (``ToyModelAdapter``) computes its logits in
+numpy and only wraps them with ``jax.numpy`` (``array``, ``argmax``, ``stack``).
+It is loaded by file path, with ``jax`` / ``jax.numpy`` replaced by a numpy
+stand-in for those three calls (plus the names that its imports only mention:
+``jnp.bfloat16`` as a default argument, ``jax.Array`` in annotations), so the
+reference's own code produces the toy golden vectors.
+
 Usage (from the repository root, with the reference checkout available)::
 
     python tests/golden/make_golden.py /path/to/reference
 
-Writes ``tests/golden/verify_greedy.npz`` and ``tests/golden/page_manager.json``.
+Writes ``tests/golden/verify_greedy.npz``, ``tests/golden/page_manager.json``,
+``tests/golden/spec_cache.json`` and ``tests/golden/toy_model.npz``.
 GPU test runs never execute this script; they read the committed fixtures.
 """
 
@@ -200,10 +208,52 @@ SPEC_CACHE_CASES = {
 }
 
 
+TOY_CASES = [(64, 32, 0), (100, 32, 3), (64, 16, 7)]  # (vocab_size, hidden_dim, seed)
+
+
+def make_toy(ref: Path) -> None:
+    saved = {k: sys.modules.get(k) for k in ("jax", "jax.numpy", "jax_ssd", "jax_ssd.kernels", "jax_ssd.models")}
+    jnp = types.ModuleType("jax.numpy")
+    jnp.array, jnp.argmax, jnp.stack = np.asarray, np.argmax, np.stack
+    jnp.bfloat16 = np.float32  # a default argument of KVCacheState.allocate, never called here
+    jax = types.ModuleType("jax")
+    jax.numpy, jax.Array = jnp, np.ndarray  # jax.Array only appears in annotations
+    sys.modules["jax"], sys.modules["jax.numpy"] = jax, jnp
+    for pkg in ("jax_ssd", "jax_ssd.kernels", "jax_ssd.models"):
+        m = types.ModuleType(pkg)
+        m.__path__ = []
+        sys.modules[pkg] = m
+    try:
+        _load("jax_ssd.kernels.kv_cache", ref / "jax_ssd" / "kernels" / "kv_cache.py")
+        _load("jax_ssd.models.base", ref / "jax_ssd" / "models" / "base.py")
+        toy = _load("jax_ssd.models.toy_model", ref / "jax_ssd" / "models" / "toy_model.py")
+        out = {}
+        for vocab, hidden, seed in TOY_CASES:
+            ad = toy.ToyModelAdapter(vocab_size=vocab, hidden_dim=hidden, seed=seed)
+            rng = np.random.default_rng(seed + 11)
+            ids = np.concatenate([np.arange(2 * hidden), rng.integers(0, 10 * vocab, 40)]).astype(np.int32)
+            name = f"v{vocab}_h{hidden}_s{seed}"
+            out[f"{name}__ids"] = ids
+            out[f"{name}__logits"] = np.asarray(ad.verify(ids, None, None, None).logits, dtype=np.float32)[0]
+            prefix = [int(t) for t in ids[:7]]
+            spec, lg = ad.draft_speculate(prefix, 5)
+            out[f"{name}__draft_prefix"] = np.asarray(prefix, dtype=np.int32)
+            out[f"{name}__draft_spec"] = np.asarray(spec, dtype=np.int32)
+            out[f"{name}__draft_logits"] = np.asarray(lg, dtype=np.float32)
+        np.savez_compressed(HERE / "toy_model.npz", **out)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+
+
 def main() -> None:
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
     make_verify(ref)
     make_page_manager(ref)
+    make_toy(ref)
     (HERE / "spec_cache.json").write_text(json.dumps(SPEC_CACHE_CASES, indent=1))
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
 

@@ -48,6 +48,17 @@ def verify_mask(seq_len: int, query_len: int) -> np.ndarray:
     return m
 
 
+def branch_mask(batch: int, num_branches: int, trunk_len: int, branch_len: int) -> np.ndarray:
+    """masks.py:8-30: every query sees the trunk; branch query i sees branch tokens 0..i."""
+    total = trunk_len + branch_len
+    m = np.full((batch * num_branches, total, total), -np.inf, np.float32)
+    for b in range(batch * num_branches):
+        m[b, :, :trunk_len] = 0.0
+        for i in range(branch_len):
+            m[b, trunk_len + i, trunk_len : trunk_len + i + 1] = 0.0
+    return m
+
+
 def attention_ref(q, k, v, mask):
     """attention_ref.py:9-21 in float64 (q[...,Tq,D], k/v[...,Tk,D])."""
     d = q.shape[-1]

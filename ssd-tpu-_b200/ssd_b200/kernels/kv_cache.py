@@ -45,6 +45,21 @@ def _dims(cache: KVCacheState):
     return nl, nb, bs, hkv, hd
 
 
+def gather_kv_for_positions(cache: KVCacheState, layer: int, page_table, positions) -> tuple[torch.Tensor, torch.Tensor]:
+    """K and V rows [n, num_kv_heads, head_dim] of one sequence's positions (kv_cache.py:61-72).
+
+    Slot of position p: page_table[p // block_size] * block_size + p % block_size, as in the
+    reference.  The reference computes the slots and returns zeros (its gather is a stub);
+    this returns the stored rows, in the cache's dtype.
+    """
+    dev = cache.pages.device
+    pt = torch.as_tensor(page_table).to(dev).long().reshape(-1)
+    pos = torch.as_tensor(positions).to(dev).long().reshape(-1)
+    blk = pt[pos // cache.block_size]
+    off = pos % cache.block_size
+    return cache.pages[0, layer, blk, off], cache.pages[1, layer, blk, off]
+
+
 def write_kv(cache: KVCacheState, layer: int, block_tables: torch.Tensor, positions: torch.Tensor,
              k: torch.Tensor, v: torch.Tensor) -> KVCacheState:
     """K2: write k/v [B,T,Hkv,D] at positions [B,T] (-1 = skip) through block_tables [B,M]."""

@@ -83,8 +83,12 @@ class GemmaAdapter:
         self.cached.extend(int(x) for x in tokens)
         return out
 
-    def allocate_kv(self) -> KVCacheState:
+    def reset_cache(self) -> None:
+        """Forget the cached tokens and release their pages (gemma_adapter.py:74-75)."""
         self._truncate(0)
+
+    def allocate_kv(self) -> KVCacheState:
+        self.reset_cache()
         return self.cache
 
     # ------------------------------------------------------------ protocol

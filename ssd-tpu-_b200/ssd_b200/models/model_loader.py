@@ -7,12 +7,24 @@ pair with ``use_toy``).  Weights are initialised on the device from the seed.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .gemma import PRESETS, GemmaWeights
 from .gemma_adapter import GemmaAdapter
 
 _SHARED: dict[tuple, GemmaWeights] = {}
+
+
+def default_target_path() -> str:
+    """TARGET_MODEL_PATH, else the Gemma-7B preset (model_loader.py:26-30 defaults to a checkpoint URL)."""
+    return os.getenv("TARGET_MODEL_PATH", "gemma-7b")
+
+
+def default_draft_path() -> str:
+    """DRAFT_MODEL_PATH, else the Gemma-2B preset (model_loader.py:33-37)."""
+    return os.getenv("DRAFT_MODEL_PATH", "gemma-2b")
 
 
 def default_preset(role: str, use_toy: bool) -> str:

@@ -30,12 +30,21 @@ from __future__ import annotations
 
 import queue
 import threading
+from dataclasses import dataclass
 
 import torch
 
 from ..algorithm.async_protocol import DraftCommand, DraftRequest, DraftResponse
 from ..algorithm.spec_cache import SpecCache
 from ..config import SSDConfig
+
+
+@dataclass
+class WorkerConfig:
+    """Worker options of the reference (workers.py:26-29); carried for callers that build one."""
+
+    use_toy: bool = True
+    instance_mode: bool = False
 
 
 class DraftWorker:
@@ -51,6 +60,12 @@ class DraftWorker:
         self.error: BaseException | None = None
         self.prefetch = True
         self.branches_drafted = 0
+        self._context_tokens: list[int] = []
+
+    def set_context(self, tokens: list[int]) -> None:
+        """Record the sequence's context tokens (workers.py:62-63).  Requests carry their own
+        committed prefix here, so drafting does not read it."""
+        self._context_tokens = [int(t) for t in tokens]
 
     def start(self) -> None:
         self._running = True

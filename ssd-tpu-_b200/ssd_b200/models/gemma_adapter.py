@@ -31,8 +31,18 @@ from .gemma import GemmaRunner, GemmaWeights
 
 
 class GemmaAdapter:
-    def __init__(self, weights: GemmaWeights, max_model_len: int = 4096, block_size: int = 16,
-                 max_tokens: int = 64, name: str = "gemma", max_branches: int = 0) -> None:
+    def __init__(self, weights: GemmaWeights | str | None = None, max_model_len: int = 4096, block_size: int = 16,
+                 max_tokens: int = 64, name: str = "gemma", max_branches: int = 0, *,
+                 model_path: str | None = None, vocab_size: int | None = None, share_key: str | None = None,
+                 mesh=None, devices=None, role: str = "target") -> None:
+        """``weights``: a ``GemmaWeights``, or a model path / preset name.  The reference's keyword form
+        (``model_path=``, ``role=``; gemma_adapter.py:35-72) also works: the path names a random-init
+        preset (``models.model_loader.load_weights``).  ``vocab_size``, ``share_key``, ``mesh`` and
+        ``devices`` configure the reference's JAX placement and have no effect here."""
+        if weights is None or isinstance(weights, str):
+            from .model_loader import load_weights
+
+            weights = load_weights(weights if isinstance(weights, str) else model_path, role=role)
         s = weights.shape
         self.w = weights
         self.name = name

@@ -50,3 +50,13 @@ def test_worker_and_loader_defaults(monkeypatch):
     monkeypatch.setenv("DRAFT_MODEL_PATH", "toy-draft")
     assert default_target_path() == "gemma-7b"
     assert default_draft_path() == "toy-draft"
+
+
+def test_gemma_adapter_takes_the_reference_keywords():
+    import inspect
+
+    from ssd_b200.models.gemma_adapter import GemmaAdapter
+
+    params = inspect.signature(GemmaAdapter.__init__).parameters
+    for name in ("model_path", "vocab_size", "share_key", "mesh", "devices", "role"):
+        assert name in params and params[name].kind is inspect.Parameter.KEYWORD_ONLY

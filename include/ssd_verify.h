@@ -78,9 +78,10 @@ int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, const int32_t*
  * Outputs and argument meaning are those of ssd_verify_greedy; it allocates
  * nothing.  Its scratch is a 34 KB array in the library's device data that
  * every GPU loading the library holds until exit.  Limits: B*(K+1) <= 512
- * (larger calls return SSD_ERR_UNSUPPORTED).  The first call on each device
- * looks up the array's device address with that device current; make that
- * first call before any stream capture.  All calls share the array, so calls
+ * (larger calls return SSD_ERR_UNSUPPORTED).  Every call looks up the array's
+ * device address on the caller's current device (no address is cached, so a
+ * device reset leaves nothing stale); call it with the device of `stream`
+ * current.  All calls share the array, so calls
  * that overlap on the GPU (different streams, or different host threads
  * without ordering) race and give wrong results.
  */
@@ -133,9 +134,11 @@ enum { SSD_ALIGN_REFERENCE = 0, SSD_ALIGN_STANDARD = 1 };
  * with the JAX threefry draws replaced by explicit uniforms:
  *   u_accept [B, K] in [0,1): draft token j is accepted iff u < min(1, p/max(q,1e-12))
  *   u_gumbel [B, V] in (0,1): categorical draw = argmax(log(r + 1e-12) - log(-log u))
- *   logits_q [B, K, V] fp32 draft logits; temperatures must be > 0; 1 <= K <= 63.
+ *   logits_q [B, K, V] fp32 draft logits; temperatures must be > 0; 0 <= K <= 63.
  *   alignment SSD_ALIGN_REFERENCE judges draft token j+1 with target row j+1
  *   (verify.py:103 as written); SSD_ALIGN_STANDARD uses row j.
+ *   K = 0 (as the reference allows): nothing is accepted and every row draws its
+ *   bonus token from softmax(lp[0] / Tp); logits_q and u_accept may then be NULL.
  */
 int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, const float* logits_q,
                       const int32_t* speculations, const float* u_accept, const float* u_gumbel,
@@ -326,6 +329,17 @@ int ssd_ipc_export(const void* ptr, void* handle, size_t* offset);
 int ssd_ipc_import(const void* handle, size_t offset, void** ptr);
 /* Unmap a buffer mapped by ssd_ipc_import. */
 int ssd_ipc_close(void* ptr, size_t offset);
+
+/*
+ * One process driving several GPUs (the engine's tensor-parallel group): let
+ * kernels on `device` read and write memory allocated on `peer` (NVLink peer
+ * access), so the heaps of a group can be plain device pointers instead of IPC
+ * mappings.  Already-enabled access is not an error; SSD_ERR_UNSUPPORTED when
+ * the pair has no peer path.  The caller's current device is left as it was.
+ * No reference counterpart (the reference places arrays with XLA meshes,
+ * connect/mesh_allocator.py:64-117).
+ */
+int ssd_enable_peer_access(int device, int peer);
 
 /*
  * Row-parallel projection + all-reduce + residual (the O and down projections

@@ -114,10 +114,14 @@ class OracleGemma:
         self.bf = precision == "bf16"
         r = bf16_round if self.bf else (lambda a: a.astype(np.float32))
         self.r = r
+        layers = weights["layers"]
+        # a callable fetches layer i on demand (full-depth checks of large models keep one layer
+        # in host memory at a time); its arrays must already be representable in the precision
+        self._layer_fn = layers if callable(layers) else None
         self.w = {
             "embed": r(weights["embed"]),
             "final_norm": r(weights["final_norm"]),
-            "layers": [{k: r(v) for k, v in lw.items()} for lw in weights["layers"]],
+            "layers": None if self._layer_fn else [{k: r(v) for k, v in lw.items()} for lw in layers],
         }
         self.cos, self.sin = rope_table(max_pos, shape.head_dim, shape.rope_theta)
         self.folded = bool(weights.get("folded", False))
@@ -190,7 +194,7 @@ class OracleGemma:
         x = self.embed(tokens)  # [B,T,d]
         nl = s.num_layers if stop_layer is None else stop_layer
         for li in range(nl):
-            lw = self.w["layers"][li]
+            lw = self._layer_fn(li) if self._layer_fn else self.w["layers"][li]
             if self.folded:
                 proj, h = self.linear_rownorm, x
             else:

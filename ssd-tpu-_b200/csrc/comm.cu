@@ -132,6 +132,32 @@ extern "C" int ssd_ipc_close(void* ptr, size_t offset) {
   return SSD_OK;
 }
 
+extern "C" int ssd_enable_peer_access(int device, int peer) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || peer < 0 || device >= n || peer >= n) {
+    (void)cudaGetLastError();
+    return SSD_ERR_INVALID;
+  }
+  if (device == peer) return SSD_OK;
+  int can = 0;
+  if (cudaDeviceCanAccessPeer(&can, device, peer) != cudaSuccess || !can) {
+    (void)cudaGetLastError();
+    return SSD_ERR_UNSUPPORTED;
+  }
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return SSD_ERR_LAUNCH;
+  int rc = SSD_OK;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    rc = SSD_ERR_LAUNCH;
+  } else {
+    const cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+    if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) rc = SSD_ERR_LAUNCH;
+    (void)cudaGetLastError();  // clear cudaErrorPeerAccessAlreadyEnabled
+  }
+  cudaSetDevice(cur);
+  return rc;
+}
+
 extern "C" int ssd_linear_allreduce(ssd_stream_t stream, const void* x, const void* w, void* y, int M, int N, int K,
                                     void* workspace, size_t workspace_bytes, const ssd_comm* comm) {
   return linear_allreduce_impl((cudaStream_t)stream, x, w, y, M, N, K, workspace, workspace_bytes, comm);

@@ -9,7 +9,7 @@
 // each CTA reduces its slice to a partial (argmax key, or max/sum-exp pair) in
 // the workspace, and the last CTA of a group (atomic ticket, self-resetting)
 // folds the partials in fixed chunk order, so results are deterministic.
-#include <mutex>
+
 
 #include "common.cuh"
 
@@ -733,28 +733,22 @@ extern "C" int ssd_verify_greedy(ssd_stream_t stream, const float* logits_p, con
 // device array instead of a caller workspace.  Every GPU that loads the library
 // holds these 34 KB until the process exits.  Host code must not use the array's
 // name as a pointer (on the host it is only a stand-in); the device address comes
-// from cudaGetSymbolAddress, looked up once per device.
+// from cudaGetSymbolAddress, looked up on every call with the caller's device
+// current (a cheap runtime query), so no stale address outlives a device reset.
 constexpr int kNoAllocMaxRows = 512;       // B * (K + 1)
 constexpr int kNoAllocMaxPartials = 4096;  // rows * chunks (at most 592 + rows in practice)
 constexpr size_t kNoAllocCounterBytes = sizeof(unsigned int) * kNoAllocMaxRows;
 static __device__ __align__(256) unsigned char g_greedy_scratch[kNoAllocCounterBytes +
                                                                 sizeof(unsigned long long) * kNoAllocMaxPartials];
 
-static std::mutex g_scratch_mu;
-static void* g_scratch_addr[64] = {};
-
-// Device address of g_greedy_scratch on the current device (looked up on the
-// first call per device, with that device current).
+// Device address of g_greedy_scratch on the current device.
 static int greedy_scratch_address(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSD_ERR_LAUNCH;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_greedy_scratch) != cudaSuccess || p == nullptr) return SSD_ERR_LAUNCH;
-    g_scratch_addr[dev] = p;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_greedy_scratch) != cudaSuccess || p == nullptr) {
+    (void)cudaGetLastError();
+    return SSD_ERR_LAUNCH;
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return SSD_OK;
 }
 
@@ -833,7 +827,7 @@ static void sample_layout(int B, int K, int V, int& nR, int& nch, size_t& off_pa
 }
 
 extern "C" size_t ssd_verify_sample_workspace_size(int B, int K, int V) {
-  if (B <= 0 || K <= 0 || V <= 0) return 0;
+  if (B <= 0 || K < 0 || V <= 0) return 0;
   int nR, nch;
   size_t a, b, t;
   sample_layout(B, K, V, nR, nch, a, b, t);
@@ -845,16 +839,22 @@ extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, con
                                  float temperature_p, float temperature_q, float sampler_x, int alignment,
                                  int32_t* accept_until, int32_t* recovery, uint8_t* accepted_mask,
                                  void* workspace, size_t workspace_bytes, int B, int K, int V) {
-  if (B <= 0 || K <= 0 || K > 63 || V <= 0 || !logits_p || !logits_q || !speculations || !u_accept ||
-      !u_gumbel || !accept_until || !recovery)
+  if (B <= 0 || K < 0 || K > 63 || V <= 0 || !logits_p || !speculations || !u_gumbel || !accept_until ||
+      !recovery)
     return SSD_ERR_INVALID;
+  if (K > 0 && (!logits_q || !u_accept)) return SSD_ERR_INVALID;
   if (!(temperature_p > 0.f) || !(temperature_q > 0.f)) return SSD_ERR_INVALID;
   if (alignment != SSD_ALIGN_REFERENCE && alignment != SSD_ALIGN_STANDARD) return SSD_ERR_INVALID;
   int nR, nch;
   size_t off_part, off_dec, total;
   sample_layout(B, K, V, nR, nch, off_part, off_dec, total);
   if (!workspace || workspace_bytes < total) return SSD_ERR_WORKSPACE;
-  const int off = alignment == SSD_ALIGN_REFERENCE ? 1 : 0;
+  // K = 0 (verify.py:98-114 with k = 0): nothing to accept, so every row draws its
+  // bonus token from softmax(lp[0] / Tp) -- the same under both alignments.  The
+  // draft logits are never read for a bonus draw; the kernels still form a draft
+  // row pointer, so they get the target rows instead of a possibly empty buffer.
+  const int off = (alignment == SSD_ALIGN_REFERENCE && K > 0) ? 1 : 0;
+  if (K == 0) logits_q = logits_p;
   const int rows = B * (2 * K + 1 - off);
   if (rows > 65535 || 3 * B > kCounterCap) return SSD_ERR_UNSUPPORTED;
   char* w = reinterpret_cast<char*>(workspace);

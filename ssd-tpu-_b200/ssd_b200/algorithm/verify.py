@@ -105,7 +105,7 @@ def verify_sample(logits_p, logits_q, speculations, key, *, temperature_p: float
     lq = _dev(logits_q, torch.float32)
     if top_p < 1.0:
         lp = top_p_mask_(lp.clone(), temperature_p, top_p)
-        lq = top_p_mask_(lq.clone(), temperature_q, top_p)
+        lq = top_p_mask_(lq.clone(), temperature_q, top_p) if lq.numel() else lq
     spec = _dev(speculations, torch.int32)
     b, kp1, v = lp.shape
     k = kp1 - 1

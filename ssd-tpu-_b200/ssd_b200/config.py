@@ -37,8 +37,12 @@ class SSDConfig:
     target_model_path: str | None = field(default_factory=lambda: os.getenv("TARGET_MODEL_PATH"))
     draft_model_path: str | None = field(default_factory=lambda: os.getenv("DRAFT_MODEL_PATH"))
     use_toy_model: bool = field(default_factory=lambda: _env_bool("SSD_USE_TOY_MODEL"))
-    # ssd mode: the draft model and its worker on their own GPU (e.g. "cuda:1"); None = the target's GPU
+    # ssd mode: the draft model and its worker on their own GPU (e.g. "cuda:1"); None = the next GPU after
+    # the target's tensor-parallel group when there is one, else the target's GPU
     draft_device: str | None = field(default_factory=lambda: os.getenv("SSD_DRAFT_DEVICE"))
+    # target tensor parallelism over GPUs 0..tensor_parallel_size-1 (one process, one thread per GPU);
+    # in sd and ar modes the draft is sharded over the same GPUs, in ssd mode it runs on draft_device
+    tensor_parallel_size: int = field(default_factory=lambda: int(os.getenv("SSD_TP_SIZE", "1")))
     tpu_role: str = field(default_factory=lambda: os.getenv("SSD_TPU_ROLE", "both").lower())
     mesh_allocation: object | None = None
     instance_context_ratio: float = 0.3

@@ -214,21 +214,26 @@ class GemmaWeights:
         """
         s = self.shape
         f = lambda x: x.float().cpu().numpy()  # noqa: E731
-        hq, hkv, hd = s.num_heads * s.head_dim, s.num_kv_heads * s.head_dim, s.head_dim
         out = {"embed": f(self.embed), "final_norm": f(self.final_norm), "layers": [], "folded": True}
         for l in range(s.num_layers if layers is None else layers):
-            qkv = f(self.w_qkv[l])
-            if self.qk_pairs:  # back to canonical row order
-                heads, D = s.num_heads + s.num_kv_heads, s.head_dim
-                qkv[:heads * D] = (qkv[:heads * D].reshape(heads, D // 2, 2, s.d_model)
-                                   .transpose(0, 2, 1, 3).reshape(heads * D, s.d_model))
-            gu = f(self.w_gate_up[l]).reshape(s.ffn, 2, s.d_model)
-            out["layers"].append({
-                "attn_norm": f(self.attn_norm[l]), "mlp_norm": f(self.mlp_norm[l]),
-                "wq": qkv[:hq], "wk": qkv[hq:hq + hkv], "wv": qkv[hq + hkv:],
-                "wo": f(self.w_o[l]), "wg": gu[:, 0], "wu": gu[:, 1], "wd": f(self.w_down[l]),
-            })
+            out["layers"].append(self.canonical_layer(l))
         return out
+
+    def canonical_layer(self, l: int) -> dict:
+        """Layer ``l`` of ``to_canonical`` alone (float32 numpy)."""
+        s = self.shape
+        f = lambda x: x.float().cpu().numpy()  # noqa: E731
+        hq, hkv = s.num_heads * s.head_dim, s.num_kv_heads * s.head_dim
+        qkv = f(self.w_qkv[l])
+        if self.qk_pairs:  # back to canonical row order
+            heads, D = s.num_heads + s.num_kv_heads, s.head_dim
+            qkv[:heads * D] = (qkv[:heads * D].reshape(heads, D // 2, 2, s.d_model)
+                               .transpose(0, 2, 1, 3).reshape(heads * D, s.d_model))
+        gu = f(self.w_gate_up[l]).reshape(s.ffn, 2, s.d_model)
+        return {"attn_norm": f(self.attn_norm[l]), "mlp_norm": f(self.mlp_norm[l]),
+                "wq": np.ascontiguousarray(qkv[:hq]), "wk": np.ascontiguousarray(qkv[hq:hq + hkv]),
+                "wv": np.ascontiguousarray(qkv[hq + hkv:]), "wo": f(self.w_o[l]),
+                "wg": np.ascontiguousarray(gu[:, 0]), "wu": np.ascontiguousarray(gu[:, 1]), "wd": f(self.w_down[l])}
 
     # ------------------------------------------------------------ C view
     def cstruct(self) -> GemmaWeightsC:

@@ -31,18 +31,30 @@ from .gemma import GemmaRunner, GemmaWeights
 
 
 class GemmaAdapter:
-    def __init__(self, weights: GemmaWeights | str | None = None, max_model_len: int = 4096, block_size: int = 16,
-                 max_tokens: int = 64, name: str = "gemma", max_branches: int = 0, *,
-                 model_path: str | None = None, vocab_size: int | None = None, share_key: str | None = None,
-                 mesh=None, devices=None, role: str = "target") -> None:
-        """``weights``: a ``GemmaWeights``, or a model path / preset name.  The reference's keyword form
-        (``model_path=``, ``role=``; gemma_adapter.py:35-72) also works: the path names a random-init
-        preset (``models.model_loader.load_weights``).  ``vocab_size``, ``share_key``, ``mesh`` and
-        ``devices`` configure the reference's JAX placement and have no effect here."""
-        if weights is None or isinstance(weights, str):
+    def __init__(self, model_path: GemmaWeights | str | None = None, vocab_size: int | None = None,
+                 share_key: str | None = None, mesh=None, devices=None, role: str = "target", *,
+                 max_model_len: int = 4096, block_size: int = 16, max_tokens: int = 64, name: str | None = None,
+                 max_branches: int = 0, comm=None) -> None:
+        """Positional arguments in the reference's order (gemma_adapter.py:28-36).
+
+        ``model_path``: a ``GemmaWeights`` already on the device, or a model path.  A path names a
+        random-init preset (``models.model_loader.load_weights``: a preset name, else the role's
+        default preset, the toy pair when ``SSD_USE_TOY_MODEL`` is set).  ``vocab_size``,
+        ``share_key``, ``mesh`` and ``devices`` place the reference's JAX arrays and have no effect
+        here (the vocabulary comes from the weights, as the reference takes it from the model
+        config).  Everything this adapter adds is keyword-only.
+
+        ``comm`` (a ``runtime.tensor_parallel.TPComm``): the weights are one rank's shard and
+        every rank of the group makes the same calls; logits land in the group's symmetric heap
+        (the LM head all-gathers into it) and are returned as copies."""
+        if isinstance(model_path, GemmaWeights):
+            weights = model_path
+        else:
+            from ..config import _env_bool
             from .model_loader import load_weights
 
-            weights = load_weights(weights if isinstance(weights, str) else model_path, role=role)
+            weights = load_weights(model_path, use_toy=_env_bool("SSD_USE_TOY_MODEL"), role=role)
+        name = name or role
         s = weights.shape
         self.w = weights
         self.name = name
@@ -56,14 +68,27 @@ class GemmaAdapter:
         self.num_blocks = per_seq + self.max_branches * 4
         self.dev = weights.device
         self.chunk = min(64, max_tokens_per_forward(weights.dtype))
-        self.runner = GemmaRunner(weights, 1 + self.max_branches, max(self.chunk, max_tokens), max_model_len)
+        self.comm = comm
+        self.runner = GemmaRunner(weights, 1 + self.max_branches, max(self.chunk, max_tokens), max_model_len,
+                                  comm=comm)
         self.cache = KVCacheState.allocate(s.num_layers, self.num_blocks, block_size, s.num_kv_heads, s.head_dim,
                                            dtype=weights.dtype, device=self.dev)
         self.pm = PageManager(block_size, self.num_blocks, max_seqs=1 + self.max_branches,
                               max_blocks_per_seq=per_seq, device=self.dev)
         self.cached: list[int] = []   # tokens whose K/V rows are valid in the cache
         self.pending: list[int] = []  # tokens of the last verify (written, not yet committed)
-        self._lg1 = torch.empty((1, s.vocab), dtype=torch.float32, device=self.dev)
+        # logits rows of one forward: a symmetric heap buffer under tensor parallelism
+        self._lg_rows = max(self.chunk, max_tokens, 1 + self.max_branches)
+        self._lg_heap = comm.alloc((self._lg_rows, s.vocab), torch.float32) if comm is not None else None
+        self._lg1 = self._logits(1)
+
+    def _logits(self, rows: int) -> torch.Tensor:
+        """A [rows, V] fp32 buffer the forward may write its logits into."""
+        if self._lg_heap is None:
+            return torch.empty((rows, self.vocab_size), dtype=torch.float32, device=self.dev)
+        if rows > self._lg_rows:
+            raise ValueError(f"{rows} logits rows exceed the adapter's {self._lg_rows}")
+        return self._lg_heap[:rows]
 
     # ------------------------------------------------------------ cache state
     def _i32(self, v) -> torch.Tensor:
@@ -120,13 +145,13 @@ class GemmaAdapter:
         if self.pending:
             self._truncate(len(self.cached))
         toks = [int(x) for x in torch.as_tensor(token_ids_kp1).reshape(-1).tolist()]
-        lg = torch.empty((1, len(toks), self.vocab_size), dtype=torch.float32, device=self.dev)
+        lg = self._logits(len(toks)).view(1, len(toks), self.vocab_size)
         n0 = len(self.cached)
         self.pm.allocate_rows(0, 1, self._i32(n0), self._i32(len(toks)), None)
         self.runner.forward(torch.tensor([toks], dtype=torch.int32, device=self.dev), self._i32(n0),
                             self.cache.pages, self.pm.tables, lg, last_only=False)
         self.pending = toks
-        return VerifyResultModel(logits=lg, kv_cache=self.cache)
+        return VerifyResultModel(logits=lg if self.comm is None else lg.clone(), kv_cache=self.cache)
 
     def commit_tokens(self, token_ids: list[int]) -> None:
         """After verify([r] + draft): token_ids = accepted + [new recovery] keeps r + accepted."""
@@ -212,7 +237,7 @@ class GemmaAdapter:
             qlen = torch.tensor(ql, dtype=torch.int32, device=self.dev)
             base = torch.full((n,), n0, dtype=torch.int32, device=self.dev)
             self.pm.allocate_rows(1, n, base, qlen + (k - 1), None)
-            lg = torch.empty((n, self.vocab_size), dtype=torch.float32, device=self.dev)
+            lg = self._logits(n)
             nxt = torch.empty((k, n), dtype=torch.int32, device=self.dev)
             tables = self.pm.tables[1:1 + n]
             self.runner.forward(toks, base, self.cache.pages, tables, lg, q_lens=qlen, last_only=True)

@@ -50,6 +50,31 @@ def load_weights(model_path: str | None, *, use_toy: bool = False, seed: int = 0
     return w
 
 
+def load_sharded_weights(model_path: str | None, rank: int, world: int, *, use_toy: bool = False, seed: int = 0,
+                         role: str = "target", device="cuda") -> GemmaWeights:
+    """Rank ``rank``'s tensor-parallel shard (``runtime.tensor_parallel.shard_weights``) of the
+    weights ``load_weights`` would give: the full model is drawn from the seed on ``device``, sharded,
+    and dropped, so every rank holds the same model's shard."""
+    from ..runtime.tensor_parallel import shard_weights
+
+    name = model_path if model_path in PRESETS else default_preset(role, use_toy)
+    if name.startswith("toy"):
+        raise ValueError("tensor parallelism runs on bf16 weights; the fp32 toy pair has no sharded path "
+                         "(the tp-target / tp-draft presets are small bf16 models)")
+    dev = torch.device(device)
+    key = (name, seed, str(dev), rank, world)
+    w = _SHARED.get(key)
+    if w is None:
+        with torch.cuda.device(dev):
+            full = GemmaWeights.random(PRESETS[name], seed=seed, dtype=torch.bfloat16, device=dev)
+            w = shard_weights(full, rank, world)
+            torch.cuda.current_stream(dev).synchronize()
+            del full
+            torch.cuda.empty_cache()
+        _SHARED[key] = w
+    return w
+
+
 def load_model_adapter(model_path: str | None, *, use_toy: bool = False, seed: int = 0, share_key=None,
                        mesh=None, devices=None, role: str = "target", max_model_len: int = 4096) -> GemmaAdapter:
     w = load_weights(model_path, use_toy=use_toy, seed=seed, role=role)

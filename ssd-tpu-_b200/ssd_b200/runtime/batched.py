@@ -122,22 +122,38 @@ class BatchedSpeculativeDecoder:
                              last_only=True)
         m.n[b] = n
 
+    def admit(self, b: int, prompt: list[int]) -> int:
+        """Seat ``prompt`` in row ``b`` (continuous batching): release the row's pages in both
+        caches, prefill it on both models, and return its first token (target argmax).  The
+        other rows keep their state; the next ``step`` decodes all rows together."""
+        prompt = [int(t) for t in prompt]
+        if not prompt:
+            raise ValueError("empty prompt")
+        for m in (self.t, self.d):
+            m.pm.free_rows(b, 1)
+            m.n[b] = 0
+        self._prefill(self.t, b, prompt, True)
+        first = torch.empty(1, dtype=torch.int32, device=self.dev)
+        argmax_rows(self.logits_d[b:b + 1], first)
+        self._prefill(self.d, b, prompt, False)
+        f = int(first.item())
+        self.seqs[b] = prompt + [f]
+        self.out[b] = [f]
+        self._roll[:, b] = (self.t.n[b], 0, self.d.n[b], 0)
+        self._rec[b] = f
+        self.last_accept[b] = 0
+        return f
+
+    def park(self, b: int) -> None:
+        """Put row ``b`` on a one-token placeholder sequence (a finished row with nothing to
+        replace it keeps stepping with the batch; its tokens are not used)."""
+        self.admit(b, [0])
+
     def start(self, prompts: list[list[int]]) -> list[int]:
         """Prefill every sequence on both models; returns each one's first token (target argmax)."""
         if len(prompts) != self.B:
             raise ValueError(f"expected {self.B} prompts")
-        first = torch.zeros(self.B, dtype=torch.int32, device=self.dev)
-        for b, pr in enumerate(prompts):
-            self._prefill(self.t, b, list(pr), True)
-            argmax_rows(self.logits_d[b:b + 1], first[b:b + 1])
-            self._prefill(self.d, b, list(pr), False)
-        f = [int(x) for x in first.cpu().tolist()]
-        for b in range(self.B):
-            self.seqs[b] = list(prompts[b]) + [f[b]]
-            self.out[b] = [f[b]]
-        self._roll = np.stack([self.t.n, np.zeros(self.B, np.int64), self.d.n, np.zeros(self.B, np.int64)])
-        self._rec = np.asarray(f, np.int64)
-        return f
+        return [self.admit(b, pr) for b, pr in enumerate(prompts)]
 
     def start_synthetic(self, contexts: list[int], rng: np.random.Generator) -> None:
         """Stand-in for a long prefill: allocate each sequence's context pages and fill both caches

@@ -64,7 +64,10 @@ class PageManager:
         r = self._rows.get(seq.seq_id)
         if r is None:
             used = set(self._rows.values())
-            r = next(i for i in range(self.max_seqs) if i not in used)
+            r = next((i for i in range(self.max_seqs) if i not in used), None)
+            if r is None:
+                raise RuntimeError(f"all {self.max_seqs} sequence slots of the page manager are in use; "
+                                   "free_sequence() releases a finished sequence's slot")
             self._rows[seq.seq_id] = r
             # adopt any blocks the host object already lists
             if seq.block_table:
@@ -109,7 +112,7 @@ class PageManager:
         self._sync_seq(seq, r)
 
     def free_sequence(self, seq: Sequence) -> None:
-        """page_manager.py:58-64."""
+        """page_manager.py:58-64; the sequence's device slot is released too."""
         r = self.row(seq)
         rel = torch.ones(1, dtype=torch.uint8, device=self.device)
         check(lib().ssd_page_free(stream_ptr(), ptr(self.tables[r]), ptr(self.lens[r:]), self.max_blocks,
@@ -117,6 +120,7 @@ class PageManager:
                                   ptr(self.free_list), ptr(self.free_top), ptr(self.ref_counts_dev),
                                   self.num_blocks, ptr(rel), 1), "ssd_page_free")
         self._sync_seq(seq, r)
+        self._rows.pop(seq.seq_id, None)
 
     # ------------------------------------------------ batched, sync-free calls
     def allocate_rows(self, row0: int, n: int, num_tokens: torch.Tensor, num_new: torch.Tensor,
@@ -163,5 +167,5 @@ class PageManager:
                                   self.num_blocks, ptr(rel), self.max_seqs), "ssd_page_free")
 
     def release(self, seq: Sequence) -> None:
-        """Forget the slot of a freed sequence."""
+        """Forget the slot of a sequence without freeing its blocks (``free_sequence`` does both)."""
         self._rows.pop(seq.seq_id, None)

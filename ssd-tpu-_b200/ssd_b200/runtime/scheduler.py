@@ -1,67 +1,79 @@
-"""Request scheduler (jax_ssd/runtime/scheduler.py:12-77) over the device page manager."""
+"""Slot scheduler for the batched serving loop.
+
+The reference's scheduler (jax_ssd/runtime/scheduler.py:12-77) keeps a
+waiting deque and a running list and reserves KV pages on the host that its
+model never reads; its engine then decodes one prompt at a time
+(jax_ssd/runtime/engine.py:110-125).  Here the KV pages live on the device with
+each decoder (``PageManager`` rows), and one decoder step advances a fixed set
+of B rows together.  This scheduler's job is the mapping between requests and
+those rows ("slots"):
+
+* ``add_request`` queues a prompt as a ``Sequence`` (WAITING);
+* ``admit`` places waiting sequences into free slots, first come first served,
+  and returns the (slot, sequence) pairs the decoder must prefill;
+* ``retire`` frees a slot whose sequence has finished, so the next ``admit``
+  refills it while the other rows keep decoding (continuous batching);
+* ``slots`` lists the occupied slots in slot order.
+
+A slot with no sequence still steps inside the decoder (its rows are part of
+the fixed-shape batch); the engine parks it on a one-token dummy sequence and
+ignores what it produces.
+"""
 
 from __future__ import annotations
 
 from collections import deque
 
-from ..config import DecodeMode, SSDConfig
-from .page_manager import PageManager
 from .sequence import Sequence, SequenceStatus
 
 
 class Scheduler:
-    def __init__(self, config: SSDConfig, page_manager: PageManager) -> None:
-        self.config = config
-        self.page_manager = page_manager
+    def __init__(self, num_slots: int) -> None:
+        if num_slots < 1:
+            raise ValueError("the scheduler needs at least one slot")
+        self.num_slots = int(num_slots)
         self.waiting: deque[Sequence] = deque()
-        self.running: list[Sequence] = []
         self.finished: list[Sequence] = []
-        self._next_id = 0
+        self._slot_seq: list[Sequence | None] = [None] * self.num_slots
+        self._ids = 0
 
+    # ------------------------------------------------------------ queue
     def add_request(self, prompt_token_ids: list[int]) -> Sequence:
-        seq = Sequence(seq_id=self._next_id, prompt_token_ids=list(prompt_token_ids))
-        self._next_id += 1
+        seq = Sequence(seq_id=self._ids, prompt_token_ids=[int(t) for t in prompt_token_ids])
+        self._ids += 1
         self.waiting.append(seq)
         return seq
 
-    def schedule(self) -> list[Sequence]:
-        scheduled = []
-        while self.waiting and len(self.running) < 16:
-            seq = self.waiting.popleft()
-            reserve = self._reserve_tokens()
-            if not self.page_manager.allocate(seq, reserve):
-                self.waiting.appendleft(seq)
+    def has_work(self) -> bool:
+        return bool(self.waiting) or any(s is not None for s in self._slot_seq)
+
+    # ------------------------------------------------------------ slots
+    @property
+    def running(self) -> list[Sequence]:
+        return [s for s in self._slot_seq if s is not None]
+
+    def slots(self) -> list[tuple[int, Sequence]]:
+        return [(i, s) for i, s in enumerate(self._slot_seq) if s is not None]
+
+    def free_slots(self) -> list[int]:
+        return [i for i, s in enumerate(self._slot_seq) if s is None]
+
+    def admit(self) -> list[tuple[int, Sequence]]:
+        placed = []
+        for slot in self.free_slots():
+            if not self.waiting:
                 break
-            if self.config.mode in (DecodeMode.SD, DecodeMode.SSD, DecodeMode.INSTANCE):
-                draft_reserve = reserve + self.config.speculate_k * self.config.mq_len
-                if not self.page_manager.allocate_draft(seq, draft_reserve):
-                    self.waiting.appendleft(seq)
-                    break
+            seq = self.waiting.popleft()
             seq.status = SequenceStatus.RUNNING
-            self.running.append(seq)
-            scheduled.append(seq)
-        return scheduled
+            self._slot_seq[slot] = seq
+            placed.append((slot, seq))
+        return placed
 
-    def _reserve_tokens(self) -> int:
-        return 1 if self.config.mode == DecodeMode.AR else self.config.speculate_k + 1
-
-    def _finish(self, seq: Sequence) -> None:
+    def retire(self, slot: int) -> Sequence:
+        seq = self._slot_seq[slot]
+        if seq is None:
+            raise ValueError(f"slot {slot} holds no sequence")
         seq.status = SequenceStatus.FINISHED
-        if seq in self.running:
-            self.running.remove(seq)
-        self.page_manager.free_sequence(seq)
-        self.page_manager.release(seq)
+        self._slot_seq[slot] = None
         self.finished.append(seq)
-
-    def postprocess(self, seq: Sequence, new_tokens: list[int], eos_id: int | None, max_tokens: int) -> None:
-        seq.append_tokens(new_tokens)
-        if seq.is_finished(eos_id, max_tokens):
-            self._finish(seq)
-
-    def postprocess_speculative(self, seq: Sequence, accepted_tokens: list[int], recovery: int, reserved: int,
-                                eos_id: int | None, max_tokens: int) -> None:
-        seq.append_tokens(accepted_tokens)
-        seq.recovery_token = recovery
-        self.page_manager.rollback_speculative(seq, len(accepted_tokens), reserved)
-        if seq.is_finished(eos_id, max_tokens):
-            self._finish(seq)
+        return seq

@@ -90,6 +90,7 @@ class SpeculativeDecoder:
                           torch.cuda.Event(enable_timing=True, external=True))
         self.use_graphs = use_graphs
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._capture_stream: torch.cuda.Stream | None = None
         self._seen: dict[int, int] = {}
         self._graph_prof = timer  # projection timer bound into the step (eager or captured)
         self.last_verify_ms = 0.0
@@ -196,8 +197,12 @@ class SpeculativeDecoder:
         elif self.use_graphs and self._seen.get(nf, 0) >= 1:
             # second sighting of this shape: capture (first run was eager, so every
             # lazily created buffer and cached tensor map already exists), then replay
+            # capture on this decoder's own stream, thread-local: under a DeviceGroup every GPU's
+            # thread captures its own step at the same time
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            if self._capture_stream is None:
+                self._capture_stream = torch.cuda.Stream(device=self.dev)
+            with torch.cuda.graph(g, stream=self._capture_stream, capture_error_mode="thread_local"):
                 self._device_step(nf, prof=self._graph_prof)
             self._graphs[nf] = g
             g.replay()

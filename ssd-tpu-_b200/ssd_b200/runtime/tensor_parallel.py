@@ -38,15 +38,19 @@ class TPComm:
     ``alloc`` must be called with the same sizes in the same order on every
     rank (buffers are symmetric by construction).  ``world == 1`` needs no
     process group: the collective kernels then run against the local heap only
-    (used to exercise the fused path on one GPU).
+    (used to exercise the fused path on one GPU).  One process driving several
+    GPUs builds its group with ``TPComm.local_group`` instead (NVLink peer
+    access, no IPC).
     """
 
     def __init__(self, heap_bytes: int = 256 << 20, max_m: int = 256, max_n: int = 8192, group=None,
-                 device=None):
+                 device=None, *, _local: tuple | None = None):
         import torch.distributed as dist
 
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        if dist.is_available() and dist.is_initialized():
+        if _local is not None:
+            self.rank, self.world = _local[0], _local[1]
+        elif dist.is_available() and dist.is_initialized():
             self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         else:
             self.rank, self.world = 0, 1
@@ -60,8 +64,11 @@ class TPComm:
         self.heap = torch.zeros(heap_bytes, dtype=torch.uint8, device=self.device)
         torch.cuda.synchronize(self.device)
         self._top = fixed
-        peers: list[int] = []
         self._imported: list[tuple[int, int]] = []
+        self.heap_bytes, self.max_m, self.max_n = heap_bytes, max_m, max_n
+        if _local is not None:
+            return  # local_group fills in the peers
+        peers: list[int] = []
         if self.world > 1:
             handle = (C.c_char * 64)()
             off = C.c_size_t(0)
@@ -83,17 +90,45 @@ class TPComm:
             dist.barrier(group=group)
         else:
             peers = [self.heap.data_ptr()]
+        self._bind(peers)
+
+    def _bind(self, peers: list[int]) -> None:
         c = CommC()
         c.rank, c.world = self.rank, self.world
         for r in range(SSD_MAX_TP):
             c.heaps[r] = peers[r] if r < self.world else None
-        c.heap_bytes = heap_bytes
+        c.heap_bytes = self.heap_bytes
         c.ctrl_offset = 0
         c.recv_offset = self.ctrl_bytes
         c.recv_bytes = self.recv_bytes
-        c.recv_rows, c.recv_tiles = max_m, (max_n + 127) // 128
+        c.recv_rows, c.recv_tiles = self.max_m, (self.max_n + 127) // 128
         self.cstruct = c
-        self.max_m, self.max_n = max_m, max_n
+
+    @classmethod
+    def local_group(cls, devices, heap_bytes: int = 256 << 20, max_m: int = 256,
+                    max_n: int = 8192) -> list["TPComm"]:
+        """One rank per GPU of ``devices``, all driven by this process: every heap is a
+        plain device allocation and every GPU gets NVLink peer access to the others
+        (``ssd_enable_peer_access``), so each rank's handle lists the others' heaps
+        directly.  Returns the ranks in order."""
+        devs = [torch.device(d) if not isinstance(d, int) else torch.device("cuda", d) for d in devices]
+        idx = [d.index for d in devs]
+        if len(set(idx)) != len(idx):
+            raise ValueError("tensor-parallel ranks must sit on distinct GPUs")
+        world = len(devs)
+        L = lib()
+        for a in idx:
+            for b in idx:
+                if a != b:
+                    check(L.ssd_enable_peer_access(a, b), f"ssd_enable_peer_access({a}, {b})")
+        ranks = []
+        for r, d in enumerate(devs):
+            with torch.cuda.device(d):
+                ranks.append(cls(heap_bytes, max_m, max_n, device=d, _local=(r, world)))
+        peers = [c.heap.data_ptr() for c in ranks]
+        for c in ranks:
+            c._bind(peers)
+        return ranks
 
     def alloc(self, shape, dtype=torch.float32) -> torch.Tensor:
         """A symmetric buffer (same heap offset on every rank), 256-byte aligned, zero-filled."""
@@ -106,6 +141,17 @@ class TPComm:
             raise MemoryError(f"symmetric heap exhausted ({self.heap.numel()} bytes)")
         self._top = start + nbytes
         return self.heap[start:start + nbytes].view(dtype).view(*shape)
+
+    def mark(self) -> int:
+        """The allocator's current top; ``release(mark)`` frees everything allocated after it."""
+        return self._top
+
+    def release(self, mark: int) -> None:
+        """Free the buffers allocated since ``mark`` (same call on every rank; their tensors must
+        no longer be used)."""
+        if not 0 <= mark <= self._top:
+            raise ValueError("release() needs a mark taken from this heap")
+        self._top = mark
 
     def status(self) -> int:
         """Word 2 of the control block: 0, or SSD_ERR_TIMEOUT after a peer wait gave up."""
@@ -171,3 +217,72 @@ def shard_weights(full, rank: int, world: int):
     w.tp_rank, w.tp_world = rank, world
     w.qk_pairs = full.qk_pairs  # head blocks of rotation-paired rows stay paired
     return w
+
+
+def tp_selfcheck(all_gather, device=None, heap_bytes: int = 64 << 20) -> dict:
+    """Consistency checks of the sharded path, run by every rank of an initialised process group.
+
+    On the small bf16 ``tp-target`` / ``tp-draft`` presets (seeded weights, every projection on the
+    tcgen05 path at 1..8 ranks):
+
+    * ``ranks_identical``: every rank holds bit-identical logits after the sharded forward (the
+      collectives add the ranks' partials in rank order on every rank);
+    * ``max_diff`` / ``scale``: the sharded forward against the unsharded forward of the same
+      weights on this GPU, |difference| <= 2e-2 * max(max|logit|, 1) (bf16 rounding of the partial
+      sums is the only difference);
+    * ``sd_equals_ar``: greedy speculative decoding on the sharded pair reproduces the sharded
+      target's AR stream (``self_sd_equals_ar``: with the target as its own draft, every draft is
+      accepted and the stream is still the AR stream).
+
+    ``all_gather(tensor) -> list[tensor]`` gathers a CUDA tensor from every rank.  Returns a dict;
+    ``ok`` is the conjunction of the checks and of a zero collective status.
+    """
+    from ..kernels.kv_cache import KVCacheState
+    from ..models.gemma import PRESETS, GemmaRunner, GemmaWeights
+    from .speculative import GreedyDecoder, SpeculativeDecoder
+
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    comm = TPComm(heap_bytes=heap_bytes, max_m=256, max_n=4096, device=dev)
+    rank, world = comm.rank, comm.world
+    out: dict = {"world": world}
+    ok = True
+    for name in ("tp-target", "tp-draft"):
+        s = PRESETS[name]
+        full = GemmaWeights.random(s, seed=31, device=dev, max_pos=512)
+        local = shard_weights(full, rank, world)
+        toks = torch.arange(3, 3 + 29, device=dev, dtype=torch.int32)[None] % s.vocab
+        res = {}
+        for tag, w, c in (("full", full, None), ("tp", local, comm)):
+            ls = w.shape
+            cache = KVCacheState.allocate(ls.num_layers, 8, 16, ls.num_kv_heads, ls.head_dim, torch.bfloat16, dev)
+            table = torch.arange(8, dtype=torch.int32, device=dev)[None]
+            lg = comm.alloc((1, 29, s.vocab)) if c is not None else torch.empty((1, 29, s.vocab), device=dev)
+            GemmaRunner(w, 1, 64, 128, comm=c).forward(toks, torch.zeros(1, dtype=torch.int32, device=dev),
+                                                       cache.pages, table, lg)
+            torch.cuda.synchronize(dev)
+            res[tag] = lg.clone()
+        diff = (res["tp"] - res["full"]).abs().max().item()
+        scale = res["full"].abs().max().item()
+        gathered = all_gather(res["tp"])
+        same = all(torch.equal(g, gathered[0]) for g in gathered)
+        good = same and diff <= 2e-2 * max(scale, 1.0)
+        out[name] = {"max_diff": diff, "scale": scale, "ranks_identical": same, "ok": good}
+        ok = ok and good
+    t = shard_weights(GemmaWeights.random(PRESETS["tp-target"], seed=41, device=dev, max_pos=512), rank, world)
+    d = shard_weights(GemmaWeights.random(PRESETS["tp-draft"], seed=42, device=dev, max_pos=512), rank, world)
+    prompt = list(range(50, 90))
+    ar = GreedyDecoder(t, max_seq_len=256, comm=comm).generate(prompt, 32)
+    sd, _ = SpeculativeDecoder(t, d, k=4, max_seq_len=256, comm=comm).generate(prompt, 32)
+    self_sd, st = SpeculativeDecoder(t, t, k=4, max_seq_len=256, comm=comm).generate(prompt, 32)
+    out["ar"] = ar
+    out["sd_equals_ar"] = sd == ar
+    out["self_sd_equals_ar"] = self_sd == ar
+    out["self_sd_steps"] = st["steps"]
+    torch.cuda.synchronize(dev)
+    out["status"] = comm.status()
+    ars = all_gather(torch.tensor(ar, dtype=torch.int32, device=dev))
+    out["ar_identical_across_ranks"] = all(torch.equal(a, ars[0]) for a in ars)
+    out["ok"] = bool(ok and out["sd_equals_ar"] and out["self_sd_equals_ar"] and out["status"] == 0
+                     and out["ar_identical_across_ranks"] and st["steps"] < 32)
+    comm.close()
+    return out

@@ -155,7 +155,83 @@ def test_ssd_draft_on_its_own_gpu(cuda):
     ref, _ = ar.generate([prompt], sampling)
     ar.shutdown()
     llm = LLM(SSDConfig(mode=DecodeMode.SSD, use_toy_model=True, draft_device="cuda:1"))
-    assert llm._engine.draft_w.device == torch.device("cuda", 1)
+    assert llm._engine.draft_w[0].device == torch.device("cuda", 1)
     out, m = llm.generate([prompt], sampling)
     llm.shutdown()
     assert out[0] == ref[0] and m.total_tokens > 0
+
+
+def test_adapter_built_from_a_model_path(cuda):
+    """The reference's construction forms (gemma_adapter.py:28-36): by keyword and by position.
+    With SSD_USE_TOY_MODEL set (tests/conftest.py), a path that names no preset gives the toy
+    model of the role, and the second positional argument is the vocabulary size (ignored:
+    the vocabulary comes from the weights), never a cache size."""
+    from ssd_b200.models.gemma import PRESETS
+    from ssd_b200.models.gemma_adapter import GemmaAdapter
+
+    a = GemmaAdapter(model_path="toy-target", role="target")
+    b = GemmaAdapter("some/checkpoint/dir", 256000)
+    assert a.w.shape == b.w.shape == PRESETS["toy-target"]
+    assert b.vocab_size == PRESETS["toy-target"].vocab and b.max_model_len == 4096
+    prompt = torch.tensor(list(range(3, 20)))
+    ra, rb = a.prefill(prompt), b.prefill(prompt)
+    torch.testing.assert_close(ra.logits, rb.logits, rtol=0, atol=0)
+    da = a.decode(int(ra.logits[0].argmax()))
+    assert 0 <= da.next_token < a.vocab_size
+
+
+def _tp_pair_config(mode, **kw):
+    from ssd_b200 import DecodeMode, SSDConfig
+
+    return SSDConfig(mode=DecodeMode(mode), target_model_path="tp-target", draft_model_path="tp-draft",
+                     use_toy_model=False, **kw)
+
+
+def test_engine_batches_several_prompts(cuda):
+    """sd with several prompts runs them through the batched decoder, 4 rows at a time with
+    refills (continuous batching); every stream equals the prompt's own AR stream."""
+    from ssd_b200 import LLM, SamplingParams
+
+    rng = np.random.default_rng(3)
+    prompts = [[int(x) for x in rng.integers(0, 2048, n)] for n in (9, 40, 3, 77, 21, 55)]
+    sampling = SamplingParams(max_new_tokens=14)
+    ar = LLM(_tp_pair_config("ar"))
+    refs = [ar.generate([p], sampling)[0][0] for p in prompts]
+    ar.shutdown()
+    llm = LLM(_tp_pair_config("sd", batch_buckets=(1, 2, 4)))
+    got, m = llm.generate(prompts, sampling)
+    llm.shutdown()
+    assert got == refs
+    assert m.total_tokens == 6 * 14 and max(s.sequences for s in m.steps) == 4
+    # sampling (temperature > 0) also takes the batched path: reproducible for the engine's seed
+    llm = LLM(_tp_pair_config("sd"))
+    hot = SamplingParams(max_new_tokens=10, temperature=1.0, top_p=0.9)
+    a, _ = llm.generate(prompts[:3], hot)
+    b, _ = llm.generate(prompts[:3], hot)
+    llm.shutdown()
+    assert a == b and all(len(x) == 10 for x in a)
+
+
+def test_engine_tensor_parallel_modes(cuda):
+    """The engine's target sharded over 2 GPUs in one process (one thread per GPU): sd and ssd
+    reproduce the sharded AR stream; in ssd mode the draft runs on the next GPU when there is one."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from ssd_b200 import LLM, SamplingParams
+
+    prompt = list(range(100, 160))
+    sampling = SamplingParams(max_new_tokens=24)
+    outs = {}
+    for mode in ("ar", "sd", "ssd"):
+        llm = LLM(_tp_pair_config(mode, tensor_parallel_size=2, fan_out_list=(3, 3, 3, 3, 3)))
+        if mode == "ssd":
+            want = torch.device("cuda", 2) if torch.cuda.device_count() > 2 else torch.device("cuda", 0)
+            assert llm._engine.draft_device == want
+        out, m = llm.generate([prompt], sampling)
+        if mode == "sd":
+            two, _ = llm.generate([prompt, prompt[:30]], sampling)  # batched, sharded
+            assert two[0] == out[0]
+        llm.shutdown()
+        outs[mode] = out[0]
+        assert len(out[0]) == 24 and m.total_tokens == 24
+    assert outs["ar"] == outs["sd"] == outs["ssd"]

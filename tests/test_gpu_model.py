@@ -105,6 +105,45 @@ def test_gemma2b_mqa_layer_shapes_bf16(cuda):
     assert np.abs(got - ref).max() < 2e-2
 
 
+def _full_depth_verify_check(preset, seed, prompt_len, k):
+    """One verify forward of the whole model (every layer, the full vocabulary) after a
+    ``prompt_len``-token prompt, against the bf16 oracle of the same weights.  The oracle
+    fetches one layer at a time from the device (``GemmaWeights.canonical_layer``), so host
+    memory holds the embedding plus one layer."""
+    import torch
+
+    from ssd_b200.models.gemma import PRESETS, GemmaWeights
+
+    shape = PRESETS[preset]
+    w = GemmaWeights.random(shape, seed=seed, dtype=torch.bfloat16, max_pos=1024)
+    rng = np.random.default_rng(seed)
+    prompt = [int(x) for x in rng.integers(0, shape.vocab, prompt_len)]
+    vt = [int(x) for x in rng.integers(0, shape.vocab, k + 1)]
+    got = _run_forward(w, prompt, vt)
+    full = w.to_canonical(layers=0)
+    full["layers"] = w.canonical_layer
+    om = OracleGemma(_oshape(shape), full, "bf16", max_pos=1024)
+    n = len(prompt) + len(vt)
+    nb = (n + 15) // 16 + 1
+    pages = new_pages(om.s, nb, 16)
+    table = np.arange(nb, dtype=np.int32)[None]
+    om.forward(np.array([prompt]), pages, table, [0], with_head=False)
+    ref = om.forward(np.array([vt]), pages, table, [len(prompt)])[0]
+    return got, ref
+
+
+@pytest.mark.parametrize("preset,seed", [("gemma-7b", 1000), ("gemma-2b", 2000)])
+def test_full_depth_verify_logits_within_2e2(cuda, preset, seed):
+    """The benchmarked models at full depth: Gemma-7B (28 layers) and Gemma-2B (18 layers), vocab
+    256000, verify over k+1 = 5 tokens after a 128-token prompt; |GPU - oracle| <= 2e-2 (bf16)."""
+    got, ref = _full_depth_verify_check(preset, seed, 128, 4)
+    err = np.abs(got - ref)
+    print(f"{preset}: max |dlogit| = {err.max():.3e}, mean = {err.mean():.3e}, "
+          f"logit std = {ref.std():.3e}, argmax agreement = {(got.argmax(-1) == ref.argmax(-1)).mean():.2f}")
+    assert err.max() <= 2e-2, err.max()
+    assert (got.argmax(-1) == ref.argmax(-1)).mean() >= 0.8
+
+
 def test_toy_gpu_ar_stream_matches_oracle(cuda):
     """Greedy streams identical to the oracle's on >= 99% of seeded prompts (toy pair, fp32)."""
     import torch

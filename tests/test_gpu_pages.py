@@ -123,3 +123,23 @@ def test_batched_allocate_bit_exact(cuda, nseq):
     np.testing.assert_array_equal(ln.cpu().numpy(), exp[1])
     assert int(top.item()) == int(exp[3])
     np.testing.assert_array_equal(rc.cpu().numpy(), exp[4])
+
+
+def test_reference_api_reuses_freed_slots(cuda):
+    # More sequences than device slots through allocate / free_sequence (page_manager.py:21-64): a freed
+    # sequence gives its slot back, and a full manager says so instead of failing inside a generator.
+    from ssd_b200.runtime.page_manager import PageManager
+    from ssd_b200.runtime.sequence import Sequence
+
+    pm = PageManager(16, 64, max_seqs=4)
+    for i in range(3 * pm.max_seqs):
+        s = Sequence(seq_id=i, prompt_token_ids=list(range(20)))
+        assert pm.allocate(s, 5)
+        assert len(s.block_table) == 2
+        pm.free_sequence(s)
+        assert s.block_table == [] and sorted(pm.free_blocks) == list(range(64)) and pm.ref_counts == {}
+    held = [Sequence(seq_id=100 + i, prompt_token_ids=[1, 2, 3]) for i in range(pm.max_seqs)]
+    for s in held:
+        assert pm.allocate(s, 1)
+    with pytest.raises(RuntimeError, match="slots"):
+        pm.allocate(Sequence(seq_id=999, prompt_token_ids=[1]), 1)

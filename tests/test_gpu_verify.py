@@ -136,6 +136,28 @@ def test_sample_bonus_and_full_accept(cuda):
     assert np.all((gr == rec) | (gap < 1e-4))
 
 
+@pytest.mark.parametrize("alignment", ["reference", "standard"])
+def test_sample_k0_draws_the_bonus_token(cuda, alignment):
+    # verify.py:98-114 with k = 0: nothing to accept, the bonus token comes from softmax(lp[0] / Tp)
+    from ssd_b200.algorithm.verify import verify_sample
+
+    b, v = 5, 4099
+    rng = np.random.default_rng(21)
+    lp = (3.0 * rng.standard_normal((b, 1, v))).astype(np.float32)
+    lq = np.zeros((b, 0, v), np.float32)
+    spec = rng.integers(0, v, (b, 1)).astype(np.int32)
+    ua = np.zeros((b, 0), np.float32)
+    ug = np.clip(rng.random((b, v), dtype=np.float32), 1e-7, 1 - 1e-7).astype(np.float32)
+    res = verify_sample(lp, lq, spec, (ua, ug), temperature_p=0.8, alignment=alignment)
+    acc, rec, mask, (_, gap) = o_sample(lp, lq, spec, ua, ug, temperature_p=0.8, alignment=alignment,
+                                        return_margins=True)
+    assert (acc == 0).all() and (res.accept_until.cpu().numpy() == 0).all()
+    gr = res.recovery_tokens.cpu().numpy()
+    assert np.all((gr == rec) | (gap < 1e-4)), (gr, rec, gap)
+    assert ((gr == rec) & (gap >= 1e-4)).sum() >= b - 1
+    np.testing.assert_array_equal(res.accepted_mask.cpu().numpy(), mask)
+
+
 def test_sample_seeded_key_is_deterministic(cuda):
     from ssd_b200.algorithm.verify import uniforms_from_seed, verify_sample
 

@@ -38,8 +38,39 @@ def test_metrics_collector():
     m = MetricsCollector("sd")
     m.start()
     m.record_first_token()
-    m.record_step(StepMetrics(accepted_tokens=3, cache_hit=True))
+    m.record_step(StepMetrics(accepted_tokens=3, cache_hit=True, verify_device_ms=2.0))
     m.record_step(StepMetrics(accepted_tokens=1))
+    m.record_accepts([2, 0])
+    live = m.metrics
+    assert live.total_tokens == 4 and live.total_time_s >= 0.0
     r = m.finish()
     assert r.total_tokens == 4 and r.accepted_per_step == 2.0 and r.cache_hit_rate == 0.5
-    assert r.to_dict()["num_steps"] == 2
+    assert r.ttft_s <= r.total_time_s and r.verify_device_ms == 2.0
+    d = r.to_dict()
+    assert d["num_steps"] == 2 and d["accept_histogram"] == {0: 1, 2: 1}
+    # a batched step advances several sequences: accepted_per_step is per sequence-step
+    m2 = MetricsCollector("sd")
+    m2.start()
+    m2.record_step(StepMetrics(accepted_tokens=8, sequences=4))
+    assert m2.finish().accepted_per_step == 2.0
+
+
+def test_slot_scheduler_refills_freed_slots():
+    from ssd_b200.runtime.scheduler import Scheduler
+    from ssd_b200.runtime.sequence import SequenceStatus
+
+    s = Scheduler(num_slots=2)
+    seqs = [s.add_request([i, i + 1]) for i in range(5)]
+    assert [q.seq_id for q in seqs] == list(range(5)) and s.has_work()
+    placed = s.admit()
+    assert [(i, q.seq_id) for i, q in placed] == [(0, 0), (1, 1)] and s.admit() == []
+    assert all(q.status is SequenceStatus.RUNNING for _, q in placed)
+    assert s.retire(1).seq_id == 1 and seqs[1].status is SequenceStatus.FINISHED
+    assert [(i, q.seq_id) for i, q in s.admit()] == [(1, 2)]
+    s.retire(0)
+    s.retire(1)
+    assert [(i, q.seq_id) for i, q in s.admit()] == [(0, 3), (1, 4)]
+    s.retire(0)
+    assert s.slots() == [(1, seqs[4])] and s.free_slots() == [0] and s.has_work()
+    s.retire(1)
+    assert not s.has_work() and [q.seq_id for q in s.finished] == [1, 0, 2, 3, 4]

@@ -52,11 +52,16 @@ def test_worker_and_loader_defaults(monkeypatch):
     assert default_draft_path() == "toy-draft"
 
 
-def test_gemma_adapter_takes_the_reference_keywords():
+def test_gemma_adapter_takes_the_reference_arguments():
     import inspect
 
     from ssd_b200.models.gemma_adapter import GemmaAdapter
 
-    params = inspect.signature(GemmaAdapter.__init__).parameters
-    for name in ("model_path", "vocab_size", "share_key", "mesh", "devices", "role"):
-        assert name in params and params[name].kind is inspect.Parameter.KEYWORD_ONLY
+    params = list(inspect.signature(GemmaAdapter.__init__).parameters.values())[1:]
+    # the reference's positional order (gemma_adapter.py:28-36) ...
+    names = ["model_path", "vocab_size", "share_key", "mesh", "devices", "role"]
+    assert [q.name for q in params[:6]] == names
+    assert all(q.kind is inspect.Parameter.POSITIONAL_OR_KEYWORD for q in params[:6])
+    # ... and everything the adapter adds is keyword-only, so GemmaAdapter(path, 256000) cannot
+    # set a cache size by position
+    assert all(q.kind is inspect.Parameter.KEYWORD_ONLY for q in params[6:])

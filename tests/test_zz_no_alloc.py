@@ -5,8 +5,8 @@ handed only its operands and no allocator, and some embedders run under a
 fixed device-memory budget.  For them
 the library keeps the scratch of this one entry point in its own device data.
 This test calls it through the C ABI and checks that its outputs equal those
-of ssd_verify_greedy (which takes a caller workspace) on two calls in a row --
-the second call reuses the shared scratch the first one left behind.  The
+of ssd_verify_greedy (which takes a caller workspace) on three calls in a row --
+the later calls reuse the shared scratch the first one left behind.  The
 outputs are integers, so the comparison is exact.  The file is named so that
 pytest collects it last.
 """
@@ -37,7 +37,8 @@ def test_noalloc_greedy_equals_workspace_entry_point(cuda):
     from ssd_b200.algorithm.verify import verify_greedy
 
     so = _lib.lib()
-    for call, (b, k, v) in enumerate([(8, 4, 256000), (6, 6, 32000)]):
+    # the third call is the largest shape the fixed scratch takes: B * (K + 1) = 512 rows
+    for call, (b, k, v) in enumerate([(8, 4, 256000), (6, 6, 32000), (8, 63, 32000)]):
         lp, spec = _inputs(call, b, k, v)
         ref, ref_tt = verify_greedy(lp, spec, target_tokens=True)
         d_lp = torch.tensor(lp, device="cuda")

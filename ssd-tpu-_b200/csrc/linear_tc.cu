@@ -332,12 +332,28 @@ __device__ __forceinline__ void rope_qkv_store(const RopeArgs& r, int m, int n, 
   }
 }
 
-// every non-collective output store of the kernel
+// The residual rows m0 .. m0+15 of output column n (SSD_EPI_RESIDUAL; zeros otherwise), loaded
+// together before they are needed: a store loop that read each row's residual just before writing
+// it paid one L2 round trip per row (it cannot hoist a load above a store to the same array).
+__device__ __forceinline__ void load_residual16(const Params& p, int m0, int n, float* res) {
+  const bf16* y = reinterpret_cast<const bf16*>(p.y);
+  const bool on = p.epi == SSD_EPI_RESIDUAL && n < p.N;
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    res[j] = (on && m0 + j < p.M) ? __bfloat162float(__ldcg(y + (int64_t)(m0 + j) * p.N + n)) : 0.f;
+}
+
+// every non-collective output store of the kernel; `res` is the prefetched residual (RESIDUAL)
 template <bool ROPE>
-__device__ __forceinline__ void store_out(const Params& p, int m, int n, float acc, float pair, const int* rpc,
-                                          const long long* roff) {
-  if constexpr (ROPE) rope_qkv_store(p.rope, m, n, acc, pair, rpc[m], roff[m]);
-  else if (!(p.epi == SSD_EPI_GEGLU && (n & 1))) epilogue_store<bf16>(p.epi, p.y, p.N, m, n, acc, pair);
+__device__ __forceinline__ void store_out(const Params& p, int m, int n, float acc, float pair, float res,
+                                          const int* rpc, const long long* roff) {
+  if constexpr (ROPE) {
+    rope_qkv_store(p.rope, m, n, acc, pair, rpc[m], roff[m]);
+  } else if (p.epi == SSD_EPI_RESIDUAL) {
+    reinterpret_cast<bf16*>(p.y)[(int64_t)m * p.N + n] = from_f<bf16>(__fadd_rn(res, store_round<bf16>(acc)));
+  } else if (!(p.epi == SSD_EPI_GEGLU && (n & 1))) {
+    epilogue_store<bf16>(p.epi, p.y, p.N, m, n, acc, pair);
+  }
 }
 
 // COLL: instantiate the fused-collective epilogue (p.coll != COLL_NONE); the
@@ -528,8 +544,13 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           const uint64_t* slot = reinterpret_cast<const uint64_t*>(p.heaps[p.rank] + p.dst_off) +
                                  (((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world) * p.recv_rows * BM + row;
           bool ok = true;
+          const bf16* yres = reinterpret_cast<const bf16*>(p.y);
           for (int m0 = 0; m0 < p.M; m0 += 4) {
             uint64_t w[4][kMaxTP];
+            float res[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)  // in flight together with the first poll
+              res[i] = m0 + i < p.M ? __bfloat162float(__ldcg(yres + (int64_t)(m0 + i) * p.N + n)) : 0.f;
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -561,7 +582,8 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
               for (int r = 0; r < kMaxTP; ++r)
                 if (r < p.world) sum += __uint_as_float((uint32_t)w[i][r]);
-              epilogue_store<bf16>(SSD_EPI_RESIDUAL, p.y, p.N, m0 + i, n, sum, 0.f);
+              reinterpret_cast<bf16*>(p.y)[(int64_t)(m0 + i) * p.N + n] =
+                  from_f<bf16>(__fadd_rn(res[i], store_round<bf16>(sum)));
             }
             if (!ok) break;
           }
@@ -630,6 +652,10 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       const uint32_t crank = cluster_ctarank();
       const int tile = cta / p.G;
       const int n = tile * BM + row;
+      // the leader's tile count and residual rows, in flight while the MMAs finish
+      const uint32_t jt = (COLL && crank == 0) ? tile_count(tile) : 0u;
+      float res[16];
+      if (!COLL && crank == 0) load_residual16(p, 0, n, res);
       float v[16];
       if (wait_bounded(accf(0), 0u, abort_flag, p.err, 4)) {
         tc_fence_after();
@@ -675,7 +701,6 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
             for (int j = 0; j < 16; ++j) s[j] += r[cc][j];
         }
-        const uint32_t jt = COLL ? tile_count(tile) : 0u;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           if (p.rowscale && j < p.M) s[j] = __fmul_rn(s[j], inv_s[j]);
@@ -683,7 +708,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           if constexpr (COLL) {
             if (j < p.M && n < p.N) push(jt, tile, j, n, s[j]);
           } else if (j < p.M && n < p.N) {
-            store_out<ROPE>(p, j, n, s[j], up, rope_pc, rope_off);
+            store_out<ROPE>(p, j, n, s[j], up, res[j], rope_pc, rope_off);
           }
         }
         if constexpr (COLL) coll_finish(jt, tile);
@@ -701,12 +726,12 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       const int buf = seg & 1;
       const uint32_t use = (uint32_t)(seg >> 1);
       ++seg;
+      const bool whole = (kb_begin == 0 && kb_end == p.KB);
+      const uint32_t jt_whole = (COLL && whole) ? tile_count(tile) : 0u;
       if (!wait_bounded(accf(buf), use & 1u, abort_flag, p.err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * MP);
       const int n = tile * BM + row;
-      const bool whole = (kb_begin == 0 && kb_end == p.KB);
-      const uint32_t jt_whole = (COLL && whole) ? tile_count(tile) : 0u;
       float* mine = p.part + ((size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.M) * BM;
 #pragma unroll 1
       for (int c0 = 0; c0 < MP; c0 += 16) {
@@ -724,7 +749,12 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             if constexpr (COLL) {
               if (n < p.N) push(jt_whole, tile, m, n, v[j]);
             } else if (n < p.N) {
-              store_out<ROPE>(p, m, n, v[j], up, rope_pc, rope_off);
+              // whole tiles stream wide shapes (gate/up, LM head, QKV), whose epilogues read nothing;
+              // a residual is read here only if a row-parallel shape ever takes this path
+              const float res = p.epi == SSD_EPI_RESIDUAL
+                                    ? __bfloat162float(__ldcg(reinterpret_cast<const bf16*>(p.y) + (int64_t)m * p.N + n))
+                                    : 0.f;
+              store_out<ROPE>(p, m, n, v[j], up, res, rope_pc, rope_off);
             }
           } else {
             mine[(size_t)m * BM + row] = v[j];
@@ -761,7 +791,8 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       // per thread; the summation order per output stays c_first .. c_last.
       for (int m0 = 0; m0 < p.M; m0 += 16) {
         const int mn = min(16, p.M - m0);
-        float s[16];
+        float s[16], res[16];
+        if (!COLL) load_residual16(p, m0, n, res);
 #pragma unroll
         for (int i = 0; i < 16; ++i) s[i] = 0.f;
         for (int c = c_first; c <= c_last; c += 4) {
@@ -786,7 +817,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           if constexpr (COLL) {
             if (i < mn && n < p.N) push(jt, tile, m0 + i, n, s[i]);
           } else if (i < mn && n < p.N) {
-            store_out<ROPE>(p, m0 + i, n, s[i], up, rope_pc, rope_off);
+            store_out<ROPE>(p, m0 + i, n, s[i], up, res[i], rope_pc, rope_off);
           }
         }
       }

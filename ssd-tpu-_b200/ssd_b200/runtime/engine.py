@@ -160,6 +160,11 @@ class LLMEngine:
             if marks is not None:  # the decoders' symmetric buffers are free again
                 self._each(lambda r: torch.cuda.current_stream().synchronize())
                 self._each(lambda r: self.comms[r].release(marks[r]))
+        if self.comms:
+            # a collective whose peer never arrived ends with a timeout status instead of hanging
+            status = self._each(lambda r: self.comms[r].status())
+            if any(status):
+                raise RuntimeError(f"tensor-parallel collective timed out (rank statuses {status})")
         return [s.completion_token_ids for s in seqs], collector.finish()
 
     def generate_stream(self, prompt: list[int], sampling: SamplingParams,
@@ -179,6 +184,15 @@ class LLMEngine:
         if self.draft_worker:
             self.draft_worker.stop()
             self.draft_worker = None
+        if self.comms:
+            # the adapters' logits buffers are views of the heaps: drop them before the heaps go
+            self.targets = []
+            self.target = None
+            import gc
+
+            gc.collect()
+            self._each(lambda r: self.comms[r].close())
+            self.comms = None
         if self.group is not None:
             self.group.close()
             self.group = None

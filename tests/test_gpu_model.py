@@ -107,9 +107,10 @@ def test_gemma2b_mqa_layer_shapes_bf16(cuda):
 
 def _full_depth_verify_check(preset, seed, prompt_len, k):
     """One verify forward of the whole model (every layer, the full vocabulary) after a
-    ``prompt_len``-token prompt, against the bf16 oracle of the same weights.  The oracle
-    fetches one layer at a time from the device (``GemmaWeights.canonical_layer``), so host
-    memory holds the embedding plus one layer."""
+    ``prompt_len``-token prompt, and the oracle's forward of the same weights in bf16 (rounding
+    where the CUDA path stores bf16) and in fp32 (no intermediate rounding).  The oracle fetches
+    one layer at a time from the device (``GemmaWeights.canonical_layer``), so host memory holds
+    the embedding plus one layer."""
     import torch
 
     from ssd_b200.models.gemma import PRESETS, GemmaWeights
@@ -122,26 +123,41 @@ def _full_depth_verify_check(preset, seed, prompt_len, k):
     got = _run_forward(w, prompt, vt)
     full = w.to_canonical(layers=0)
     full["layers"] = w.canonical_layer
-    om = OracleGemma(_oshape(shape), full, "bf16", max_pos=1024)
-    n = len(prompt) + len(vt)
-    nb = (n + 15) // 16 + 1
-    pages = new_pages(om.s, nb, 16)
-    table = np.arange(nb, dtype=np.int32)[None]
-    om.forward(np.array([prompt]), pages, table, [0], with_head=False)
-    ref = om.forward(np.array([vt]), pages, table, [len(prompt)])[0]
-    return got, ref
+    refs = {}
+    for precision in ("bf16", "fp32"):
+        om = OracleGemma(_oshape(shape), full, precision, max_pos=1024)
+        n = len(prompt) + len(vt)
+        nb = (n + 15) // 16 + 1
+        pages = new_pages(om.s, nb, 16)
+        table = np.arange(nb, dtype=np.int32)[None]
+        om.forward(np.array([prompt]), pages, table, [0], with_head=False)
+        refs[precision] = om.forward(np.array([vt]), pages, table, [len(prompt)])[0]
+    return got, refs["bf16"], refs["fp32"]
 
 
 @pytest.mark.parametrize("preset,seed", [("gemma-7b", 1000), ("gemma-2b", 2000)])
-def test_full_depth_verify_logits_within_2e2(cuda, preset, seed):
+def test_full_depth_verify_logits(cuda, preset, seed):
     """The benchmarked models at full depth: Gemma-7B (28 layers) and Gemma-2B (18 layers), vocab
-    256000, verify over k+1 = 5 tokens after a 128-token prompt; |GPU - oracle| <= 2e-2 (bf16)."""
-    got, ref = _full_depth_verify_check(preset, seed, 128, 4)
-    err = np.abs(got - ref)
-    print(f"{preset}: max |dlogit| = {err.max():.3e}, mean = {err.mean():.3e}, "
-          f"logit std = {ref.std():.3e}, argmax agreement = {(got.argmax(-1) == ref.argmax(-1)).mean():.2f}")
-    assert err.max() <= 2e-2, err.max()
-    assert (got.argmax(-1) == ref.argmax(-1)).mean() >= 0.8
+    256000, verify over k+1 = 5 tokens after a 128-token prompt.
+
+    The per-op bf16 tolerance (2e-2, met by the 2-layer tests above) does not bound the maximum over
+    1.28 M logits after 28 layers: every bf16 rounding point of the forward can round an fp32 value
+    that the GPU and the oracle summed in different orders to neighbouring bf16 values, and these
+    one-ulp differences propagate through the residual stream.  So the full-depth criteria are
+    stated against the fp32 forward of the same weights: the GPU must be as close to it as the bf16
+    oracle is (within 1.5x, max and mean), the GPU-vs-bf16-oracle difference must stay small
+    (max <= 5e-2, mean <= 1e-2, for logits of standard deviation ~0.25), and the greedy choice must
+    agree on at least 4 of the 5 positions (a top-2 gap inside the rounding noise may flip one)."""
+    got, ref, ref32 = _full_depth_verify_check(preset, seed, 128, 4)
+    e16 = np.abs(got - ref)
+    g32 = np.abs(got - ref32)
+    o32 = np.abs(ref - ref32)
+    print(f"{preset}: |GPU - bf16 oracle| max {e16.max():.3e} mean {e16.mean():.3e}; "
+          f"|GPU - fp32| max {g32.max():.3e} mean {g32.mean():.3e}; "
+          f"|bf16 oracle - fp32| max {o32.max():.3e} mean {o32.mean():.3e}; logit std {ref32.std():.3e}")
+    assert g32.max() <= 1.5 * o32.max() and g32.mean() <= 1.5 * o32.mean()
+    assert e16.max() <= 5e-2 and e16.mean() <= 1e-2
+    assert (got.argmax(-1) == ref.argmax(-1)).mean() >= 0.8 and (got.argmax(-1) == ref32.argmax(-1)).mean() >= 0.8
 
 
 def test_toy_gpu_ar_stream_matches_oracle(cuda):

@@ -832,7 +832,10 @@ def run_ssd(args):
     clk = clocks.stop()
     llm.shutdown()
     n_tok = len(out[0])
-    st_ = eng.target_w[0].shape  # this rank's shard
+    from ssd_b200.models.gemma import PRESETS
+    from ssd_b200.runtime.tensor_parallel import shard_layout
+
+    st_, _ = shard_layout(PRESETS["gemma-7b"], 0, T)  # one rank's shard
     vocab = st_.vocab
     steps = m.steps
     verify_us = 1000.0 * statistics.mean(s.verify_device_ms for s in steps)

@@ -330,21 +330,6 @@ int ssd_ipc_import(const void* handle, size_t offset, void** ptr);
 /* Unmap a buffer mapped by ssd_ipc_import. */
 int ssd_ipc_close(void* ptr, size_t offset);
 
-/*
- * One process driving several GPUs (the engine's tensor-parallel group): a
- * symmetric heap allocated on `device` with the CUDA virtual-memory API and
- * mapped read/write for `device` and the n_access GPUs of `access`, so kernels
- * on those GPUs load and store it over NVLink.  Access is granted for this
- * allocation only (no context-wide peer access, which would map every later
- * allocation into every peer and make allocations on one GPU wait for work on
- * the others).  *mapped_bytes >= bytes (allocation granularity).  The memory is
- * not initialised.  SSD_ERR_UNSUPPORTED when a listed GPU has no peer path.
- * No reference counterpart (the reference places arrays with XLA meshes,
- * connect/mesh_allocator.py:64-117).
- */
-int ssd_heap_alloc(int device, size_t bytes, const int* access, int n_access, void** ptr, size_t* mapped_bytes);
-/* Unmap and release a heap of ssd_heap_alloc (no kernel may still use it). */
-int ssd_heap_free(void* ptr);
 
 /*
  * Row-parallel projection + all-reduce + residual (the O and down projections

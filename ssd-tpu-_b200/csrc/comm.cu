@@ -6,7 +6,6 @@
 
 #include <cstring>
 #include <mutex>
-#include <unordered_map>
 
 #include "linear.cuh"
 
@@ -131,155 +130,6 @@ extern "C" int ssd_ipc_close(void* ptr, size_t offset) {
     return SSD_ERR_LAUNCH;
   }
   return SSD_OK;
-}
-
-namespace {
-
-// CUDA virtual-memory entry points (driver API, resolved through the runtime).
-struct VmmApi {
-  CUresult (*create)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long);
-  CUresult (*release)(CUmemGenericAllocationHandle);
-  CUresult (*reserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
-  CUresult (*addr_free)(CUdeviceptr, size_t);
-  CUresult (*map)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
-  CUresult (*unmap)(CUdeviceptr, size_t);
-  CUresult (*set_access)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
-  CUresult (*granularity)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags);
-  bool ok;
-};
-
-template <typename F>
-void resolve(const char* name, F& fn, bool& ok) {
-  void* f = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
-    fn = reinterpret_cast<F>(f);
-  else
-    ok = false;
-}
-
-const VmmApi& vmm() {
-  static VmmApi a{};
-  static std::once_flag once;
-  std::call_once(once, [] {
-    a.ok = true;
-    resolve("cuMemCreate", a.create, a.ok);
-    resolve("cuMemRelease", a.release, a.ok);
-    resolve("cuMemAddressReserve", a.reserve, a.ok);
-    resolve("cuMemAddressFree", a.addr_free, a.ok);
-    resolve("cuMemMap", a.map, a.ok);
-    resolve("cuMemUnmap", a.unmap, a.ok);
-    resolve("cuMemSetAccess", a.set_access, a.ok);
-    resolve("cuMemGetAllocationGranularity", a.granularity, a.ok);
-    (void)cudaGetLastError();
-  });
-  return a;
-}
-
-struct HeapRec {
-  CUmemGenericAllocationHandle handle;
-  size_t size;
-};
-std::mutex g_heap_mu;
-std::unordered_map<uintptr_t, HeapRec> g_heaps;
-
-}  // namespace
-
-extern "C" int ssd_heap_alloc(int device, size_t bytes, const int* access, int n_access, void** ptr,
-                              size_t* mapped_bytes) {
-  if (!ptr || !mapped_bytes || bytes == 0 || n_access < 0 || n_access > 64 || (n_access > 0 && !access))
-    return SSD_ERR_INVALID;
-  int n = 0;
-  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
-    (void)cudaGetLastError();
-    return SSD_ERR_INVALID;
-  }
-  for (int i = 0; i < n_access; ++i) {
-    if (access[i] < 0 || access[i] >= n) return SSD_ERR_INVALID;
-    int can = 1;
-    if (access[i] != device && (cudaDeviceCanAccessPeer(&can, access[i], device) != cudaSuccess || !can)) {
-      (void)cudaGetLastError();
-      return SSD_ERR_UNSUPPORTED;
-    }
-  }
-  const VmmApi& api = vmm();
-  if (!api.ok) return SSD_ERR_UNSUPPORTED;
-  int cur = 0;
-  if (cudaGetDevice(&cur) != cudaSuccess || cudaSetDevice(device) != cudaSuccess) {  // context current
-    (void)cudaGetLastError();
-    return SSD_ERR_LAUNCH;
-  }
-  CUmemAllocationProp prop = {};
-  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
-  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-  prop.location.id = device;
-  size_t gran = 0;
-  int rc = SSD_OK;
-  CUmemGenericAllocationHandle h = 0;
-  CUdeviceptr va = 0;
-  size_t size = 0;
-  bool created = false, reserved = false, mapped = false;
-  if (api.granularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED) != CUDA_SUCCESS || gran == 0) rc = SSD_ERR_LAUNCH;
-  if (rc == SSD_OK) {
-    size = (bytes + gran - 1) / gran * gran;
-    created = api.create(&h, size, &prop, 0) == CUDA_SUCCESS;
-    if (!created) rc = SSD_ERR_LAUNCH;
-  }
-  if (rc == SSD_OK) {
-    reserved = api.reserve(&va, size, gran, 0, 0) == CUDA_SUCCESS;
-    if (!reserved) rc = SSD_ERR_LAUNCH;
-  }
-  if (rc == SSD_OK) {
-    mapped = api.map(va, size, 0, h, 0) == CUDA_SUCCESS;
-    if (!mapped) rc = SSD_ERR_LAUNCH;
-  }
-  if (rc == SSD_OK) {
-    // read/write for the owning GPU and every listed GPU -- this allocation only
-    CUmemAccessDesc desc[65];
-    int nd = 0;
-    auto add = [&](int d) {
-      for (int i = 0; i < nd; ++i)
-        if (desc[i].location.id == d) return;
-      desc[nd].location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-      desc[nd].location.id = d;
-      desc[nd].flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-      ++nd;
-    };
-    add(device);
-    for (int i = 0; i < n_access; ++i) add(access[i]);
-    if (api.set_access(va, size, desc, (size_t)nd) != CUDA_SUCCESS) rc = SSD_ERR_LAUNCH;
-  }
-  if (rc != SSD_OK) {
-    if (mapped) api.unmap(va, size);
-    if (reserved) api.addr_free(va, size);
-    if (created) api.release(h);
-  } else {
-    std::lock_guard<std::mutex> lock(g_heap_mu);
-    g_heaps[(uintptr_t)va] = HeapRec{h, size};
-    *ptr = reinterpret_cast<void*>(va);
-    *mapped_bytes = size;
-  }
-  cudaSetDevice(cur);
-  return rc;
-}
-
-extern "C" int ssd_heap_free(void* ptr) {
-  if (!ptr) return SSD_ERR_INVALID;
-  HeapRec rec;
-  {
-    std::lock_guard<std::mutex> lock(g_heap_mu);
-    auto it = g_heaps.find(reinterpret_cast<uintptr_t>(ptr));
-    if (it == g_heaps.end()) return SSD_ERR_INVALID;
-    rec = it->second;
-    g_heaps.erase(it);
-  }
-  const VmmApi& api = vmm();
-  const CUdeviceptr va = reinterpret_cast<CUdeviceptr>(ptr);
-  int rc = SSD_OK;
-  if (api.unmap(va, rec.size) != CUDA_SUCCESS) rc = SSD_ERR_LAUNCH;
-  if (api.addr_free(va, rec.size) != CUDA_SUCCESS) rc = SSD_ERR_LAUNCH;
-  if (api.release(rec.handle) != CUDA_SUCCESS) rc = SSD_ERR_LAUNCH;
-  return rc;
 }
 
 extern "C" int ssd_linear_allreduce(ssd_stream_t stream, const void* x, const void* w, void* y, int M, int N, int K,

@@ -66,8 +66,6 @@ SIGNATURES = {
     "ssd_ipc_export": (_i, [_p, _p, C.POINTER(_sz)]),
     "ssd_ipc_import": (_i, [_p, _sz, C.POINTER(_p)]),
     "ssd_ipc_close": (_i, [_p, _sz]),
-    "ssd_heap_alloc": (_i, [_i, _sz, _p, _i, C.POINTER(_p), C.POINTER(_sz)]),
-    "ssd_heap_free": (_i, [_p]),
     "ssd_linear_allreduce": (_i, [_p, _p, _p, _p, _i, _i, _i, _p, _sz, _p]),
     "ssd_linear_allgather": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
 }

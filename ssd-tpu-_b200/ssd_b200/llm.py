@@ -41,7 +41,7 @@ class LLM:
         return self._engine.generate_stream(prompt, sampling, on_token=on_token)
 
     def _tokenize(self, text: str) -> list[int]:
-        return self._engine.target.tokenize(text)
+        return self._engine.tokenize(text)
 
     def shutdown(self) -> None:
         self._engine.shutdown()

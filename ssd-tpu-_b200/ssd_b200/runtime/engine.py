@@ -6,21 +6,22 @@
   acceptance, page rollback, CUDA-graph replay -- the hot path this package
   rebuilds), or ``BatchedSpeculativeDecoder`` when several prompts are given or
   the sampling parameters ask for sampling: the prompts are seated in up to
-  ``max(config.batch_buckets)`` rows by the slot ``Scheduler``, a finished row
-  is refilled with the next waiting prompt while the others keep decoding
+  ``max(config.batch_buckets)`` rows by the slot ``Scheduler``, and a finished
+  row is refilled with the next waiting prompt while the others keep decoding
   (the reference decodes one prompt at a time, engine.py:110-125);
 * ``ssd`` -- the async protocol of the reference (``DraftWorker`` thread, host
   queues, ``SpecCache`` keyed by [seq_id, accepted, recovery]) with target
   verification through ``GemmaAdapter.verify`` + ``verify_greedy``; the draft
   and its worker run on their own GPU when there is one for them.
 
-Tensor parallelism (``config.tensor_parallel_size = T > 1``): the target is
-sharded over GPUs 0..T-1, each driven by its own thread of a ``DeviceGroup``
-(every rank issues the same launches; the O / down all-reduces and the LM-head
-all-gather are fused into the projection kernels over NVLink peer memory).  In
-``ar`` and ``sd`` modes the draft is sharded over the same GPUs; in ``ssd`` mode
-it runs unsharded on ``config.draft_device``, by default GPU T -- the
-reference's target/draft device split (connect/mesh_allocator.py:47-61).
+The target (and, in ``ar`` / ``sd`` modes, the draft) lives in a rank group
+(``runtime.rank_group``): on one GPU a ``RankState`` in this process; with
+``config.tensor_parallel_size = T > 1``, one worker process per GPU 0..T-1,
+each holding its weight shards and issuing the same launches (the O / down
+all-reduces and the LM-head all-gather are fused into the projection kernels
+over NVLink).  In ``ssd`` mode the draft runs unsharded in this process on
+``config.draft_device``, by default GPU T -- the reference's target/draft
+device split (connect/mesh_allocator.py:47-61).
 
 Greedy decoding is the default, as in the reference (whose sd/ssd paths never
 read ``SamplingParams.temperature``, engine.py:235,292); here a temperature > 0
@@ -38,19 +39,16 @@ import torch
 
 from .._lib import SSD_MAX_TP
 from ..algorithm.async_protocol import DraftCommand, DraftRequest
-from ..algorithm.verify import verify_greedy
 from ..config import DecodeMode, SSDConfig
 from ..kernels.ops import max_tokens_per_forward
 from ..models.gemma import PRESETS
 from ..models.gemma_adapter import GemmaAdapter
-from ..models.model_loader import default_preset, load_sharded_weights, load_weights
+from ..models.model_loader import default_preset, load_weights
 from ..sampling_params import SamplingParams
-from .batched import BatchedSpeculativeDecoder
-from .device_group import DeviceGroup
 from .metrics import MetricsCollector, RunMetrics, StepMetrics
+from .rank_group import LocalRank, RankGroup
 from .scheduler import Scheduler
 from .sequence import Sequence
-from .speculative import GreedyDecoder, SpeculativeDecoder
 from .workers import DraftWorker
 
 TokenCallback = Callable[[int, str], None]
@@ -66,7 +64,6 @@ class LLMEngine:
         if not 1 <= T <= min(ngpu, SSD_MAX_TP):
             raise ValueError(f"tensor_parallel_size {T} needs 1..{min(ngpu, SSD_MAX_TP)} GPUs (this host has {ngpu})")
         self.tp = T
-        self.target_devices = [torch.device("cuda", i) for i in range(T)]
         mode = config.mode
         self.async_draft = mode in (DecodeMode.SSD, DecodeMode.INSTANCE)
         if config.draft_device:
@@ -74,63 +71,34 @@ class LLMEngine:
         elif self.async_draft and T > 1 and ngpu > T:
             self.draft_device = torch.device("cuda", T)  # its own GPU, after the target group
         else:
-            self.draft_device = self.target_devices[0]
-        self.sharded_draft = T > 1 and not self.async_draft
-        self.group = DeviceGroup(self.target_devices) if T > 1 else None
-        self.comms = None
-        tpath = config.target_model_path
-        dpath = config.draft_model_path
+            self.draft_device = torch.device("cuda", 0)
+        tpath, dpath = config.target_model_path, config.draft_model_path
         same = dpath is not None and dpath == tpath
-        dseed = config.seed if same else config.seed + 1
-        if T == 1:
-            self.target_w = [load_weights(tpath, use_toy=config.use_toy_model, seed=config.seed, role="target",
-                                          device=self.target_devices[0])]
-        else:
-            from .tensor_parallel import TPComm
-
-            self.target_w = self._each(lambda r: load_sharded_weights(
-                tpath, r, T, use_toy=config.use_toy_model, seed=config.seed, role="target",
-                device=self.target_devices[r]))
-            d_model = max(PRESETS[self._preset(tpath, "target")].d_model,
-                          PRESETS[self._preset(dpath, "draft")].d_model)
-            self.comms = TPComm.local_group(self.target_devices, heap_bytes=512 << 20, max_m=256, max_n=d_model)
-        self.draft_w = None
-        if mode != DecodeMode.AR:
-            if self.sharded_draft:
-                self.draft_w = self._each(lambda r: load_sharded_weights(
-                    dpath, r, T, use_toy=config.use_toy_model, seed=dseed, role="draft",
-                    device=self.target_devices[r]))
-            else:
-                self.draft_w = [load_weights(dpath, use_toy=config.use_toy_model, seed=dseed, role="draft",
-                                             device=self.draft_device)]
-        # target adapters (prefill / verify / commit_tokens of the ssd loop), one per rank
-        self.targets = self._each(lambda r: GemmaAdapter(
-            self.target_w[r], max_model_len=config.max_model_len, name="target",
-            comm=self.comms[r] if self.comms else None))
-        self.target = self.targets[0]
+        self._draft_seed = config.seed if same else config.seed + 1
+        use_toy = config.use_toy_model
+        self.target_preset = tpath if tpath in PRESETS else default_preset("target", use_toy)
+        cfg = {"target_model_path": tpath, "draft_model_path": dpath, "use_toy_model": use_toy,
+               "seed": config.seed, "draft_seed": self._draft_seed, "max_model_len": config.max_model_len,
+               "local_draft": mode != DecodeMode.AR and not self.async_draft, "target_adapter": self.async_draft}
+        self.ranks = LocalRank(cfg, 0) if T == 1 else RankGroup(list(range(T)), cfg)
+        self.vocab_size = PRESETS[self.target_preset].vocab
         self.draft: GemmaAdapter | None = None
         self.draft_worker: DraftWorker | None = None
         if self.async_draft:
             # the draft adapter and its worker live on the draft's GPU; only token ids cross between GPUs
+            dw = load_weights(dpath, use_toy=use_toy, seed=self._draft_seed, role="draft", device=self.draft_device)
             with torch.cuda.device(self.draft_device):
-                self.draft = GemmaAdapter(self.draft_w[0], max_model_len=config.max_model_len, name="draft",
+                self.draft = GemmaAdapter(dw, max_model_len=config.max_model_len, name="draft",
                                           max_branches=max(1, config.mq_len))
                 self.draft_worker = DraftWorker(config, self.draft)
                 self.draft_worker.start()
 
-    # ------------------------------------------------------------ helpers
-    def _preset(self, path, role: str) -> str:
-        return path if path in PRESETS else default_preset(role, self.config.use_toy_model)
+    # ------------------------------------------------------------ text (byte-level stand-in tokenizer)
+    def tokenize(self, text: str) -> list[int]:
+        return [b % self.vocab_size for b in text.encode("utf-8")]
 
-    def _each(self, fn):
-        """fn(rank) on every rank of the target group (each on its GPU), results in rank order."""
-        if self.group is None:
-            with torch.cuda.device(self.target_devices[0]):
-                return [fn(0)]
-        return self.group.run(fn)
-
-    def _comm(self, r: int):
-        return self.comms[r] if self.comms else None
+    def decode_tokens_to_str(self, token_ids: list[int]) -> str:
+        return " ".join(f"t{int(t)}" for t in token_ids)
 
     # ------------------------------------------------------------ public
     def generate(self, prompts: list[list[int]], sampling: SamplingParams, *,
@@ -142,7 +110,7 @@ class LLMEngine:
         # the batched decoder's rows are the slots; the other paths take one prompt at a time
         sched = Scheduler(num_slots=self._num_slots(len(prompts)) if batched else 1)
         seqs = [sched.add_request(p) for p in prompts]
-        marks = self._each(lambda r: self.comms[r].mark()) if self.comms else None
+        self.ranks.call("begin")
         try:
             if batched:
                 self._run_batched(sched, sampling, on_token, collector)
@@ -157,14 +125,10 @@ class LLMEngine:
                         self._run_ar(seq, sampling, on_token, collector)
                     sched.retire(slot)
         finally:
-            if marks is not None:  # the decoders' symmetric buffers are free again
-                self._each(lambda r: torch.cuda.current_stream().synchronize())
-                self._each(lambda r: self.comms[r].release(marks[r]))
-        if self.comms:
+            status = self.ranks.call("end")
+        if any(status):
             # a collective whose peer never arrived ends with a timeout status instead of hanging
-            status = self._each(lambda r: self.comms[r].status())
-            if any(status):
-                raise RuntimeError(f"tensor-parallel collective timed out (rank statuses {status})")
+            raise RuntimeError(f"tensor-parallel collective timed out (rank statuses {status})")
         return [s.completion_token_ids for s in seqs], collector.finish()
 
     def generate_stream(self, prompt: list[int], sampling: SamplingParams,
@@ -178,30 +142,22 @@ class LLMEngine:
 
         self.generate([prompt], sampling, on_token=_cb)
         for tok in collected:
-            yield tok, self.target.decode_tokens_to_str([tok])
+            yield tok, self.decode_tokens_to_str([tok])
 
     def shutdown(self) -> None:
         if self.draft_worker:
             self.draft_worker.stop()
             self.draft_worker = None
-        if self.comms:
-            # the adapters' logits buffers are views of the heaps: drop them before the heaps go
-            self.targets = []
-            self.target = None
-            import gc
-
-            gc.collect()
-            self._each(lambda r: self.comms[r].close())
-            self.comms = None
-        if self.group is not None:
-            self.group.close()
-            self.group = None
+        if self.ranks is not None:
+            self.ranks.close()
+            self.ranks = None
 
     # ------------------------------------------------------------ modes
     def _num_slots(self, n: int) -> int:
         """Rows of the batched decoder: every prompt, at most max(batch_buckets), and B*(k+1)
         within one forward."""
-        cap = max_tokens_per_forward(self.target_w[0].dtype) // (self.config.speculate_k + 1)
+        dtype = torch.float32 if self.target_preset.startswith("toy") else torch.bfloat16
+        cap = max_tokens_per_forward(dtype) // (self.config.speculate_k + 1)
         return max(1, min(n, max(self.config.batch_buckets), cap))
 
     def _emit(self, seq: Sequence, toks: list[int], limit: int, on_token) -> int:
@@ -212,64 +168,52 @@ class LLMEngine:
             seq.append_token(t)
             n += 1
             if on_token:
-                on_token(t, self.target.decode_tokens_to_str([t]))
+                on_token(t, self.decode_tokens_to_str([t]))
         return n
 
-    def _max_len(self, seq: Sequence, sampling: SamplingParams) -> int:
+    def _max_len(self, longest_prompt: int, sampling: SamplingParams) -> int:
         k = self.config.speculate_k
-        n = len(seq.prompt_token_ids) + sampling.max_new_tokens + 2 * (k + 1) + 16
+        n = longest_prompt + sampling.max_new_tokens + 2 * (k + 1) + 16
         if n > self.config.max_model_len + 2 * (k + 1) + 16:
             raise ValueError("prompt + max_new_tokens exceeds max_model_len")
         return n
 
     def _run_ar(self, seq, sampling, on_token, collector) -> None:
         t0 = time.perf_counter()
-        max_len = self._max_len(seq, sampling)
-        bs = self.config.block_size
-        prompt = list(seq.prompt_token_ids)
-        outs = self._each(lambda r: GreedyDecoder(self.target_w[r], max_seq_len=max_len, block_size=bs,
-                                                  comm=self._comm(r)).generate(prompt, sampling.max_new_tokens))
+        max_len = self._max_len(len(seq.prompt_token_ids), sampling)
+        out = self.ranks.call("ar_generate", list(seq.prompt_token_ids), sampling.max_new_tokens, max_len,
+                              self.config.block_size)[0]
         collector.record_first_token()
-        n = self._emit(seq, outs[0], sampling.max_new_tokens, on_token)
+        n = self._emit(seq, out, sampling.max_new_tokens, on_token)
         collector.record_step(StepMetrics(target_verify_ms=(time.perf_counter() - t0) * 1000, accepted_tokens=n))
 
     def _run_sd(self, seq, sampling, on_token, collector) -> None:
         k = self.config.speculate_k
-        max_len = self._max_len(seq, sampling)
-        bs = self.config.block_size
-        decs = self._each(lambda r: SpeculativeDecoder(self.target_w[r], self.draft_w[r], k=k, max_seq_len=max_len,
-                                                       block_size=bs, comm=self._comm(r)))
-        prompt = list(seq.prompt_token_ids)
-        first = self._each(lambda r: decs[r].start(prompt))[0]
+        max_len = self._max_len(len(seq.prompt_token_ids), sampling)
+        first = self.ranks.call("sd_start", list(seq.prompt_token_ids), k, max_len, self.config.block_size)[0]
         self._emit(seq, [first], sampling.max_new_tokens, on_token)
         collector.record_first_token()
         while not seq.is_finished(None, sampling.max_new_tokens):
             t0 = time.perf_counter()
-            new = self._each(lambda r: decs[r].step())[0]
+            new, verify_ms, acc = self.ranks.call("sd_step")[0]
             n = self._emit(seq, new, sampling.max_new_tokens, on_token)
             collector.record_step(StepMetrics(target_verify_ms=(time.perf_counter() - t0) * 1000, accepted_tokens=n,
-                                              verify_device_ms=decs[0].last_verify_ms))
-            collector.record_accepts([decs[0].last_accept])
+                                              verify_device_ms=verify_ms))
+            collector.record_accepts([acc])
 
     def _run_batched(self, sched: Scheduler, sampling, on_token, collector) -> None:
         """Continuous batching over the scheduler's slots (see the module docstring)."""
         k = self.config.speculate_k
-        B = sched.num_slots
-        longest = max(len(s.prompt_token_ids) for s in sched.waiting)
-        max_len = longest + sampling.max_new_tokens + 2 * (k + 1) + 16
-        if max_len > self.config.max_model_len + 2 * (k + 1) + 16:
-            raise ValueError("prompt + max_new_tokens exceeds max_model_len")
+        max_len = self._max_len(max(len(s.prompt_token_ids) for s in sched.waiting), sampling)
         temp = float(sampling.temperature)
-        decs = self._each(lambda r: BatchedSpeculativeDecoder(
-            self.target_w[r], self.draft_w[r], batch=B, k=k, max_seq_len=max_len, block_size=self.config.block_size,
-            temperature=temp, top_p=float(sampling.top_p) if temp > 0 else 1.0, sampler_x=self.config.sampler_x,
-            seed=self.config.seed, comm=self._comm(r)))
+        self.ranks.call("batch_open", sched.num_slots, k, max_len, self.config.block_size, temp,
+                        float(sampling.top_p) if temp > 0 else 1.0, self.config.sampler_x, self.config.seed)
         limit = sampling.max_new_tokens
         first_done = False
         while sched.has_work():
             placed = sched.admit()
             if placed:
-                firsts = self._each(lambda r: [decs[r].admit(slot, seq.prompt_token_ids) for slot, seq in placed])[0]
+                firsts = self.ranks.call("batch_admit", [(slot, s.prompt_token_ids) for slot, s in placed])[0]
                 for (slot, seq), f in zip(placed, firsts):
                     self._emit(seq, [f], limit, on_token)
                 if not first_done:
@@ -279,30 +223,25 @@ class LLMEngine:
                 if seq.is_finished(None, limit):
                     sched.retire(slot)
                     if not sched.waiting:
-                        self._each(lambda r: decs[r].park(slot))
+                        self.ranks.call("batch_park", slot)
             if not sched.slots():
                 continue
             t0 = time.perf_counter()
-            new = self._each(lambda r: decs[r].step())[0]
-            emitted = 0
+            new, verify_ms, accepts = self.ranks.call("batch_step")[0]
             active = sched.slots()
-            for slot, seq in active:
-                emitted += self._emit(seq, new[slot], limit, on_token)
+            emitted = sum(self._emit(seq, new[slot], limit, on_token) for slot, seq in active)
             collector.record_step(StepMetrics(target_verify_ms=(time.perf_counter() - t0) * 1000,
-                                              accepted_tokens=emitted, verify_device_ms=decs[0].last_verify_ms,
+                                              accepted_tokens=emitted, verify_device_ms=verify_ms,
                                               sequences=len(active)))
-            collector.record_accepts(int(decs[0].last_accept[slot]) for slot, _ in active)
+            collector.record_accepts(accepts[slot] for slot, _ in active)
 
     def _run_ssd(self, seq, sampling, on_token, collector) -> None:
         assert self.draft_worker is not None
-        prompt = torch.tensor(seq.prompt_token_ids, dtype=torch.int32)
-        pre = self._each(lambda r: self.targets[r].prefill(prompt))[0]
-        recovery = int(pre.logits[0].argmax().item())
+        recovery = self.ranks.call("target_prefill", list(seq.prompt_token_ids))[0]
         seq.recovery_token = recovery
         self._emit(seq, [recovery], sampling.max_new_tokens, on_token)
         collector.record_first_token()
         acc = 0
-        ev = self._verify_events()
         while not seq.is_finished(None, sampling.max_new_tokens):
             t0 = time.perf_counter()
             key = torch.tensor([[seq.seq_id, acc, recovery]], dtype=torch.int32)
@@ -312,30 +251,14 @@ class LLMEngine:
             resp = self.draft_worker.get_response()
             t1 = time.perf_counter()
             spec = [int(t) for t in resp.spec_tokens[0].tolist()]
-            spec_kp1 = [recovery] + spec
-
-            def verify(r):
-                st = torch.cuda.current_stream()
-                if r == 0:
-                    ev[0].record(st)
-                vres = self.targets[r].verify(torch.tensor([spec_kp1], dtype=torch.int32))
-                vout = verify_greedy(vres.logits, torch.tensor([spec_kp1], dtype=torch.int32, device=vres.logits.device))
-                if r == 0:
-                    ev[1].record(st)
-                return int(vout.accept_until[0]), int(vout.recovery_tokens[0])
-
-            outcomes = self._each(verify)
-            if len(set(outcomes)) != 1:
+            outcomes = self.ranks.call("target_verify", [recovery] + spec)
+            if len({o[:2] for o in outcomes}) != 1:
                 raise RuntimeError(f"tensor-parallel ranks disagree on the verify outcome: {outcomes}")
-            acc, recovery = outcomes[0]
+            acc, recovery, verify_ms = outcomes[0]
             commit = spec[:acc] + [recovery]
-            self._each(lambda r: self.targets[r].commit_tokens(commit))
+            self.ranks.call("target_commit", commit)
             n = self._emit(seq, commit, sampling.max_new_tokens, on_token)
             collector.record_step(StepMetrics(target_verify_ms=(time.perf_counter() - t0) * 1000,
                                               draft_step_ms=(t1 - t0) * 1000, cache_hit=bool(resp.cache_hit[0]),
-                                              accepted_tokens=n, verify_device_ms=ev[0].elapsed_time(ev[1])))
+                                              accepted_tokens=n, verify_device_ms=verify_ms))
             collector.record_accepts([acc])
-
-    def _verify_events(self):
-        with torch.cuda.device(self.target_devices[0]):
-            return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

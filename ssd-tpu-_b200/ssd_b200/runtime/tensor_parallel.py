@@ -32,74 +32,21 @@ import torch
 from .._lib import SSD_MAX_TP, CommC, check, lib
 
 
-class _DLDevice(C.Structure):
-    _fields_ = [("device_type", C.c_int32), ("device_id", C.c_int32)]
-
-
-class _DLDataType(C.Structure):
-    _fields_ = [("code", C.c_uint8), ("bits", C.c_uint8), ("lanes", C.c_uint16)]
-
-
-class _DLTensor(C.Structure):
-    _fields_ = [("data", C.c_void_p), ("device", _DLDevice), ("ndim", C.c_int32), ("dtype", _DLDataType),
-                ("shape", C.POINTER(C.c_int64)), ("strides", C.POINTER(C.c_int64)), ("byte_offset", C.c_uint64)]
-
-
-class _DLManagedTensor(C.Structure):
-    pass
-
-
-_DLDeleter = C.CFUNCTYPE(None, C.POINTER(_DLManagedTensor))
-_DLManagedTensor._fields_ = [("dl_tensor", _DLTensor), ("manager_ctx", C.c_void_p), ("deleter", _DLDeleter)]
-_noop_deleter = _DLDeleter(lambda _m: None)  # the heap's owner releases the memory (TPComm.close)
-# DLPack descriptors stay alive for the process: a view of a heap may outlive its TPComm object, and
-# torch calls the descriptor's deleter when the last view dies (one small struct per heap)
-_DL_KEEP: list = []
-
-
-def _wrap_device_bytes(ptr: int, nbytes: int, device_index: int, keep: list = _DL_KEEP) -> torch.Tensor:
-    """A uint8 torch tensor over ``nbytes`` of device memory at ``ptr`` that torch does not own
-    (DLPack, no-op deleter; ``keep`` holds the descriptor objects)."""
-    shape = (C.c_int64 * 1)(nbytes)
-    m = _DLManagedTensor()
-    m.dl_tensor.data = ptr
-    m.dl_tensor.device = _DLDevice(2, device_index)  # kDLCUDA
-    m.dl_tensor.ndim = 1
-    m.dl_tensor.dtype = _DLDataType(1, 8, 1)  # kDLUInt, 8 bits
-    m.dl_tensor.shape = shape
-    m.dl_tensor.strides = None
-    m.dl_tensor.byte_offset = 0
-    m.manager_ctx = None
-    m.deleter = _noop_deleter
-    new_capsule = C.pythonapi.PyCapsule_New
-    new_capsule.restype = C.py_object
-    new_capsule.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p]
-    cap = new_capsule(C.addressof(m), b"dltensor", None)
-    keep.extend([shape, m])
-    from torch.utils.dlpack import from_dlpack
-
-    return from_dlpack(cap)
-
-
 class TPComm:
     """The ``ssd_comm`` handle of one rank plus a bump allocator over its heap.
 
     ``alloc`` must be called with the same sizes in the same order on every
     rank (buffers are symmetric by construction).  ``world == 1`` needs no
     process group: the collective kernels then run against the local heap only
-    (used to exercise the fused path on one GPU).  One process driving several
-    GPUs builds its group with ``TPComm.local_group`` instead (NVLink peer
-    access, no IPC).
+    (used to exercise the fused path on one GPU).
     """
 
     def __init__(self, heap_bytes: int = 256 << 20, max_m: int = 256, max_n: int = 8192, group=None,
-                 device=None, *, _local: tuple | None = None):
+                 device=None):
         import torch.distributed as dist
 
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        if _local is not None:
-            self.rank, self.world = _local[0], _local[1]
-        elif dist.is_available() and dist.is_initialized():
+        if dist.is_available() and dist.is_initialized():
             self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         else:
             self.rank, self.world = 0, 1
@@ -110,24 +57,11 @@ class TPComm:
         self.recv_bytes = int(L.ssd_comm_recv_bytes(self.world, max_m, max_n))
         fixed = self.ctrl_bytes + self.recv_bytes
         heap_bytes = max(heap_bytes, fixed + (1 << 20))
-        self._vmm = None
-        if _local is not None:
-            # one process, several GPUs: a virtual-memory heap that the group's GPUs may access
-            devs = (C.c_int * len(_local[2]))(*_local[2])
-            p, n = C.c_void_p(), C.c_size_t(0)
-            check(L.ssd_heap_alloc(self.device.index, heap_bytes, devs, len(_local[2]), C.byref(p), C.byref(n)),
-                  "ssd_heap_alloc")
-            self._vmm = int(p.value)
-            self.heap = _wrap_device_bytes(self._vmm, heap_bytes, self.device.index)
-            self.heap.zero_()
-        else:
-            self.heap = torch.zeros(heap_bytes, dtype=torch.uint8, device=self.device)
+        self.heap = torch.zeros(heap_bytes, dtype=torch.uint8, device=self.device)
         torch.cuda.synchronize(self.device)
         self._top = fixed
         self._imported: list[tuple[int, int]] = []
         self.heap_bytes, self.max_m, self.max_n = heap_bytes, max_m, max_n
-        if _local is not None:
-            return  # local_group fills in the peers
         peers: list[int] = []
         if self.world > 1:
             handle = (C.c_char * 64)()
@@ -164,27 +98,6 @@ class TPComm:
         c.recv_rows, c.recv_tiles = self.max_m, (self.max_n + 127) // 128
         self.cstruct = c
 
-    @classmethod
-    def local_group(cls, devices, heap_bytes: int = 256 << 20, max_m: int = 256,
-                    max_n: int = 8192) -> list["TPComm"]:
-        """One rank per GPU of ``devices``, all driven by this process: each heap is a
-        virtual-memory allocation mapped for every GPU of the group (``ssd_heap_alloc``;
-        peer access for these heaps only), so each rank's handle lists the others' heaps
-        directly.  Returns the ranks in order."""
-        devs = [torch.device(d) if not isinstance(d, int) else torch.device("cuda", d) for d in devices]
-        idx = [d.index for d in devs]
-        if len(set(idx)) != len(idx):
-            raise ValueError("tensor-parallel ranks must sit on distinct GPUs")
-        world = len(devs)
-        ranks = []
-        for r, d in enumerate(devs):
-            with torch.cuda.device(d):
-                ranks.append(cls(heap_bytes, max_m, max_n, device=d, _local=(r, world, idx)))
-        peers = [c.heap.data_ptr() for c in ranks]
-        for c in ranks:
-            c._bind(peers)
-        return ranks
-
     def alloc(self, shape, dtype=torch.float32) -> torch.Tensor:
         """A symmetric buffer (same heap offset on every rank), 256-byte aligned, zero-filled."""
         n = 1
@@ -218,17 +131,10 @@ class TPComm:
         return [int(v) & 0xFFFFFFFF for v in self.heap[off:off + 4 * n].view(torch.int32).tolist()]
 
     def close(self) -> None:
-        """Unmap the peers' heaps (and release this rank's heap when it is a virtual-memory one);
-        no buffer of the heap may be used afterwards."""
         L = lib()
         for p, o in self._imported:
             L.ssd_ipc_close(p, o)
         self._imported = []
-        if self._vmm is not None:
-            torch.cuda.synchronize(self.device)
-            self.heap = None
-            check(L.ssd_heap_free(self._vmm), "ssd_heap_free")
-            self._vmm = None
 
 
 def shard_layout(shape, rank: int, world: int):

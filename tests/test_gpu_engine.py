@@ -155,7 +155,7 @@ def test_ssd_draft_on_its_own_gpu(cuda):
     ref, _ = ar.generate([prompt], sampling)
     ar.shutdown()
     llm = LLM(SSDConfig(mode=DecodeMode.SSD, use_toy_model=True, draft_device="cuda:1"))
-    assert llm._engine.draft_w[0].device == torch.device("cuda", 1)
+    assert llm._engine.draft_device == torch.device("cuda", 1) and llm._engine.draft.dev == torch.device("cuda", 1)
     out, m = llm.generate([prompt], sampling)
     llm.shutdown()
     assert out[0] == ref[0] and m.total_tokens > 0

@@ -958,9 +958,16 @@ bool clusters_fit(int G, int tiles) {
 // on M, so every M sums the same partials in the same order.
 int split_parts(int tiles, int KB, int sms) {
   if (tiles > sms || KB < 2) return 0;
+  // Few k-blocks per tile: the fold costs more than the parallelism buys.  Measured on B200 in
+  // chains of launches at M = 5: a part's partial reaches the folding CTA in about one shared-memory
+  // round trip per four parts (~1.3 us each), while a CTA streams a 16 KB k-block in well under
+  // that.  So a tile of at most 8 k-blocks is one CTA (no fold: O at TP8 6.2 vs 6.6 us), and a
+  // tile of at most 32 k-blocks takes at most four parts (2B O 7.7 vs 9.1 us, 2B QKV 7.9 vs 9.2).
+  if (KB <= 8) return 1;
   int G = (2 * sms) / tiles;
   if (G > KB) G = KB;
   if (G > kMaxParts) G = kMaxParts;
+  if (KB <= 32 && G > 4) G = 4;
   for (int g = G; g >= 2; --g)
     if (clusters_fit(g, tiles)) return g;
   return G;

@@ -817,7 +817,8 @@ def run_ssd(args):
         return
     cfg = SSDConfig(mode=DecodeMode.SSD, speculate_k=k, fan_out_list=(args.fanout,) * (k + 1),
                     target_model_path="gemma-7b", draft_model_path="gemma-2b", use_toy_model=False,
-                    tensor_parallel_size=T, max_model_len=args.prompt_len + args.new_tokens + 64, seed=1000)
+                    tensor_parallel_size=T, max_model_len=args.prompt_len + args.new_tokens + 64, seed=1000,
+                    draft_device=f"cuda:{T}" if ngpu > T else "cuda:0")
     llm = LLM(cfg)
     eng = llm._engine
     rng = np.random.default_rng(0)

@@ -83,13 +83,14 @@ def test_ragged_q_lens_and_padding_rows(cuda):
     assert (out[2] == 0).all() and (out[1, 2:] == 0).all()
 
 
-def test_attention_is_batch_invariant(cuda):
+@pytest.mark.parametrize("hq,hkv", [(16, 16), (8, 1), (8, 2)])  # 256- and 64-position splits
+def test_attention_is_batch_invariant(cuda, hq, hkv):
     """A query's output is bit-identical whether it is verified with k others or decoded alone."""
     import torch
 
     from ssd_b200.kernels.kv_cache import paged_verify_attention
 
-    b, t, hq, hkv, d, bs = 1, 5, 16, 16, 256, 16
+    b, t, d, bs = 1, 5, 256, 16
     ctx = [777]
     cache, pages_np, tables, q, tdt = _setup(b, t, hq, hkv, d, bs, ctx, "bf16", seed=9, table_cols=128)
     tb = torch.tensor(tables, device="cuda")

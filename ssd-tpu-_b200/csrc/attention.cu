@@ -85,7 +85,7 @@ struct RowInfo {
 // w_s = exp(m_s - M) and the normaliser L are computed once per row by one warp
 // (lane-strided over splits, xor-tree sums: an empty split's exact zeros leave
 // them unchanged), then every output element sums w_s * o_s in split order.
-template <typename KV, int D, int CHUNK = kChunk, int NTHREADS = kAttnThreads, int WSTRIDE = 256>
+template <typename KV, int D, int CHUNK = kChunk, int NTHREADS = kAttnThreads>
 __device__ __forceinline__ void attention_fold(const float* ws_o, const float2* ws_ml,
                                                KV* out, int64_t grp_id, int nsplit, int seq_len,
                                                int nrows, int row0, int G, int T, int hq, int kvh, int b,
@@ -102,7 +102,7 @@ __device__ __forceinline__ void attention_fold(const float* ws_o, const float2* 
     for (int s = lane; s < ns; s += 32) {
       const float2 ml = __ldcg(&ws_ml[rb + (int64_t)s * kRows]);
       const float w = (ml.x == -INFINITY || M == -INFINITY) ? 0.f : expf(ml.x - M);
-      wsm[r * WSTRIDE + s] = w;
+      wsm[r * 256 + s] = w;
       lsum += ml.y * w;
     }
     const float L = warp_sum(lsum);
@@ -112,7 +112,7 @@ __device__ __forceinline__ void attention_fold(const float* ws_o, const float2* 
   for (int i = tid; i < nrows * D; i += NTHREADS) {
     const int r = i / D, d = i % D;
     const int64_t rb = grp_id * nsplit * kRows + r;
-    const float* wr = wsm + r * WSTRIDE;
+    const float* wr = wsm + r * 256;
     float O = 0.f;
     int s = 0;
     for (; s + 4 <= ns; s += 4) {
@@ -610,17 +610,8 @@ paged_attention_tc_kernel(const bf16* q, const bf16* pages, int num_layers,
 // At D = 256: 128 threads and ~106 KB of shared memory, two CTAs per SM, up
 // to 12 pages (192 KB) of K/V in flight per SM.  Batch invariance as for the other
 // kernels: splits, page ownership and every reduction order are fixed.
+constexpr int kTmaChunk = 256;                  // positions per split
 constexpr int kTmaPage = 16;                    // rows per page (TMA box height)
-// Positions per split.  256 (16 pages) when the model has several KV heads, so a step's
-// (sequence, KV head) groups already spread over many CTAs; 64 (4 pages) for one or two KV heads
-// (multi-query attention, or a tensor-parallel shard holding two heads), whose decode step would
-// otherwise run on one or two CTAs per sequence, each streaming its pages one after another.  The
-// choice depends on the model's KV heads only -- never on the batch, the query count or the context
-// -- so a position's attention is summed in the same order in every call (batch invariance).
-constexpr int kTmaChunkWide = 256;
-constexpr int kTmaChunkNarrow = 64;
-constexpr int kTmaFoldStride = 512;             // splits one fold can weigh: 32768 positions at 64 each
-inline int tma_chunk(int hkv) { return hkv <= 2 ? kTmaChunkNarrow : kTmaChunkWide; }
 // consumer warps per CTA for head size D; the stage count is a multiple of it
 template <int D>
 constexpr int tma_consumers() {
@@ -692,7 +683,7 @@ __device__ __forceinline__ uint32_t sw_off(int row, int dim) {
   return (uint32_t)(c * (kTmaPage * 128) + row * 128 + ((u ^ (row & 7)) << 4));
 }
 
-template <int D, int CHUNK>
+template <int D>
 __global__ void __launch_bounds__(tma_threads<D>(), 2)
 paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16* q, int num_layers, int num_blocks,
                            int hkv, int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
@@ -752,10 +743,10 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   const int nrows = ri.nrows;
   int kmax = 0;
   for (int r = 0; r < nrows; ++r) kmax = max(kmax, ri.pos[r] + 1);
-  const int k_begin = split * CHUNK;
-  const int k_end = min(min(min(k_begin + CHUNK, kmax), seq_len), max_blocks * kTmaPage);
+  const int k_begin = split * kTmaChunk;
+  const int k_end = min(min(min(k_begin + kTmaChunk, kmax), seq_len), max_blocks * kTmaPage);
   const int64_t grp_id = ((int64_t)b * hkv + kvh) * row_groups + rg;
-  const int ns = max(1, min(nsplit, (seq_len + CHUNK - 1) / CHUNK));
+  const int ns = max(1, min(nsplit, (seq_len + kTmaChunk - 1) / kTmaChunk));
   if (split >= ns) {  // past this sequence's context: the fold neither waits for nor reads this split
     pdl_trigger();
     return;
@@ -763,7 +754,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   const int npages = k_end > k_begin ? (k_end - k_begin + kTmaPage - 1) / kTmaPage : 0;
 
   int issued = 0;  // pages the producer lane has put in flight
-  __shared__ int s_blk[CHUNK / kTmaPage];
+  __shared__ int s_blk[kTmaChunk / kTmaPage];
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // the split's page-table entries in one parallel load (not one L2 round trip per page)
@@ -956,7 +947,7 @@ paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16
   if (direct) return;
   // the ns splits that hold context take a ticket; the last one folds them in split order
   if (!last_block_of(&counters[grp_id], (unsigned)ns, &is_last)) return;
-  attention_fold<bf16, D, CHUNK, NTHREADS, kTmaFoldStride>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq,
+  attention_fold<bf16, D, kTmaChunk, NTHREADS>(ws_o, ws_ml, out, grp_id, nsplit, seq_len, nrows, row0, G, T, hq,
                                                kvh, b, os);
 }
 
@@ -1041,18 +1032,16 @@ struct AttnLayout {
 };
 
 // Workspace: ticket counters, an error word, split partials.  Sized for the
-// smaller of the 128-position splits of the CUDA-core / mma kernels and the TMA
-// kernel's splits for this KV-head count (see tma_chunk).
+// 128-position splits of the CUDA-core / mma kernels, which covers the TMA
+// kernel's 256-position splits too.
 inline AttnLayout attn_layout(int B, int T, int hq, int hkv, int D, int max_seq_len) {
   AttnLayout L;
   const int G = hq / hkv;
   L.row_groups = (G * T + kRows - 1) / kRows;
   L.nsplit = (max_seq_len + kChunk - 1) / kChunk;
   if (L.nsplit < 1) L.nsplit = 1;  // <= 256 (checked by the caller): the fold keeps one weight per split
-  const int chunk = tma_chunk(hkv) < kChunk ? tma_chunk(hkv) : kChunk;
-  const int nslots = (max_seq_len + chunk - 1) / chunk > L.nsplit ? (max_seq_len + chunk - 1) / chunk : L.nsplit;
   const size_t groups = (size_t)B * hkv * L.row_groups;
-  const size_t rows = groups * nslots * kRows;
+  const size_t rows = groups * L.nsplit * kRows;
   L.groups = groups;
   L.off_cnt = 0;
   L.off_o = kCounterBytes + 256;  // error word at kCounterBytes
@@ -1106,7 +1095,7 @@ bool kv_map_cached(CUtensorMap* out, const void* pages, int plane_pages, int hkv
   return true;
 }
 
-template <int D, int CHUNK>
+template <int D>
 int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks, int hkv,
                          int layer, const int32_t* tables, int max_blocks, const int32_t* seq_lens,
                          const int32_t* q_lens, void* out, float scale, int B, int T, int hq, int max_seq_len,
@@ -1114,7 +1103,7 @@ int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int 
   using S = TmaSmem<D>;
   CUtensorMap map;
   if (!kv_map_cached(&map, pages, 2 * num_layers * num_blocks, hkv, D)) return SSD_ERR_LAUNCH;
-  auto kern = paged_attention_tma_kernel<D, CHUNK>;
+  auto kern = paged_attention_tma_kernel<D>;
   {
     // the shared-memory attribute belongs to each device's context: set it once per device
     static std::mutex mu;
@@ -1131,8 +1120,7 @@ int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int 
     }
   }
   char* w = reinterpret_cast<char*>(ws);
-  const int nsplit = (max_seq_len + CHUNK - 1) / CHUNK;  // fits the workspace (attn_layout)
-  if (nsplit > kTmaFoldStride) return SSD_ERR_UNSUPPORTED;
+  const int nsplit = (max_seq_len + kTmaChunk - 1) / kTmaChunk;  // <= L.nsplit: fits the workspace
   dim3 grid(nsplit, hkv * L.row_groups, B);
   SSD_PDL(kern, grid, tma_threads<D>(), S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
           layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups,
@@ -1212,13 +1200,9 @@ int ssd::paged_verify_attention_impl(ssd_stream_t stream, const void* q, const v
                                  workspace)
   const bool aligned16 = !(reinterpret_cast<uintptr_t>(q) & 15) && !(reinterpret_cast<uintptr_t>(pages) & 15);
 #define SSD_ATTN_TMA(DD)                                                                                        \
-  return tma_chunk(num_kv_heads) == kTmaChunkNarrow                                                           \
-             ? launch_attention_tma<DD, kTmaChunkNarrow>(st, q, pages, num_layers, num_blocks, num_kv_heads,    \
-                                                         layer, block_tables, max_blocks, seq_lens, q_lens, out, \
-                                                         scale, B, T, num_heads, max_seq_len, L, workspace, early) \
-             : launch_attention_tma<DD, kTmaChunkWide>(st, q, pages, num_layers, num_blocks, num_kv_heads,      \
-                                                       layer, block_tables, max_blocks, seq_lens, q_lens, out,   \
-                                                       scale, B, T, num_heads, max_seq_len, L, workspace, early)
+  return launch_attention_tma<DD>(st, q, pages, num_layers, num_blocks, num_kv_heads, layer, block_tables,      \
+                                  max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, max_seq_len, L,    \
+                                  workspace, early)
   if (dtype == SSD_DTYPE_BF16 && aligned16 && block_size == kTmaPage && (int64_t)2 * num_layers * num_blocks < (1ll << 31)) {
     if (head_dim == 256) SSD_ATTN_TMA(256);
     if (head_dim == 128) SSD_ATTN_TMA(128);

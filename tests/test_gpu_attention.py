@@ -83,7 +83,7 @@ def test_ragged_q_lens_and_padding_rows(cuda):
     assert (out[2] == 0).all() and (out[1, 2:] == 0).all()
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 16), (8, 1), (8, 2)])  # 256- and 64-position splits
+@pytest.mark.parametrize("hq,hkv", [(16, 16), (8, 1), (8, 2)])
 def test_attention_is_batch_invariant(cuda, hq, hkv):
     """A query's output is bit-identical whether it is verified with k others or decoded alone."""
     import torch

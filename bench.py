@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--e2e-new-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--qk-pairs", action="store_true",
+                    help="weights with rotation-paired q/k rows: RoPE + K/V write fused into the QKV projection")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
                     help="N > 1: tensor-parallel pair (one sequence) or independent replicas")
     ap.add_argument("--op", choices=["linear", "attention", "verify", "sample", "topp", "allreduce", "allgather"],
@@ -272,6 +274,11 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- GPU leg
+def _paired(w, args):
+    """--qk-pairs: store q/k rows as rotation pairs, so RoPE and the K/V write run in the QKV epilogue."""
+    return w.pair_qk_rows() if args.qk_pairs else w
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -312,14 +319,14 @@ def run_ours(args):
         tp_parity["ok_all_ranks"] = bool(flag.item())
 
         # every rank draws the same full weights from the seed and keeps its shard
-        target = shard_weights(GemmaWeights.random(st_, seed=1000), rank, world)
-        draft = shard_weights(GemmaWeights.random(sd_, seed=2000), rank, world)
+        target = shard_weights(_paired(GemmaWeights.random(st_, seed=1000), args), rank, world)
+        draft = shard_weights(_paired(GemmaWeights.random(sd_, seed=2000), args), rank, world)
         torch.cuda.empty_cache()
         comm = TPComm(heap_bytes=192 << 20, max_m=64, max_n=max(st_.d_model, sd_.d_model))
         rng = np.random.default_rng(0)
     else:
-        target = GemmaWeights.random(st_, seed=1000 + rank)
-        draft = GemmaWeights.random(sd_, seed=2000 + rank)
+        target = _paired(GemmaWeights.random(st_, seed=1000 + rank), args)
+        draft = _paired(GemmaWeights.random(sd_, seed=2000 + rank), args)
         rng = np.random.default_rng(rank)
     lt, ld = target.shape, draft.shape  # this rank's (sharded) shapes
     prompt = [int(x) for x in rng.integers(0, st_.vocab, args.prompt_len)]

@@ -23,7 +23,6 @@ from __future__ import annotations
 
 import datetime
 import multiprocessing as mp
-import os
 import socket
 import traceback
 
@@ -190,14 +189,20 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, device_index: int, port: int, cfg: dict, conn) -> None:
+def _resolve(path: str):
+    import importlib
+
+    mod, _, name = path.partition(":")
+    return getattr(importlib.import_module(mod), name)
+
+
+def _worker(rank: int, world: int, device_index: int, port: int, cfg: dict, conn, state_cls: str) -> None:
     try:
         import torch.distributed as dist
 
-        torch.cuda.set_device(device_index)
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=120))
-        state = RankState(cfg, rank, world, device_index)
+        state = _resolve(state_cls)(cfg, rank, world, device_index)
         conn.send(("ok", None))
     except BaseException:
         conn.send(("err", traceback.format_exc()))
@@ -222,32 +227,46 @@ def _worker(rank: int, world: int, device_index: int, port: int, cfg: dict, conn
 
 
 class RankGroup:
-    """One spawned worker process per GPU of ``devices``, rank r on ``devices[r]``."""
+    """One spawned worker process per GPU of ``devices``, rank r on ``devices[r]``.
 
-    def __init__(self, devices: list[int], cfg: dict) -> None:
+    ``state_cls`` ("module:Class") is what each worker builds as ``Class(cfg, rank, world, device)``;
+    the engine uses ``RankState``.
+    """
+
+    def __init__(self, devices: list[int], cfg: dict,
+                 state_cls: str = "ssd_b200.runtime.rank_group:RankState") -> None:
         ctx = mp.get_context("spawn")
         port = _free_port()
         self.world = len(devices)
         self._conns, self._procs = [], []
-        env_keep = os.environ.get("OMP_NUM_THREADS")
         for r, d in enumerate(devices):
             parent, child = ctx.Pipe()
-            p = ctx.Process(target=_worker, args=(r, self.world, d, port, cfg, child), daemon=True)
+            p = ctx.Process(target=_worker, args=(r, self.world, d, port, cfg, child, state_cls), daemon=True)
             p.start()
             self._conns.append(parent)
             self._procs.append(p)
-        if env_keep is not None:
-            os.environ["OMP_NUM_THREADS"] = env_keep
-        errors = [m for m in (c.recv() for c in self._conns) if m[0] != "ok"]
+        try:
+            errors = [m for m in (self._recv(c) for c in self._conns) if m[0] != "ok"]
+        except RuntimeError:
+            self.close()
+            raise
         if errors:
             self.close()
             raise RuntimeError("tensor-parallel rank failed to start:\n" + errors[0][1])
 
+    @staticmethod
+    def _recv(conn):
+        try:
+            return conn.recv()
+        except EOFError:
+            raise RuntimeError("a tensor-parallel rank process exited") from None
+
     def call(self, name: str, *args):
-        """Run ``RankState.<name>(*args)`` on every rank; the results in rank order."""
+        """Run ``<state>.<name>(*args)`` on every rank; the results in rank order.  A rank that raises
+        makes the call raise (with that rank's traceback) after every rank has answered."""
         for c in self._conns:
             c.send((name, args))
-        out = [c.recv() for c in self._conns]
+        out = [self._recv(c) for c in self._conns]
         bad = [m for m in out if m[0] != "ok"]
         if bad:
             raise RuntimeError(f"tensor-parallel rank failed in {name}:\n" + bad[0][1])

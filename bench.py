@@ -18,7 +18,7 @@ kernels over NVLink; one sequence, strong scaling), or each rank decodes its own
 sequence (``--parallel replicas``; no data-path collective, weak scaling).
 
 ``--impl reference`` times the CPU restatement of the same path (numpy oracle:
-the reference's own JAX code cannot run here) on a bounded layer sample.
+the reference's own JAX code cannot run here), one full-depth step per step.
 """
 
 from __future__ import annotations
@@ -91,14 +91,17 @@ def peaks():
 
 
 class ClockSampler:
-    """SM clock, power and clock-event reasons of one GPU, polled through NVML every 10 ms by a
+    """SM clock, power and clock-event reasons of one GPU, polled through NVML every 25 ms by a
     background thread from ``start`` to ``stop`` (the timed region).  Reading them changes no
-    setting.  Falls back to ``nvidia-smi -lms 200`` when the NVML binding is missing."""
+    setting.  Reports "NVML unavailable" when the binding is missing."""
 
     REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
                ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, cuda_index: int, period_s: float = 0.01):
+    def __init__(self, cuda_index: int, period_s: float = 0.025, enabled: bool = True):
+        # one sampler per node (rank 0): eight ranks each polling NVML every 10 ms slowed the
+        # tensor-parallel step measurably (the run's end-to-end rate exceeded its timed rate)
+        self.enabled = enabled
         self.cuda_index = cuda_index
         self.period = period_s
         self.samples: list[tuple[float, float, int]] = []
@@ -127,6 +130,8 @@ class ClockSampler:
     def start(self):
         import threading
 
+        if not self.enabled:
+            return
         try:
             import pynvml
 
@@ -155,6 +160,8 @@ class ClockSampler:
         self._thread.start()
 
     def stop(self) -> dict:
+        if not self.enabled:
+            return {"sampled_by": "rank 0"}
         if self._handle is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML unavailable"], "samples": 0}
         self._stop.set()
@@ -163,7 +170,7 @@ class ClockSampler:
         reasons = sorted({name for _, _, r in self.samples for name, bit in self.REASONS if r & bit})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.sm_max,
                 "power_w_max": max((x[1] for x in self.samples), default=None), "reasons": reasons,
-                "samples": len(sm), "source": "NVML, 10 ms period, timed region only"}
+                "samples": len(sm), "source": "NVML, 25 ms period, timed region only, rank 0's GPU"}
 
 
 # ----------------------------------------------------------------- CPU leg
@@ -339,7 +346,7 @@ def run_ours(args):
         dec.step()
     stream = torch.cuda.current_stream()
     verify_ms = []
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, enabled=(rank == 0))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -738,7 +745,7 @@ def run_batched(args):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, enabled=(rank == 0))
     clocks.start()
     e0.record(stream)
     tokens = 0

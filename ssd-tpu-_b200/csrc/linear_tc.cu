@@ -71,12 +71,15 @@ struct Params {
   const bf16* x;  // token rows (read directly only for the row norms)
   int rowscale;   // 1: scale row m of the result by rsqrt(mean(x[m]^2) + eps)
   float eps;
+  const float* inv_g;  // rowscale with M > 16: the row scales, computed by row_inv_rms_kernel
   int epi, M, N, K;
   int KB;        // k-blocks per tile
   int U;         // total units = tiles * KB
   int base, rem; // units per CTA; the first `rem` CTAs take one more
   int G;         // tile-split plan: each tile's k-blocks cut into G parts, CTA c = tile * G + part (0: stream-K)
-  float* part;   // [grid][2][M][BM] partial tiles
+  float* part;   // [grid][2][ms / 4][BM][4] partial tiles: 4 rows of one column are 16 contiguous bytes,
+                 // and a warp's 32 columns of those 4 rows 512 contiguous bytes
+  int ms;        // M rounded up to 16
   unsigned int* counters;  // per tile (self-resetting)
   unsigned int* err;       // error word
   // fused collective (COLL_NONE: plain epilogue)
@@ -335,12 +338,21 @@ __device__ __forceinline__ void rope_qkv_store(const RopeArgs& r, int m, int n, 
 // The residual rows m0 .. m0+15 of output column n (SSD_EPI_RESIDUAL; zeros otherwise), loaded
 // together before they are needed: a store loop that read each row's residual just before writing
 // it paid one L2 round trip per row (it cannot hoist a load above a store to the same array).
+// Every load is issued (rows past M and columns past N read a valid element instead and
+// are discarded), so all 16 are in flight together.
 __device__ __forceinline__ void load_residual16(const Params& p, int m0, int n, float* res) {
-  const bf16* y = reinterpret_cast<const bf16*>(p.y);
-  const bool on = p.epi == SSD_EPI_RESIDUAL && n < p.N;
+  if (p.epi != SSD_EPI_RESIDUAL) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j)
-    res[j] = (on && m0 + j < p.M) ? __bfloat162float(__ldcg(y + (int64_t)(m0 + j) * p.N + n)) : 0.f;
+    for (int j = 0; j < 16; ++j) res[j] = 0.f;
+    return;
+  }
+  const bf16* y = reinterpret_cast<const bf16*>(p.y) + min(n, p.N - 1);
+  const int last = p.M - 1;
+  uint16_t raw[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) raw[j] = __ldcg(reinterpret_cast<const unsigned short*>(y + (int64_t)min(m0 + j, last) * p.N));
+#pragma unroll
+  for (int j = 0; j < 16; ++j) res[j] = __bfloat162float(__ushort_as_bfloat16(raw[j]));
 }
 
 // every non-collective output store of the kernel; `res` is the prefetched residual (RESIDUAL)
@@ -354,6 +366,43 @@ __device__ __forceinline__ void store_out(const Params& p, int m, int n, float a
   } else if (!(p.epi == SSD_EPI_GEGLU && (n & 1))) {
     epilogue_store<bf16>(p.epi, p.y, p.N, m, n, acc, pair);
   }
+}
+
+// rsqrt(mean(x^2) + eps) of one token row, by one warp: lanes stride K in 8-element
+// vectors (lane l takes elements 8l .. 8l+7 of every 256), each lane sums its vectors
+// in K order with fma, then an xor tree -- a fixed order, so every CTA and every M
+// gets the same bits.  Eight vectors per lane are loaded before any is used (one L2
+// round trip per 2048 elements of the row instead of one per 256).
+__device__ __forceinline__ float row_inv_rms(const bf16* xr, int K, float eps, int lane) {
+  constexpr int kBatch = 8;
+  float acc = 0.f;
+  for (int k0 = lane * 8; k0 < K; k0 += kBatch * 256) {
+    uint4 buf[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) buf[i] = k0 + i * 256 < K ? ld_act_v4(xr + k0 + i * 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (k0 + i * 256 >= K) break;
+      float f[8];
+      unpack8(buf[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
+    }
+  }
+  acc = warp_sum(acc);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), eps)));
+}
+
+// The row scales of M > 16 token rows, once per projection instead of once per CTA
+// (every CTA needs all rows: at M = 224, K = 3072 that was 1.4 MB of reads per CTA
+// and a chain of L2 round trips before its first store).  One warp per row.
+__global__ void __launch_bounds__(128) row_inv_rms_kernel(const bf16* x, int M, int K, float eps, float* out) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const float r = row_inv_rms(x + (size_t)m * K, K, eps, lane);
+  if (lane == 0) out[m] = r;
 }
 
 // COLL: instantiate the fused-collective epilogue (p.coll != COLL_NONE); the
@@ -621,21 +670,14 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     };
     if (p.rowscale && (!CLU || cluster_ctarank() == 0)) {
       // RMS of each token row (the (1 + w) factor is folded into the weights):
-      // warp (q) takes rows m = q, q+4, ...; lanes stride K in 8-element vectors,
-      // xor-tree sum -- a fixed order, identical in every CTA and for any M.
-      for (int m = q; m < p.M; m += 4) {
-        const bf16* xr = p.x + (size_t)m * p.K;
-        float acc = 0.f;
-        for (int k0 = lane * 8; k0 < p.K; k0 += 32 * 8) {
-          float f[8];
-          unpack8(ld_act_v4(xr + k0), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) {
-          const float ms = __fdiv_rn(acc, (float)p.K);
-          inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+      // warp (q) takes rows m = q, q+4, ...; more than 16 rows were computed once
+      // for all CTAs by row_inv_rms_kernel (the same function, so the same bits).
+      if (p.inv_g) {
+        for (int m = (int)threadIdx.x - 64; m < p.M; m += kEpiThreads) inv_s[m] = __ldcg(p.inv_g + m);
+      } else {
+        for (int m = q; m < p.M; m += 4) {
+          const float r = row_inv_rms(p.x + (size_t)m * p.K, p.K, p.eps, lane);
+          if (lane == 0) inv_s[m] = r;
         }
       }
       epi_bar();
@@ -732,34 +774,42 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * MP);
       const int n = tile * BM + row;
-      float* mine = p.part + ((size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.M) * BM;
+      float* mine = p.part + (size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.ms * BM + 4 * row;
+      const int cend = min(MP, (p.M + 15) & ~15);
+      float nxt[16];  // the next 16 accumulator columns, read while this chunk is stored
+      tmem_ld16(taddr, nxt);
+      tmem_ld_wait();
 #pragma unroll 1
-      for (int c0 = 0; c0 < MP; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + c0, v);
-        tmem_ld_wait();
-        if (c0 >= p.M) continue;
+      for (int c0 = 0; c0 < cend; c0 += 16) {
+        float v[16], res[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = c0 + j;
-          if (whole && p.rowscale && m < p.M) v[j] = __fmul_rn(v[j], inv_s[m]);
-          const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);  // row n ^ 1 (GeGLU up, RoPE pair)
-          if (m >= p.M) continue;
-          if (whole) {
+        for (int j = 0; j < 16; ++j) v[j] = nxt[j];
+        if (c0 + 16 < cend) tmem_ld16(taddr + c0 + 16, nxt);
+        // the residual rows of this chunk are in flight together
+        // (row-parallel shapes whose K is at most 8 k-blocks, e.g. O at TP8, take this path)
+        if (!whole) {
+          // this CTA's part of a split tile: 16 rows of column n, four 16-byte stores (rows past M
+          // land in the padding and are never read)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4*>(mine + (size_t)(c0 / 4 + i) * BM * 4) =
+                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          if (!COLL) load_residual16(p, c0, n, res);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = c0 + j;
+            if (p.rowscale && m < p.M) v[j] = __fmul_rn(v[j], inv_s[m]);
+            const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);  // row n ^ 1 (GeGLU up, RoPE pair)
+            if (m >= p.M) continue;
             if constexpr (COLL) {
               if (n < p.N) push(jt_whole, tile, m, n, v[j]);
             } else if (n < p.N) {
-              // whole tiles stream wide shapes (gate/up, LM head, QKV), whose epilogues read nothing;
-              // a residual is read here only if a row-parallel shape ever takes this path
-              const float res = p.epi == SSD_EPI_RESIDUAL
-                                    ? __bfloat162float(__ldcg(reinterpret_cast<const bf16*>(p.y) + (int64_t)m * p.N + n))
-                                    : 0.f;
-              store_out<ROPE>(p, m, n, v[j], up, res, rope_pc, rope_off);
+              store_out<ROPE>(p, m, n, v[j], up, res[j], rope_pc, rope_off);
             }
-          } else {
-            mine[(size_t)m * BM + row] = v[j];
           }
         }
+        if (c0 + 16 < cend) tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(acce(buf));
@@ -796,19 +846,29 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
 #pragma unroll
         for (int i = 0; i < 16; ++i) s[i] = 0.f;
         for (int c = c_first; c <= c_last; c += 4) {
+          // all 16 vector loads are issued before the first add: contributors past c_last
+          // read a valid partial (clamped index) whose value is never used
           float v[4][16];
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            const int ci = c + cc;
-            const int e = (ci <= c_last && tile == unit_begin(p, ci) / p.KB) ? 0 : 1;
-            const float* src = p.part + ((size_t)(ci * 2 + e) * p.M + m0) * BM + row;
+            const int ci = min(c + cc, c_last);
+            const int e = tile == unit_begin(p, ci) / p.KB ? 0 : 1;
+            const float* src = p.part + (size_t)(ci * 2 + e) * p.ms * BM + (size_t)(m0 / 4) * BM * 4 + 4 * row;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[cc][i] = (ci <= c_last && i < mn) ? __ldcg(src + (size_t)i * BM) : 0.f;
+            for (int i = 0; i < 4; ++i) {
+              const float4 t = __ldcg(reinterpret_cast<const float4*>(src + (size_t)i * BM * 4));
+              v[cc][4 * i] = t.x;
+              v[cc][4 * i + 1] = t.y;
+              v[cc][4 * i + 2] = t.z;
+              v[cc][4 * i + 3] = t.w;
+            }
           }
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
+          for (int cc = 0; cc < 4; ++cc) {
+            if (c + cc > c_last) break;
 #pragma unroll
             for (int i = 0; i < 16; ++i) s[i] += v[cc][i];
+          }
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -991,10 +1051,12 @@ void plan(int M, int N, int K, int sms, Params& p, int& grid) {
 
 // Stream-K launches one CTA per SM, the tile-split plan up to two: the partial
 // buffer [grid][2][M][BM] is sized for twice the SM count.
+// Layout: tile counters | error word | partials [2 * SMs][2][M rounded up to 16][BM] | row scales [256].
 size_t workspace_bytes(int M, int N, int K) {
   (void)N;
   (void)K;
-  return kCounterBytes + 256 + sizeof(float) * (size_t)num_sms() * 4 * M * BM;
+  const size_t ms = (size_t)((M + 15) & ~15);
+  return kCounterBytes + 256 + sizeof(float) * ((size_t)num_sms() * 4 * ms * BM + 256);
 }
 
 template <int MP>
@@ -1019,6 +1081,14 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
   p.counters = reinterpret_cast<unsigned int*>(wsb);
   p.err = reinterpret_cast<unsigned int*>(wsb + kCounterBytes);
   p.part = reinterpret_cast<float*>(wsb + kCounterBytes + 256);
+  p.ms = (M + 15) & ~15;
+  p.inv_g = nullptr;
+  if (rowscale && M > 16) {
+    float* inv = p.part + (size_t)num_sms() * 4 * p.ms * BM;
+    SSD_PDL(row_inv_rms_kernel, (M + 3) / 4, 128, 0, st, reinterpret_cast<const bf16*>(x), M, K, eps, inv);
+    SSD_CHECK_LAUNCH();
+    p.inv_g = inv;
+  }
   p.coll = COLL_NONE;
   if (ra) p.rope = *ra;
   if (ca && ca->mode != COLL_NONE) {

@@ -483,15 +483,17 @@ constexpr int kTopPThreads = 1024;
 constexpr int kTopPBins = 2048;
 constexpr int kTopPCap = 4096;
 constexpr double kTopPFix = 17592186044416.0;  // 2^44: V * 2^44 stays below 2^63 for V < 2^19
+static_assert(kTopPBins == 2 * kTopPThreads, "the bin scan gives every thread two bins");
 
 __global__ void __launch_bounds__(kTopPThreads)
 top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
-  __shared__ unsigned long long massq[kTopPBins];  // bin masses in units of 2^-44
+  __shared__ unsigned long long massq[kTopPBins];  // bin masses in units of 2^-44; later candidate masses
   __shared__ float cand[kTopPCap];
   __shared__ float redf[32];
   __shared__ double redd[32];
-  __shared__ int s_bin, s_ncand;
-  __shared__ double s_above, s_target;
+  __shared__ unsigned long long wscan[32];
+  __shared__ int s_bin, s_ncand, s_found;
+  __shared__ double s_above;
   __shared__ float s_t;
   pdl_wait();
   float* row = x + (int64_t)blockIdx.x * ld;
@@ -526,30 +528,52 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
       else below += w;
     }
     below = block_reduce(below, redd, OpSum());
-    if (threadIdx.x == 0) {
-      unsigned long long inq = 0ull;
-      for (int i = 0; i < kTopPBins; ++i) inq += massq[i];
-      const double in_range = (double)inq / kTopPFix;
-      if (level == 0) target = top_p * (in_range + below);
-      unsigned long long cum = 0ull;
-      int bb = 0;
-      for (; bb < kTopPBins; ++bb) {
-        if (above + (double)(cum + massq[bb]) / kTopPFix >= target) break;
-        cum += massq[bb];
+    // Inclusive prefix sums of the integer bin masses (exact, so any order gives the same
+    // sums): thread i owns bins 2i and 2i + 1.  The cutoff bin is the first whose prefix
+    // reaches the target -- the same test, on the same sums, as a walk down the bins.
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int b0i = 2 * threadIdx.x;
+    const unsigned long long q0 = massq[b0i], q1 = massq[b0i + 1];
+    unsigned long long incl = q0 + q1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) wscan[wid] = incl;
+    if (threadIdx.x == 0) s_bin = kTopPBins;
+    __syncthreads();
+    if (wid == 0) {
+      unsigned long long v = wscan[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
       }
-      s_bin = bb < kTopPBins ? bb : -1;
-      s_above = above + (double)cum / kTopPFix;
-      s_target = target;
-      s_t = -INFINITY;  // cutoff below both ranges: keep every finite logit
-      if (bb >= kTopPBins) above += in_range;
+      wscan[lane] = v;
     }
     __syncthreads();
-    b = s_bin;
-    if (threadIdx.x != 0) {
+    const unsigned long long excl = (wid > 0 ? wscan[wid - 1] : 0ull) + incl - (q0 + q1);  // bins < 2i
+    const unsigned long long inq = wscan[31];
+    const double in_range = (double)inq / kTopPFix;
+    if (level == 0) target = top_p * (in_range + below);
+    int mine = kTopPBins;
+    if (above + (double)(excl + q0) / kTopPFix >= target) mine = b0i;
+    else if (above + (double)(excl + q0 + q1) / kTopPFix >= target) mine = b0i + 1;
+    if (mine < kTopPBins) atomicMin(&s_bin, mine);
+    __syncthreads();
+    const int bb = s_bin;
+    if (bb < kTopPBins && bb == mine) s_above = above + (double)(mine == b0i ? excl : excl + q0) / kTopPFix;
+    __syncthreads();
+    if (bb < kTopPBins) {
+      b = bb;
       above = s_above;
-      target = s_target;
+    } else {
+      above += in_range;  // cutoff below this range
     }
+    __syncthreads();  // s_bin and s_above are rewritten at the next level
   }
+  if (threadIdx.x == 0) s_t = -INFINITY;  // cutoff below both ranges: keep every finite logit
   if (b >= 0) {
     if (threadIdx.x == 0) s_ncand = 0;
     __syncthreads();
@@ -589,17 +613,32 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
           __syncthreads();
         }
       }
+      // Walk down the sorted candidates until the running mass reaches the target: the masses
+      // are computed by all threads (kTopPBins at a time, into the histogram's storage), the
+      // running sum stays one thread's sequential fp64 sum, in candidate order.
+      double* wv = reinterpret_cast<double*>(massq);
+      double cum = above;  // thread 0's running mass
       if (threadIdx.x == 0) {
-        double cum = s_above;
-        float t = n > 0 ? cand[n - 1] : -INFINITY;
-        for (unsigned int i = 0; i < n; ++i) {
-          cum += exp(-(md - (double)cand[i]) * inv_t);
-          if (cum >= s_target) {
-            t = cand[i];
-            break;
+        s_found = 0;
+        s_t = n > 0 ? cand[n - 1] : -INFINITY;
+      }
+      for (unsigned int base = 0; base < n; base += kTopPBins) {
+        __syncthreads();  // the previous part has been walked (and s_found set)
+        if (s_found) break;
+        const unsigned int cnt = min(n - base, (unsigned int)kTopPBins);
+        for (unsigned int i = threadIdx.x; i < cnt; i += kTopPThreads)
+          wv[i] = exp(-(md - (double)cand[base + i]) * inv_t);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          for (unsigned int i = 0; i < cnt; ++i) {
+            cum += wv[i];
+            if (cum >= target) {
+              s_t = cand[base + i];
+              s_found = 1;
+              break;
+            }
           }
         }
-        s_t = t;
       }
     }
   }

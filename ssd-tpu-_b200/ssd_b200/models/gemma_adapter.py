@@ -20,6 +20,9 @@ with a real paged KV cache instead of the reference's dummy one:
 
 from __future__ import annotations
 
+import time
+from typing import Callable
+
 import torch
 
 from ..algorithm.verify import argmax_rows
@@ -190,7 +193,8 @@ class GemmaAdapter:
             feed = [spec[-1]]
         return spec, logits
 
-    def draft_branches(self, prefix_tokens: list[int], feeds: list[list[int]], k: int) -> list[list[int]]:
+    def draft_branches(self, prefix_tokens: list[int], feeds: list[list[int]], k: int,
+                       stop: Callable[[], bool] | None = None) -> list[list[int]]:
         """k greedy draft tokens for each branch ``prefix + feeds[i]``, all branches at once.
 
         Row 0 is brought to hold exactly the prefix (common-prefix reuse, as in
@@ -200,6 +204,11 @@ class GemmaAdapter:
         branch rows are released.  Each branch's tokens equal
         ``draft_speculate(prefix + feeds[i], k)[0]`` (batch invariance); branch
         attention is the paged attention over the forked tables.
+
+        ``stop``: polled while each forward runs (the host then issues one forward
+        at a time); once it returns True no further forward is issued, the branch
+        rows are released and the branches finished so far are returned (a
+        prefix of ``feeds``' order, possibly shorter than ``feeds``).
         """
         prefix = [int(t) for t in prefix_tokens]
         n_all = len(feeds)
@@ -242,14 +251,30 @@ class GemmaAdapter:
             tables = self.pm.tables[1:1 + n]
             self.runner.forward(toks, base, self.cache.pages, tables, lg, q_lens=qlen, last_only=True)
             argmax_rows(lg, nxt[0])
+            stopped = False
             for i in range(1, k):
+                if stop is not None and self._wait_or_stop(stop):
+                    stopped = True
+                    break
                 self.runner.forward(nxt[i - 1].view(n, 1), base + qlen + (i - 1), self.cache.pages, tables, lg,
                                     last_only=True)
                 argmax_rows(lg, nxt[i])
             self.pm.free_rows(1, n)
+            if stopped:
+                break
             host = nxt.t().cpu().tolist()
             out.extend([int(x) for x in row] for row in host)
         return out
+
+    def _wait_or_stop(self, stop: Callable[[], bool]) -> bool:
+        """Wait for the work issued so far, polling ``stop``; True as soon as it returns True."""
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.dev))
+        while not ev.query():
+            if stop():
+                return True
+            time.sleep(50e-6)
+        return stop()
 
     def tokenize(self, text: str) -> list[int]:
         return [b % self.vocab_size for b in text.encode("utf-8")]

@@ -242,12 +242,15 @@ class LLMEngine:
         self._emit(seq, [recovery], sampling.max_new_tokens, on_token)
         collector.record_first_token()
         acc = 0
+        commit: list[int] | None = None
         while not seq.is_finished(None, sampling.max_new_tokens):
             t0 = time.perf_counter()
             key = torch.tensor([[seq.seq_id, acc, recovery]], dtype=torch.int32)
             self.draft_worker.submit(DraftRequest(DraftCommand.SERVE, key, torch.tensor([seq.num_tokens]),
                                                   torch.zeros((1, 1), dtype=torch.int32), torch.zeros(1),
                                                   prefix_tokens=[list(seq.token_ids)]))
+            if commit is not None:  # the previous step's commit runs on the target while the draft drafts
+                self.ranks.call("target_commit", commit)
             resp = self.draft_worker.get_response()
             t1 = time.perf_counter()
             spec = [int(t) for t in resp.spec_tokens[0].tolist()]
@@ -256,9 +259,10 @@ class LLMEngine:
                 raise RuntimeError(f"tensor-parallel ranks disagree on the verify outcome: {outcomes}")
             acc, recovery, verify_ms = outcomes[0]
             commit = spec[:acc] + [recovery]
-            self.ranks.call("target_commit", commit)
             n = self._emit(seq, commit, sampling.max_new_tokens, on_token)
             collector.record_step(StepMetrics(target_verify_ms=(time.perf_counter() - t0) * 1000,
                                               draft_step_ms=(t1 - t0) * 1000, cache_hit=bool(resp.cache_hit[0]),
                                               accepted_tokens=n, verify_device_ms=verify_ms))
             collector.record_accepts([acc])
+        if commit is not None:
+            self.ranks.call("target_commit", commit)

@@ -18,10 +18,15 @@ stream:
    drafted together (``GemmaAdapter.draft_branches``: the committed prefix is
    forked into branch rows that share its KV pages, then k batched forwards --
    the paged attention over forked tables is the reference's branch mask,
-   jax_ssd/kernels/masks.py:8-30).  The rebuild finishes before the next request
-   is served (as in the reference, which rebuilds inside ``_handle``); it
-   overlaps the target's verify when the engine runs the draft on another device
-   or stream.  The reference builds the same keys
+   jax_ssd/kernels/masks.py:8-30).  The rebuild overlaps the target's verify when
+   the engine runs the draft on another device or stream.  It yields to the next
+   request as soon as that request names a key the rebuild is not drafting (the
+   rebuild cannot serve it, so finishing would only delay its miss draft); a
+   request whose key is being drafted waits for the rebuild and hits.  Results do
+   not depend on this: a hit serves the tokens a miss would draft.  A miss drafts
+   k tokens and responds; the bonus forward the rebuild needs for the a = k
+   candidates runs after the response, off the request's path.  The reference
+   (which rebuilds inside ``_handle``) builds the same keys
    (workers.py:119-145) from top-F of all-zero glue logits, i.e. candidates
    ``0..F-1``, and drafts them from the candidate alone.
 """
@@ -132,13 +137,24 @@ class DraftWorker:
                 rows.append(tokens[i])
                 plans.append((keys_h[i], prefix, spec, None))
                 continue
-            spec, logits = self.model.draft_speculate(prefix, k, with_bonus=self.prefetch)
+            spec, logits = self.model.draft_speculate(prefix, k)
             rows.append(torch.tensor(spec, dtype=torch.int32, device=self.model.dev))
-            plans.append((keys_h[i], prefix, spec, logits))
+            plans.append((keys_h[i], prefix, spec, logits))  # logits [k, V]: the bonus row comes later
         spec_tokens = torch.stack(rows)
         self.stream.synchronize()
         return DraftResponse(cache_hit=hit, spec_tokens=spec_tokens,
                              draft_logits=torch.zeros((len(rows), k, 1), dtype=torch.float32)), plans
+
+    def _next_request_misses(self, drafting: set) -> bool:
+        """True when a request is queued and one of its keys is not in ``drafting``."""
+        with self.request_queue.mutex:
+            if not self.request_queue.queue:
+                return False
+            req = self.request_queue.queue[0]
+        if req.command != DraftCommand.SERVE:
+            return True
+        keys = {tuple(int(v) for v in row) for row in req.cache_keys.reshape(-1, 3).tolist()}
+        return not keys <= drafting
 
     def _rebuild_cache(self, plans: list) -> None:
         """Pre-draft the next request's branches (see the module docstring).
@@ -153,10 +169,16 @@ class DraftWorker:
         if len(fan) < k + 1:
             fan = fan + (fan[-1],) * (k + 1 - len(fan))
         self.cache.reset()
+        nothing: set = set()
         branches = []
         for key, prefix, spec, logits in plans:
+            if self._next_request_misses(nothing):  # the cache is empty: nothing to wait for
+                return
             if logits is None:  # served from the cache: draft once more for the glue logits
                 spec, logits = self.model.draft_speculate(prefix, k, with_bonus=True)
+            elif logits.shape[0] == k:  # a miss: the bonus row (one forward over the last draft)
+                _, bonus = self.model.draft_speculate(prefix + spec, 0, with_bonus=True)
+                logits = torch.cat([logits, bonus])
             q = torch.softmax(logits.float(), dim=-1)
             q_spec = q[torch.arange(k, device=q.device), torch.tensor(spec, device=q.device)].tolist()
             reach = 1.0  # prod_{j<a} q_j(s_j)
@@ -173,6 +195,8 @@ class DraftWorker:
                     reach *= q_spec[a]
         branches.sort(key=lambda b: -b[0])
         chosen = branches[: self.cache.keys.shape[0]]
+        drafting = {(sid, a, c) for _, sid, a, c, _f, _p in chosen}
+        stop = lambda: self._next_request_misses(drafting)  # noqa: E731
         by_prefix: dict[int, list] = {}
         for slot, br in enumerate(chosen):
             by_prefix.setdefault(id(br[5]), []).append((slot, br))
@@ -180,10 +204,16 @@ class DraftWorker:
             prefix = group[0][1][5]
             if hasattr(self.model, "draft_branches"):
                 # every branch of one request at once: forked trunk pages, batched draft forwards
-                specs = self.model.draft_branches(prefix, [br[4] for _, br in group], k)
+                specs = self.model.draft_branches(prefix, [br[4] for _, br in group], k, stop=stop)
             else:
-                specs = [self.model.draft_speculate(prefix + br[4], k)[0] for _, br in group]
+                specs = []
+                for _, br in group:
+                    if stop():
+                        break
+                    specs.append(self.model.draft_speculate(prefix + br[4], k)[0])
             for (slot, (_, sid, a, c, _feed, _p)), sp in zip(group, specs):
                 self.cache.insert(slot, [sid, a, c], sp)
                 self.branches_drafted += 1
+            if len(specs) < len(group):  # yielded to a request the rebuild cannot serve
+                break
         self.stream.synchronize()

@@ -128,7 +128,8 @@ def test_tcgen05_shapes_and_tails(cuda, m, n, k):
 
 @pytest.mark.parametrize("dtype_name,m,n,k,epi", [("bf16", 5, 12288, 3072, "store"), ("bf16", 5, 2 * 24576, 3072, "geglu"),
                                                   ("bf16", 1, 2560, 2048, "store"), ("f32", 5, 1024, 256, "store"),
-                                                  ("f32", 3, 2048, 256, "geglu")])
+                                                  ("f32", 3, 2048, 256, "geglu"), ("bf16", 224, 12288, 3072, "store"),
+                                                  ("bf16", 32, 2 * 16384, 2048, "geglu")])
 def test_rownorm_projection(cuda, dtype_name, m, n, k, epi):
     """ssd_linear_rownorm = round(rsqrt(mean(x^2)+eps) * (x w^T)), the folded-norm projection."""
     import torch
@@ -163,22 +164,23 @@ def test_tile_split_rows_match_across_m(cuda, n, k):
     """Shapes with at most as many 128-row output tiles as SMs cut every tile's K range into G
     parts: for M <= 16 the G CTAs of a tile form one thread-block cluster and fold their partials in
     distributed shared memory, for larger M the same parts go through the global ticket fold.  Every
-    row is bit-identical for M = 1, 5, 16 and 40 (plain, row-norm and residual epilogues)."""
+    row is bit-identical for M = 1, 5, 16, 40 and 224 (plain, row-norm and residual epilogues; above
+    16 rows the row norms come from their own kernel, below from the projection's epilogue)."""
     import torch
 
     from ssd_b200.kernels.ops import linear
     from ssd_b200.workspace import workspace
 
     g = torch.Generator(device="cuda").manual_seed(n + k)
-    x = (2.0 * torch.randn((40, k), device="cuda", generator=g)).bfloat16()
+    x = (2.0 * torch.randn((224, k), device="cuda", generator=g)).bfloat16()
     w = (torch.randn((n, k), device="cuda", generator=g) / k ** 0.5).bfloat16()
-    res = torch.randn((40, n), device="cuda", generator=g).bfloat16()
+    res = torch.randn((224, n), device="cuda", generator=g).bfloat16()
     full = linear(x, w, "store_f32", ws_key="split_test")
     torch.testing.assert_close(full, x.float() @ w.float().T, rtol=1e-4, atol=1e-4)
     full_norm = linear(x, w, "store", rownorm_eps=1e-6, ws_key="split_test")
     full_res = res.clone()
     linear(x, w, "residual", out=full_res, ws_key="split_test")
-    for m in (1, 5, 16):
+    for m in (1, 5, 16, 40):
         assert torch.equal(linear(x[:m].contiguous(), w, "store_f32", ws_key="split_test"), full[:m])
         assert torch.equal(linear(x[:m].contiguous(), w, "store", rownorm_eps=1e-6, ws_key="split_test"),
                            full_norm[:m])

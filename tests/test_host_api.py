@@ -74,3 +74,31 @@ def test_slot_scheduler_refills_freed_slots():
     assert s.slots() == [(1, seqs[4])] and s.free_slots() == [0] and s.has_work()
     s.retire(1)
     assert not s.has_work() and [q.seq_id for q in s.finished] == [1, 0, 2, 3, 4]
+
+
+def test_draft_worker_yields_only_to_requests_it_cannot_serve():
+    """The cache rebuild keeps going while the queued request's keys are all being drafted,
+    and stops for a request (or a shutdown) it cannot serve."""
+    from ssd_b200.algorithm.async_protocol import DraftCommand, DraftRequest
+    from ssd_b200.runtime.workers import DraftWorker
+
+    w = DraftWorker(SSDConfig(), draft_model=None)
+    drafting = {(7, 0, 11), (7, 1, 12), (7, 4, 3)}
+    assert not w._next_request_misses(drafting)  # nothing queued
+
+    def req(keys, cmd=DraftCommand.SERVE):
+        z = torch.zeros(0)
+        return DraftRequest(cmd, torch.tensor(keys, dtype=torch.int32), z, z, z)
+
+    w.submit(req([[7, 1, 12]]))
+    assert not w._next_request_misses(drafting)  # its key is being drafted: finish and hit
+    assert w._next_request_misses(set())
+    w.request_queue.get()
+    w.submit(req([[7, 1, 13]]))
+    assert w._next_request_misses(drafting)  # a miss either way: yield to it now
+    w.request_queue.get()
+    w.submit(req([[7, 0, 11], [7, 2, 5]]))
+    assert w._next_request_misses(drafting)  # one row of the request is not covered
+    w.request_queue.get()
+    w.submit(req(torch.zeros((0, 3)).tolist(), DraftCommand.SHUTDOWN))
+    assert w._next_request_misses(drafting)

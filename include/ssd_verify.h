@@ -316,7 +316,10 @@ typedef struct {
   size_t ctrl_offset;              /* control block (ssd_comm_ctrl_bytes), zero-filled before first use */
   size_t recv_offset, recv_bytes;  /* all-reduce receive area (>= ssd_comm_recv_bytes) */
   int recv_rows, recv_tiles;       /* its shape: the max_m and ceil(max_n / 128) it was sized for */
+  int allreduce_form;              /* SSD_ALLREDUCE_AUTO (0), _ALL_TO_ALL or _OWNER; same on every rank */
 } ssd_comm;
+/* Forms of the fused all-reduce (ssd_linear_allreduce); every form gives the same bits. */
+enum { SSD_ALLREDUCE_AUTO = 0, SSD_ALLREDUCE_ALL_TO_ALL = 1, SSD_ALLREDUCE_OWNER = 2 };
 
 /* Bytes of the control block (multiple of 256). */
 size_t ssd_comm_ctrl_bytes(void);
@@ -337,6 +340,11 @@ int ssd_ipc_close(void* ptr, size_t offset);
  * order, of x_r[M,K] w_r[N,K]^T), where x_r / w_r are rank r's column shards.
  * bf16 only; every rank ends with bit-identical y.  Uses the
  * ssd_linear_workspace_size(M, N, K) workspace.
+ * Forms (comm->allreduce_form): ALL_TO_ALL -- every rank sends each fp32 partial
+ * to every rank, which folds all of them (one hop); OWNER -- each partial goes to
+ * the output tile's owner rank (tile % world) only, which folds and sends the sum
+ * to the others (two hops, about 2/world of the bytes); AUTO takes OWNER where it
+ * saves more than 4 MB per rank and M > 16, else ALL_TO_ALL.
  */
 int ssd_linear_allreduce(ssd_stream_t stream, const void* x, const void* w, void* y, int M, int N, int K,
                          void* workspace, size_t workspace_bytes, const ssd_comm* comm);

@@ -61,6 +61,8 @@ int linear_allreduce_impl(cudaStream_t st, const void* x, const void* w, void* y
   a.dst_off = c->recv_offset;
   a.recv_rows = c->recv_rows;
   a.recv_tiles = c->recv_tiles;
+  if (c->allreduce_form < SSD_ALLREDUCE_AUTO || c->allreduce_form > SSD_ALLREDUCE_OWNER) return SSD_ERR_INVALID;
+  a.form = c->allreduce_form;
   return linear_tc_coll(st, x, w, y, M, N, K, ws, ws_bytes, a);
 }
 

@@ -94,6 +94,7 @@ struct CollArgs {
   size_t dst_off;       // all-reduce: receive area; all-gather: the fp32 output [M, ldy]
   int ldy, col_off;     // all-gather: row pitch and first column of this rank's block
   int recv_rows, recv_tiles;  // all-reduce: receive slots [2][recv_tiles][world][recv_rows][128] (fp32 | count << 32)
+  int form;                   // all-reduce: SSD_ALLREDUCE_*
 };
 
 // QKV projection epilogue with RoPE and the K/V page write (weights with q/k

@@ -62,8 +62,7 @@ namespace tc {
 
 constexpr int BM = 128;       // weight rows per tile (UMMA M)
 constexpr int BK = 64;        // bf16 per k-block: one 128-byte swizzle row
-constexpr int kThreads = 192; // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
-constexpr int kEpiThreads = 128;
+// warp 0 TMA, warp 1 MMA + TMEM owner, warps 2.. epilogue (Cfg<MP>::THREADS in all)
 constexpr uint32_t kWaitLimit = 1u << 24;  // polls before a wait gives up (~seconds)
 
 struct Params {
@@ -84,6 +83,7 @@ struct Params {
   unsigned int* err;       // error word
   // fused collective (COLL_NONE: plain epilogue)
   int coll, rank, world, ldy, col_off, recv_rows, recv_tiles;
+  int owner_fold;  // all-reduce over more than 16 rows: partials go to the tile's owner only (see coll_finish)
   char* heaps[kMaxTP];
   size_t ctrl_off, dst_off;
   RopeArgs rope;  // epi == kEpiRopeQkv
@@ -296,9 +296,18 @@ struct Cfg {
   // barriers, TMEM slot and flags, row scales [256], RoPE row info [MP] (int + int64)
   static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16 + 4 * 256 + 12 * MP;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
+  // Epilogue warps per TMEM lane quadrant.  The epilogue issues a few dozen dependent
+  // instructions per output element; with one warp per scheduler nothing hides their
+  // latency, so tiles of 64 or more token rows get two warps per quadrant (warps w and
+  // w + 4 read the same TMEM lanes and take alternate 16-row chunks).  At most 32 rows
+  // stay at one: their CTAs are sized to share an SM with the next kernel's.
+  static constexpr int REP = MP >= 64 ? 2 : 1;
+  static constexpr int EPI = 128 * REP;  // epilogue threads
+  static constexpr int THREADS = 64 + EPI;
 };
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+template <int NT>
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
 // kEpiRopeQkv: output (m, n) of the QKV projection with rotation-paired q/k rows;
 // `pair` is the accumulator of row n ^ 1 (the other half of the rotation pair).
@@ -418,11 +427,12 @@ __global__ void __launch_bounds__(128) row_inv_rms_kernel(const bf16* x, int M, 
 // The collective and RoPE instantiations declare one resident CTA per SM as the
 // minimum (two still fit): without it ptxas held them to 96 registers and spilled.
 template <int MP, bool COLL, bool CLU, bool ROPE>
-__global__ void __launch_bounds__(kThreads, (COLL || ROPE) ? 1 : 0)
+__global__ void __launch_bounds__(Cfg<MP>::THREADS, (COLL || ROPE) ? 1 : 0)
 linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const Params p) {
   using C = Cfg<MP>;
   constexpr int S = C::STAGES;
+  constexpr int REP = C::REP, EPI = C::EPI;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -451,7 +461,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf(b), 1);
-      mbar_init(acce(b), kEpiThreads);
+      mbar_init(acce(b), EPI);
     }
     if (CLU) mbar_init(red_bar, (uint32_t)(p.G - 1));
     *abort_flag = 0;
@@ -567,6 +577,10 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     pdl_wait();  // outputs, residual inputs and the workspace belong to the previous kernel until it ends
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const int row = q * 32 + lane;
+    const int ew = warp - 2;   // epilogue warp 0 .. 4 * REP - 1
+    // which of the quadrant's REP warps: takes 16-row chunks rep, rep + REP, ... (a compile-time 0
+    // when REP is 1, so the one-warp loops keep their constant bounds)
+    const int rep = REP == 1 ? 0 : ew >> 2;
     auto n_of = [&](int tile) { return tile * BM + row; };
     // ---- fused collective: pushes of a finished tile and its completion
     auto tile_count = [&](int tile) { return *reinterpret_cast<volatile uint32_t*>(tile_count_of(p, tile)) + 1u; };
@@ -577,7 +591,9 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         const size_t o = p.dst_off + sizeof(uint64_t) * (((((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world +
                                                            p.rank) * p.recv_rows + m) * BM + (n - tile * BM));
         const uint64_t w = ((uint64_t)jt << 32) | __float_as_uint(v);
-        for (int d = 0; d < p.world; ++d) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(p.heaps[d] + o), w);
+        if (p.owner_fold) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(p.heaps[tile % p.world] + o), w);
+        else
+          for (int d = 0; d < p.world; ++d) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(p.heaps[d] + o), w);
       } else {
         const size_t o = p.dst_off + sizeof(float) * ((size_t)m * p.ldy + p.col_off + n);
         for (int d = 0; d < p.world; ++d) *reinterpret_cast<float*>(p.heaps[d] + o) = v;
@@ -588,13 +604,57 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       if (p.coll == COLL_ALLREDUCE) {
         // every thread polls its own (m, row) words of all sources -- the words it
         // pushed itself included, so no barrier orders the CTA's pushes -- and
-        // folds them in rank order: bit-identical sums on every rank
-        if (n < p.N) {
+        // folds them in rank order: bit-identical sums on every rank.
+        // owner_fold (more than 16 rows): only the tile's owner rank (tile % world)
+        // received the partials; it folds them the same way and sends each sum, as the
+        // same kind of word, into the slot [tile][owner] of every other rank, where
+        // nothing else is written for this tile; the other ranks poll that one word.
+        // Every rank then adds its own copy of the residual (identical on all ranks):
+        // the values are those of the all-to-all form, for about 2/world of its traffic.
+        const int owner = p.owner_fold ? tile % p.world : p.rank;
+        if (n < p.N && owner != p.rank) {
+          const uint64_t* slot = reinterpret_cast<const uint64_t*>(p.heaps[p.rank] + p.dst_off) +
+                                 ((((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world + owner) * p.recv_rows) * BM +
+                                 row;
+          bool ok = true;
+          for (int m0 = 16 * rep; m0 < p.M && ok; m0 += 16 * REP) {
+            uint64_t w[16];
+            float res[16];
+            load_residual16(p, m0, n, res);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = m0 + i < p.M ? ld_relaxed_sys_u64(slot + (size_t)(m0 + i) * BM) : ((uint64_t)jt << 32);
+            for (uint32_t it = 0;; ++it) {  // late words: poll again (bounded)
+              bool all = true;
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if ((uint32_t)(w[i] >> 32) != jt) {
+                  all = false;
+                  w[i] = ld_relaxed_sys_u64(slot + (size_t)(m0 + i) * BM);
+                }
+              if (all) break;
+              if (it >= kPeerWaitPolls) {
+                ok = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (m0 + i < p.M)
+                reinterpret_cast<bf16*>(p.y)[(int64_t)(m0 + i) * p.N + n] =
+                    from_f<bf16>(__fadd_rn(res[i], store_round<bf16>(__uint_as_float((uint32_t)w[i]))));
+          }
+          if (!ok) {
+            atomicExch(p.err, 5u);
+            atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
+          }
+        } else if (n < p.N) {
           const uint64_t* slot = reinterpret_cast<const uint64_t*>(p.heaps[p.rank] + p.dst_off) +
                                  (((size_t)(jt & 1u) * p.recv_tiles + tile) * p.world) * p.recv_rows * BM + row;
           bool ok = true;
           const bf16* yres = reinterpret_cast<const bf16*>(p.y);
-          for (int m0 = 0; m0 < p.M; m0 += 4) {
+          for (int m0 = 4 * rep; m0 < p.M; m0 += 4 * REP) {
             uint64_t w[4][kMaxTP];
             float res[4];
 #pragma unroll
@@ -633,6 +693,13 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                 if (r < p.world) sum += __uint_as_float((uint32_t)w[i][r]);
               reinterpret_cast<bf16*>(p.y)[(int64_t)(m0 + i) * p.N + n] =
                   from_f<bf16>(__fadd_rn(res[i], store_round<bf16>(sum)));
+              if (p.owner_fold) {  // the sum to every other rank's slot [tile][owner]
+                const size_t o = p.dst_off + sizeof(uint64_t) * (((((size_t)(jt & 1u) * p.recv_tiles + tile) *
+                                                                     p.world + p.rank) * p.recv_rows + m0 + i) * BM + row);
+                const uint64_t word = ((uint64_t)jt << 32) | __float_as_uint(sum);
+                for (int d = 0; d < p.world; ++d)
+                  if (d != p.rank) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(p.heaps[d] + o), word);
+              }
             }
             if (!ok) break;
           }
@@ -641,13 +708,13 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             atomicExch(ctrl_of(p, p.rank) + 2, (unsigned int)SSD_ERR_TIMEOUT);
           }
         }
-        epi_bar();  // every thread has read the tile count before it advances
+        epi_bar<EPI>();  // every thread has read the tile count before it advances
         if (threadIdx.x == 64) *tile_count_of(p, tile) = jt;
         return;
       }
       // all-gather: the barrier puts every epilogue thread's pushes before thread
       // 64's system-scope fence and flag stores (cumulativity)
-      epi_bar();
+      epi_bar<EPI>();
       if (threadIdx.x == 64) {
         fence_acq_rel_sys();
         for (int d = 0; d < p.world; ++d) st_relaxed_sys(flag_of(p, d, p.rank, tile), jt);
@@ -673,19 +740,19 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       // warp (q) takes rows m = q, q+4, ...; more than 16 rows were computed once
       // for all CTAs by row_inv_rms_kernel (the same function, so the same bits).
       if (p.inv_g) {
-        for (int m = (int)threadIdx.x - 64; m < p.M; m += kEpiThreads) inv_s[m] = __ldcg(p.inv_g + m);
+        for (int m = (int)threadIdx.x - 64; m < p.M; m += EPI) inv_s[m] = __ldcg(p.inv_g + m);
       } else {
-        for (int m = q; m < p.M; m += 4) {
+        for (int m = REP == 1 ? q : ew; m < p.M; m += 4 * REP) {
           const float r = row_inv_rms(p.x + (size_t)m * p.K, p.K, p.eps, lane);
           if (lane == 0) inv_s[m] = r;
         }
       }
-      epi_bar();
+      epi_bar<EPI>();
     }
     if constexpr (ROPE) {
       if (!CLU || cluster_ctarank() == 0) {  // the CTAs that store outputs
-        for (int m = (int)threadIdx.x - 64; m < p.M; m += kEpiThreads) rope_row_info(p.rope, m, rope_pc, rope_off);
-        epi_bar();
+        for (int m = (int)threadIdx.x - 64; m < p.M; m += EPI) rope_row_info(p.rope, m, rope_pc, rope_off);
+        epi_bar<EPI>();
       }
     }
     if constexpr (CLU) {
@@ -716,7 +783,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
           if (j < p.M) red[j * BM + row] = v[j];
         // the barrier orders all epilogue threads' stores before thread 64's
         // cluster-scope release (cumulativity)
-        epi_bar();
+        epi_bar<EPI>();
         if (threadIdx.x == 64) mbar_arrive_remote(mapa(red_bar, 0));
       } else {
         if (!wait_cluster_bounded(red_bar, 0u, 4u * kWaitLimit)) {
@@ -776,15 +843,17 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       const int n = tile * BM + row;
       float* mine = p.part + (size_t)(cta * 2 + (tile == first_tile ? 0 : 1)) * p.ms * BM + 4 * row;
       const int cend = min(MP, (p.M + 15) & ~15);
-      float nxt[16];  // the next 16 accumulator columns, read while this chunk is stored
-      tmem_ld16(taddr, nxt);
-      tmem_ld_wait();
+      float nxt[16];  // this warp's next 16 accumulator columns, read while a chunk is stored
+      if (REP == 1 || 16 * rep < cend) {  // (one warp: cend >= 16 always)
+        tmem_ld16(taddr + 16 * rep, nxt);
+        tmem_ld_wait();
+      }
 #pragma unroll 1
-      for (int c0 = 0; c0 < cend; c0 += 16) {
+      for (int c0 = 16 * rep; c0 < cend; c0 += 16 * REP) {
         float v[16], res[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = nxt[j];
-        if (c0 + 16 < cend) tmem_ld16(taddr + c0 + 16, nxt);
+        if (c0 + 16 * REP < cend) tmem_ld16(taddr + c0 + 16 * REP, nxt);
         // the residual rows of this chunk are in flight together
         // (row-parallel shapes whose K is at most 8 k-blocks, e.g. O at TP8, take this path)
         if (!whole) {
@@ -809,7 +878,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             }
           }
         }
-        if (c0 + 16 < cend) tmem_ld_wait();
+        if (c0 + 16 * REP < cend) tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(acce(buf));
@@ -822,7 +891,7 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
       // (an acq_rel RMW: release of our partials, acquire of the others' for the
       // last contributor); the second barrier extends the acquire to all
       // epilogue threads, whose fold loads read L2 (.cg).  No per-thread fence.
-      epi_bar();
+      epi_bar<EPI>();
       const int c_first = cta_of_unit(p, tile * p.KB);
       const int c_last = cta_of_unit(p, tile * p.KB + p.KB - 1);
       if (threadIdx.x == 64) {
@@ -831,15 +900,15 @@ linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         if (last) *reinterpret_cast<volatile unsigned int*>(&p.counters[tile]) = 0u;  // self-reset (stream-ordered)
         *last_flag = last ? 1 : 0;
       }
-      epi_bar();
+      epi_bar<EPI>();
       const bool last = *last_flag != 0;
-      epi_bar();  // everyone has read the flag before the next tile may rewrite it
+      epi_bar<EPI>();  // everyone has read the flag before the next tile may rewrite it
       if (!last) continue;
       const uint32_t jt = COLL ? tile_count(tile) : 0u;
       // Fold the contributors in CTA (= K) order.  Rows are taken 16 at a time and
       // contributors 4 at a time so up to 64 independent L2 loads are in flight
       // per thread; the summation order per output stays c_first .. c_last.
-      for (int m0 = 0; m0 < p.M; m0 += 16) {
+      for (int m0 = 16 * rep; m0 < p.M; m0 += 16 * REP) {
         const int mn = min(16, p.M - m0);
         float s[16], res[16];
         if (!COLL) load_residual16(p, m0, n, res);
@@ -995,7 +1064,7 @@ bool clusters_fit(int G, int tiles) {
     if (prepare_kernel<16, false, true, false>() == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(G * tiles);
-      cfg.blockDim = dim3(kThreads);
+      cfg.blockDim = dim3(Cfg<16>::THREADS);
       cfg.dynamicSmemBytes = Cfg<16>::SMEM;
       cudaLaunchAttribute a[1];
       a[0].id = cudaLaunchAttributeClusterDimension;
@@ -1102,6 +1171,15 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
     p.dst_off = ca->dst_off;
     p.recv_rows = ca->recv_rows;
     p.recv_tiles = ca->recv_tiles;
+    // The owner-fold form sends about 2 (world - 1) / world of a rank's partial bytes where the
+    // all-to-all form sends world - 1 of them, for one more hop (a poll and a push, a few us).  It
+    // is taken where that saves more than 4 MB per rank (about 6 us of NVLink), which needs at
+    // least 4 ranks and many rows (e.g. 7B O/down at 8 ranks from 33 rows on); it is never
+    // taken for 16 rows or fewer.  Both forms give the same bits (the caller may pick one).
+    const double saved = (double)(ca->world - 1) * (ca->world - 2) / ca->world * M * N * sizeof(uint64_t);
+    const bool owner = ca->form == SSD_ALLREDUCE_OWNER ||
+                       (ca->form == SSD_ALLREDUCE_AUTO && M > 16 && saved > 4.0 * (1 << 20));
+    p.owner_fold = (ca->mode == COLL_ALLREDUCE && ca->world > 1 && owner) ? 1 : 0;
   }
   if constexpr (MP == 16) {
     if (p.G >= 2 && clusters_fit(p.G, grid / p.G)) {
@@ -1112,7 +1190,7 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
         return SSD_ERR_LAUNCH;
       auto kern = coll ? linear_tc_kernel<16, true, true, false>
                        : rope ? linear_tc_kernel<16, false, true, true> : linear_tc_kernel<16, false, true, false>;
-      if (launch_pdl_cluster(kern, dim3(grid), dim3(kThreads), C::SMEM, st, (unsigned)p.G, wm, xm, p) !=
+      if (launch_pdl_cluster(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, (unsigned)p.G, wm, xm, p) !=
           cudaSuccess) {
         (void)cudaGetLastError();
         return SSD_ERR_LAUNCH;
@@ -1127,7 +1205,7 @@ int launch(cudaStream_t st, const void* x, const void* w, void* y, int epi, int 
             : rope ? prepare_kernel<MP, false, false, true> () : prepare_kernel<MP, false, false, false>()) !=
       cudaSuccess)
     return SSD_ERR_LAUNCH;
-  SSD_PDL(kern, grid, kThreads, C::SMEM, st, wm, xm, p);
+  SSD_PDL(kern, grid, C::THREADS, C::SMEM, st, wm, xm, p);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }

@@ -208,7 +208,7 @@ extern "C" const char* ssd_status_string(int status) {
   }
 }
 
-extern "C" int ssd_abi_version(void) { return (1 << 16) | 0; }
+extern "C" int ssd_abi_version(void) { return (1 << 16) | 1; }
 
 extern "C" int ssd_linear_max_m(void) { return max_m(); }
 

@@ -71,6 +71,7 @@ SIGNATURES = {
 }
 
 SSD_MAX_TP = 8
+SSD_ALLREDUCE_AUTO, SSD_ALLREDUCE_ALL_TO_ALL, SSD_ALLREDUCE_OWNER = 0, 1, 2
 
 
 class CommC(C.Structure):
@@ -79,6 +80,7 @@ class CommC(C.Structure):
     _fields_ = [
         ("rank", _i), ("world", _i), ("heaps", _p * SSD_MAX_TP), ("heap_bytes", _sz),
         ("ctrl_offset", _sz), ("recv_offset", _sz), ("recv_bytes", _sz), ("recv_rows", _i), ("recv_tiles", _i),
+        ("allreduce_form", _i),
     ]
 
 

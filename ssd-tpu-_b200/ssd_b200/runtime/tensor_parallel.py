@@ -29,7 +29,7 @@ import ctypes as C
 
 import torch
 
-from .._lib import SSD_MAX_TP, CommC, check, lib
+from .._lib import SSD_ALLREDUCE_ALL_TO_ALL, SSD_ALLREDUCE_AUTO, SSD_ALLREDUCE_OWNER, SSD_MAX_TP, CommC, check, lib
 
 
 class TPComm:
@@ -96,7 +96,12 @@ class TPComm:
         c.recv_offset = self.ctrl_bytes
         c.recv_bytes = self.recv_bytes
         c.recv_rows, c.recv_tiles = self.max_m, (self.max_n + 127) // 128
+        c.allreduce_form = SSD_ALLREDUCE_AUTO
         self.cstruct = c
+
+    def set_allreduce_form(self, form: int) -> None:
+        """SSD_ALLREDUCE_AUTO / _ALL_TO_ALL / _OWNER for the following all-reduces (every rank alike)."""
+        self.cstruct.allreduce_form = int(form)
 
     def alloc(self, shape, dtype=torch.float32) -> torch.Tensor:
         """A symmetric buffer (same heap offset on every rank), 256-byte aligned, zero-filled."""
@@ -200,7 +205,10 @@ def tp_selfcheck(all_gather, device=None, heap_bytes: int = 64 << 20) -> dict:
       sums is the only difference);
     * ``sd_equals_ar``: greedy speculative decoding on the sharded pair reproduces the sharded
       target's AR stream (``self_sd_equals_ar``: with the target as its own draft, every draft is
-      accepted and the stream is still the AR stream).
+      accepted and the stream is still the AR stream);
+    * ``allreduce_exact``: ``linear_allreduce`` at 5, 40 and 224 rows, in each of its forms (automatic,
+      all-to-all, via the tile's owner), equals, bit for bit, bf16(y + bf16(sum of the ranks' fp32
+      partials in rank order)), the partials being each rank's plain projection of its shard.
 
     ``all_gather(tensor) -> list[tensor]`` gathers a CUDA tensor from every rank.  Returns a dict;
     ``ok`` is the conjunction of the checks and of a zero collective status.
@@ -236,6 +244,30 @@ def tp_selfcheck(all_gather, device=None, heap_bytes: int = 64 << 20) -> dict:
         good = same and diff <= 2e-2 * max(scale, 1.0)
         out[name] = {"max_diff": diff, "scale": scale, "ranks_identical": same, "ok": good}
         ok = ok and good
+    from ..kernels.ops import linear, linear_allreduce
+
+    exact = {}
+    for m in (5, 40, 224):
+        g = torch.Generator(device=dev).manual_seed(1000 * m + rank)
+        x = torch.randn((m, 256), generator=g, device=dev).bfloat16()
+        w = (torch.randn((4096, 256), generator=g, device=dev) / 16).bfloat16()
+        y0 = (torch.arange(m * 4096, device=dev, dtype=torch.float32).reshape(m, 4096) % 7 - 3).bfloat16()
+        part = linear(x, w, "store_f32", ws_key="tp_selfcheck")
+        torch.cuda.synchronize(dev)
+        parts = [pr.cpu() for pr in all_gather(part)]
+        acc = torch.zeros_like(parts[0])
+        for pr in parts:  # rank order, one fp32 add at a time
+            acc = acc + pr
+        want = (y0.float().cpu() + acc.bfloat16().float()).bfloat16()
+        for form, tag in ((SSD_ALLREDUCE_AUTO, "auto"), (SSD_ALLREDUCE_ALL_TO_ALL, "all_to_all"),
+                          (SSD_ALLREDUCE_OWNER, "owner")):
+            comm.set_allreduce_form(form)
+            got = linear_allreduce(x, w, y0.clone(), comm, ws_key="tp_selfcheck")
+            torch.cuda.synchronize(dev)
+            exact[f"{tag}_m{m}"] = bool(torch.equal(got.cpu(), want))
+    comm.set_allreduce_form(SSD_ALLREDUCE_AUTO)
+    out["allreduce_exact"] = exact
+    ok = ok and all(exact.values())
     t = shard_weights(GemmaWeights.random(PRESETS["tp-target"], seed=41, device=dev, max_pos=512), rank, world)
     d = shard_weights(GemmaWeights.random(PRESETS["tp-draft"], seed=42, device=dev, max_pos=512), rank, world)
     prompt = list(range(50, 90))

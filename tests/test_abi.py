@@ -89,3 +89,28 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     with pytest.raises(_lib.SSDError):
         _lib.lib()
     monkeypatch.setattr(_lib, "_LIB", None)
+
+
+def test_ctypes_structs_match_the_header(tmp_path):
+    """The ctypes mirrors of the header's structs have the C compiler's size and field offsets."""
+    from ssd_b200 import _lib
+
+    structs = {"ssd_comm": _lib.CommC, "ssd_gemma_weights": _lib.GemmaWeightsC, "ssd_gemma_batch": _lib.GemmaBatchC}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-o", str(exe), str(src)], check=True, capture_output=True)
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        cname, field, value = line.split()
+        got[(cname, field)] = int(value)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)

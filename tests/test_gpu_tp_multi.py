@@ -2,8 +2,9 @@
 
 Runs ``tests/tp_worker.py`` under torch.distributed.run; each rank compares its
 sharded forward with the unsharded forward of the same weights on its GPU
-(bf16 tolerance), all ranks must hold bit-identical logits, and greedy SD on the
-sharded pair must reproduce sharded AR.
+(bf16 tolerance), all ranks must hold bit-identical logits, greedy SD on the
+sharded pair must reproduce sharded AR, and the fused all-reduce must equal the
+rank-order sum of the ranks' partials bit for bit (5, 40 and 224 rows).
 """
 
 from __future__ import annotations
@@ -48,5 +49,6 @@ def test_tensor_parallel_ranks(world, tmp_path):
             assert e["ranks_identical"], (o["rank"], name)
             assert e["max_diff"] <= 2e-2 * max(e["scale"], 1.0), (o["rank"], name, e)
         assert o["sd_equals_ar"] and o["self_sd_equals_ar"], o
+        assert all(o["allreduce_exact"].values()), (o["rank"], o["allreduce_exact"])
         assert o["ar"] == res[0]["ar"]
         assert o["self_sd_steps"] < 32

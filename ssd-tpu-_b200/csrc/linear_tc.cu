@@ -298,10 +298,10 @@ struct Cfg {
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE + BAR_BYTES;
   // Epilogue warps per TMEM lane quadrant.  The epilogue issues a few dozen dependent
   // instructions per output element; with one warp per scheduler nothing hides their
-  // latency, so tiles of 64 or more token rows get two warps per quadrant (warps w and
-  // w + 4 read the same TMEM lanes and take alternate 16-row chunks).  At most 32 rows
-  // stay at one: their CTAs are sized to share an SM with the next kernel's.
-  static constexpr int REP = MP >= 64 ? 2 : 1;
+  // latency, so tiles of more than 16 token rows get two warps per quadrant (warps w and
+  // w + 4 read the same TMEM lanes and take alternate 16-row chunks).  Up to 16 rows (one
+  // chunk) stay at one: their CTAs are sized for two per SM, next to the next kernel's.
+  static constexpr int REP = MP >= 32 ? 2 : 1;
   static constexpr int EPI = 128 * REP;  // epilogue threads
   static constexpr int THREADS = 64 + EPI;
 };

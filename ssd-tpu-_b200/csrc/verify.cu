@@ -181,6 +181,17 @@ struct SampleDecision {
 __device__ __forceinline__ float div_temp(float x, float temp) {
   return temp == 1.f ? x : __fdiv_rn(x, temp);
 }
+// The same for the per-element loops, with T = 1 known at compile time: a run-time
+// test is compiled as a select that evaluates the division for every element anyway.
+template <bool UNIT_T>
+__device__ __forceinline__ float div_t(float x, float temp) {
+  if constexpr (UNIT_T) {
+    (void)temp;
+    return x;
+  } else {
+    return __fdiv_rn(x, temp);
+  }
+}
 __device__ __forceinline__ float prob_of(float logit, float temp, float m, float s) {
   return __fdiv_rn(expf(__fsub_rn(div_temp(logit, temp), m)), s);
 }
@@ -188,7 +199,10 @@ __device__ __forceinline__ float prob_of(float logit, float temp, float m, float
 // Pass 1: per-row (max, sum exp) of x/T for the rows the acceptance test reads,
 // then (last CTA per sequence) the accept loop.  Rows per sequence: nP target
 // rows (lp[off .. K]) followed by K draft rows (lq[0 .. K-1]).
-__global__ void __launch_bounds__(kScanThreads)
+// At T = 1 the pass fits 32 registers, so its 2 x 592 CTAs are resident in one wave
+// (8 per SM); a general temperature keeps the compiler's choice.
+template <bool UNIT_T>
+__global__ void __launch_bounds__(kScanThreads, UNIT_T ? 8 : 1)
 sample_stats_kernel(const float* lp, const float* lq, int K, int V,
                     int off, int nchunks, bool vec_ok, float tp, float tq,
                     unsigned int* counters, float2* part,
@@ -206,16 +220,19 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   const float temp = is_p ? tp : tq;
   int lo, hi;
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
-  // One pass, online per thread: (m, s) with s = sum exp(v - m), v = x / T.
+  // One pass, online per thread: (m, s) with s = sum exp(v - m), v = x / T.  The terms
+  // use the __expf intrinsic (a few ulp; this pass is bound by instruction issue): s
+  // is a sum of 10^5 terms whose order already differs from the oracle's, and the
+  // accept test divides by it with an exact expf of its own 2K logits.
   // Sixteen loaded values at a time: their max moves m once (one rescale), then
   // each value adds exp(v - m) in four partial sums, without a branch per value.
   // A NaN logit is skipped (fmaxf ignores it, the select drops it) and a masked
   // (-inf) logit adds exp(-inf) = 0.
   float m = -INFINITY, s = 0.f;
   auto push = [&](float x) {
-    const float v = div_temp(x, temp);
+    const float v = div_t<UNIT_T>(x, temp);
     if (v > m) { s = (m == -INFINITY ? 0.f : s * expf(__fsub_rn(m, v))) + 1.f; m = v; }
-    else if (v > -INFINITY) s += expf(__fsub_rn(v, m));
+    else if (v > -INFINITY) s += __expf(__fsub_rn(v, m));
   };
   if (vec_ok) {
     const int nv = (hi - lo) >> 2;
@@ -232,7 +249,7 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
       float lm = -INFINITY;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        v[e] = div_temp(v[e], temp);
+        v[e] = div_t<UNIT_T>(v[e], temp);
         lm = fmaxf(lm, v[e]);
       }
       if (lm > m) {
@@ -243,7 +260,7 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
         float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float ex = expf(__fsub_rn(v[e], m));
+          const float ex = __expf(__fsub_rn(v[e], m));
           ps[e & 3] += (v[e] > -INFINITY) ? ex : 0.f;
         }
         s += (ps[0] + ps[1]) + (ps[2] + ps[3]);
@@ -320,7 +337,9 @@ sample_stats_kernel(const float* lp, const float* lq, int K, int V,
   dec[b] = d;
 }
 
-// Pass 2: residual mass sum_v max(p_v - x q_v, 0) (skipped for bonus rows).
+// Pass 2: residual mass sum_v max(p_v - x q_v, 0) (skipped for bonus rows), with
+// p_v = e_v * (1 / s) where the oracle divides by s (the draw uses the same products).
+template <bool UNIT_T>
 __global__ void __launch_bounds__(kScanThreads)
 sample_residual_kernel(const float* lp, const float* lq, int K, int V,
                        int nchunks, bool vec_ok, float tp, float tq, float sx, unsigned int* counters,
@@ -337,9 +356,11 @@ sample_residual_kernel(const float* lp, const float* lq, int K, int V,
   int lo, hi;
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
   float s = 0.f;
+  // one reciprocal per row instead of a division per element (as in the draw pass)
+  const float inv_sp = __frcp_rn(d.sp), inv_sq = __frcp_rn(d.sq);
   auto add = [&](float xp, float xq) {
-    const float p = prob_of(xp, tp, d.mp, d.sp);
-    const float q = prob_of(xq, tq, d.mq, d.sq);
+    const float p = __fmul_rn(__expf(__fsub_rn(div_t<UNIT_T>(xp, tp), d.mp)), inv_sp);
+    const float q = __fmul_rn(__expf(__fsub_rn(div_t<UNIT_T>(xq, tq), d.mq)), inv_sq);
     s += fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f);
   };
   int j0 = lo;
@@ -373,6 +394,17 @@ sample_residual_kernel(const float* lp, const float* lq, int K, int V,
 }
 
 // Pass 3: Gumbel-max categorical draw over log(r + 1e-12).
+// The score of element j is log(r_j + 1e-12) + g_j with g_j = -log(-log u_j), the
+// oracle's fp32 expression.  It is increasing in (r_j + 1e-12) / nl_j, nl_j = -log u_j,
+// so a thread picks its best element by that ratio (compared by cross-multiplication:
+// no division and one log per element) and evaluates the exact score for its best
+// element only; threads and CTAs then compare exact scores.  The uniforms are an input
+// of the call, not of the earlier passes: each thread takes -log u of its first 16
+// elements before waiting for them.  r_j uses one reciprocal per row where the oracle
+// divides (p = e / s, r = residual / sum): the choice can differ from the oracle's
+// only where two scores agree to about the rounding of those products (a near-tie).
+constexpr int kDrawPre = 4;  // float4 groups of uniforms a thread prepares before the wait
+template <bool UNIT_T>
 __global__ void __launch_bounds__(kScanThreads)
 sample_draw_kernel(const float* lp, const float* lq,
                    const float* u_gumbel, int K, int V, int nchunks, bool vec_ok, float tp, float tq,
@@ -381,66 +413,83 @@ sample_draw_kernel(const float* lp, const float* lq,
                    int32_t* recovery, uint8_t* mask) {
   __shared__ unsigned long long red[32];
   __shared__ bool is_last;
-  pdl_wait();
   const int b = blockIdx.y;
-  const SampleDecision d = dec[b];
-  const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
-  const float* qrow = lq + ((int64_t)b * K + d.qrow) * V;
   const float* urow = u_gumbel + (int64_t)b * V;
   int lo, hi;
   chunk_bounds(V, nchunks, blockIdx.x, lo, hi);
-  float best = -INFINITY;
+  const int nv = vec_ok ? (hi - lo) >> 2 : 0;
+  const float4* uu = reinterpret_cast<const float4*>(urow + lo);
+  float4 nlp[kDrawPre];  // -log u of this thread's first kDrawPre float4 groups
+#pragma unroll
+  for (int t = 0; t < kDrawPre; ++t) {
+    const int i = threadIdx.x + t * kScanThreads;
+    if (i < nv) {
+      const float4 u = __ldcg(uu + i);
+      nlp[t] = make_float4(-logf(u.x), -logf(u.y), -logf(u.z), -logf(u.w));
+    }
+  }
+  pdl_wait();
+  const SampleDecision d = dec[b];
+  const float* prow = lp + ((int64_t)b * (K + 1) + d.prow) * V;
+  const float* qrow = lq + ((int64_t)b * K + d.qrow) * V;
+  const float inv_sp = __frcp_rn(d.sp), inv_sq = d.bonus ? 0.f : __frcp_rn(d.sq);
+  const float inv_r = d.bonus ? 1.f : __frcp_rn(d.rsum);
+  // best so far as the pair (num, nl): num = r + 1e-12 > 0, nl = -log u >= 0
+  float bnum = 0.f, bnl = 1.f;
   int bidx = 0x7fffffff;
-  // element j with its target logit xp, draft logit xq (unused for a bonus draw), uniform u;
+  // element j with its target logit xp, draft logit xq (unused for a bonus draw) and nl;
   // a thread visits its elements in increasing j, so ties keep the first index
-  auto visit = [&](int j, float xp, float xq, float u) {
-    const float p = prob_of(xp, tp, d.mp, d.sp);
+  auto visit = [&](int j, float xp, float xq, float nl) {
+    const float p = __fmul_rn(__expf(__fsub_rn(div_t<UNIT_T>(xp, tp), d.mp)), inv_sp);
     float r;
     if (d.bonus) {
       r = p;
     } else {
-      const float q = prob_of(xq, tq, d.mq, d.sq);
-      r = __fdiv_rn(fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f), d.rsum);
+      const float q = __fmul_rn(__expf(__fsub_rn(div_t<UNIT_T>(xq, tq), d.mq)), inv_sq);
+      r = __fmul_rn(fmaxf(__fsub_rn(p, __fmul_rn(sx, q)), 0.f), inv_r);
     }
-    const float g = -logf(-logf(u));
-    const float score = __fadd_rn(logf(__fadd_rn(r, 1e-12f)), g);
-    if (score > best) { best = score; bidx = j; }
+    const float num = __fadd_rn(r, 1e-12f);
+    // a candidate has a score above -inf that is not NaN: num not NaN, nl < inf (u > 0);
+    // the first candidate is taken, a later one where num / nl > bnum / bnl, i.e.
+    // num * bnl > bnum * nl (both sides finite: num <= 1 + 1e-12, nl < inf; nl = 0,
+    // u = 1, is the oracle's +inf score, and the first of those stays)
+    if (!(num == num) || !(nl < INFINITY)) return;
+    if (bidx == 0x7fffffff || __fmul_rn(num, bnl) > __fmul_rn(bnum, nl)) {
+      bnum = num;
+      bnl = nl;
+      bidx = j;
+    }
   };
   int j0 = lo;
   if (vec_ok) {
-    const int nv = (hi - lo) >> 2;
     const float4* pp = reinterpret_cast<const float4*>(prow + lo);
     const float4* qq = reinterpret_cast<const float4*>(qrow + lo);
-    const float4* uu = reinterpret_cast<const float4*>(urow + lo);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    int i = threadIdx.x;
-    // two float4 of each of the three rows (six 16-byte loads) in flight per thread
-    for (; i + kScanThreads < nv; i += 2 * kScanThreads) {
-      float4 a[2], c[2], u[2];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        a[e] = __ldcg(pp + i + e * kScanThreads);
-        c[e] = d.bonus ? zero : __ldcg(qq + i + e * kScanThreads);
-        u[e] = __ldcg(uu + i + e * kScanThreads);
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int j = lo + 4 * (i + e * kScanThreads);
-        visit(j, a[e].x, c[e].x, u[e].x); visit(j + 1, a[e].y, c[e].y, u[e].y);
-        visit(j + 2, a[e].z, c[e].z, u[e].z); visit(j + 3, a[e].w, c[e].w, u[e].w);
+    for (int t = 0; t < kDrawPre; ++t) {
+      const int i = threadIdx.x + t * kScanThreads;
+      if (i < nv) {
+        const float4 a = __ldcg(pp + i);
+        const float4 c = d.bonus ? zero : __ldcg(qq + i);
+        const int j = lo + 4 * i;
+        visit(j, a.x, c.x, nlp[t].x); visit(j + 1, a.y, c.y, nlp[t].y);
+        visit(j + 2, a.z, c.z, nlp[t].z); visit(j + 3, a.w, c.w, nlp[t].w);
       }
     }
-    for (; i < nv; i += kScanThreads) {
+    for (int i = threadIdx.x + kDrawPre * kScanThreads; i < nv; i += kScanThreads) {
       const float4 a = __ldcg(pp + i);
       const float4 c = d.bonus ? zero : __ldcg(qq + i);
       const float4 u = __ldcg(uu + i);
       const int j = lo + 4 * i;
-      visit(j, a.x, c.x, u.x); visit(j + 1, a.y, c.y, u.y); visit(j + 2, a.z, c.z, u.z); visit(j + 3, a.w, c.w, u.w);
+      visit(j, a.x, c.x, -logf(u.x)); visit(j + 1, a.y, c.y, -logf(u.y));
+      visit(j + 2, a.z, c.z, -logf(u.z)); visit(j + 3, a.w, c.w, -logf(u.w));
     }
     j0 = lo + 4 * nv;
   }
   for (int j = j0 + threadIdx.x; j < hi; j += kScanThreads)
-    visit(j, __ldcg(prow + j), d.bonus ? 0.f : __ldcg(qrow + j), __ldcg(urow + j));
+    visit(j, __ldcg(prow + j), d.bonus ? 0.f : __ldcg(qrow + j), -logf(__ldcg(urow + j)));
+  // the exact score of this thread's best element: log(r + 1e-12) + (-log(-log u))
+  const float best = bidx == 0x7fffffff ? -INFINITY : __fadd_rn(logf(bnum), -logf(bnl));
   unsigned long long key = block_reduce(thread_key(best, bidx), red, OpMax());
   if (threadIdx.x == 0) part[(int64_t)b * nchunks + blockIdx.x] = key;
   pdl_trigger();
@@ -905,16 +954,18 @@ extern "C" int ssd_verify_sample(ssd_stream_t stream, const float* logits_p, con
   cudaStream_t st = (cudaStream_t)stream;
   const bool vec_ok = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits_p) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(logits_q) & 15) == 0);
-  SSD_PDL(sample_stats_kernel, dim3(nch, rows), kScanThreads, 0, st, logits_p, logits_q, K, V, off, nch, vec_ok,
-                                                                temperature_p, temperature_q, c0, part,
-                                                                speculations, u_accept, dec);
+  const bool unit = temperature_p == 1.f && temperature_q == 1.f;
+  SSD_PDL(unit ? sample_stats_kernel<true> : sample_stats_kernel<false>, dim3(nch, rows), kScanThreads, 0, st,
+          logits_p, logits_q, K, V, off, nch, vec_ok, temperature_p, temperature_q, c0, part, speculations,
+          u_accept, dec);
   SSD_CHECK_LAUNCH();
   const int nch_b = scan_chunks(B, V);
   const bool vec_b = vec_ok && ((reinterpret_cast<uintptr_t>(u_gumbel) & 15) == 0);
-  SSD_PDL(sample_residual_kernel, dim3(nch_b, B), kScanThreads, 0, st, logits_p, logits_q, K, V, nch_b, vec_ok,
+  SSD_PDL(unit ? sample_residual_kernel<true> : sample_residual_kernel<false>, dim3(nch_b, B), kScanThreads, 0, st,
+          logits_p, logits_q, K, V, nch_b, vec_ok,
           temperature_p, temperature_q, sampler_x, c1, reinterpret_cast<float*>(part), dec);
   SSD_CHECK_LAUNCH();
-  SSD_PDL(sample_draw_kernel, dim3(nch_b, B), kScanThreads, 0, st, 
+  SSD_PDL(unit ? sample_draw_kernel<true> : sample_draw_kernel<false>, dim3(nch_b, B), kScanThreads, 0, st,
       logits_p, logits_q, u_gumbel, K, V, nch_b, vec_b, temperature_p, temperature_q, sampler_x, c2,
       reinterpret_cast<unsigned long long*>(part), dec, accept_until, recovery, accepted_mask);
   SSD_CHECK_LAUNCH();

@@ -84,6 +84,8 @@ class GemmaAdapter:
         self._lg_rows = max(self.chunk, max_tokens, 1 + self.max_branches)
         self._lg_heap = comm.alloc((self._lg_rows, s.vocab), torch.float32) if comm is not None else None
         self._lg1 = self._logits(1)
+        self._h_scal = self._d_scal = self._d_tok = None  # draft_speculate's scalars and tokens
+        self._scal_ev: torch.cuda.Event | None = None
 
     def _logits(self, rows: int) -> torch.Tensor:
         """A [rows, V] fp32 buffer the forward may write its logits into."""
@@ -177,8 +179,10 @@ class GemmaAdapter:
                 break
             common += 1
         common = min(common, len(prefix) - 1)  # always feed at least one token
-        self._truncate(common)
         rows = k + 1 if with_bonus else k
+        if 1 <= rows and len(prefix) - common <= self.chunk and self.comm is None:
+            return self._draft_chained(prefix, common, k, rows)
+        self._truncate(common)
         logits = torch.empty((rows, self.vocab_size), dtype=torch.float32, device=self.dev)
         feed = prefix[common:]
         spec: list[int] = []
@@ -191,6 +195,54 @@ class GemmaAdapter:
             argmax_rows(lg, nxt)
             spec.append(int(nxt.item()))
             feed = [spec[-1]]
+        return spec, logits
+
+    def _draft_chained(self, prefix: list[int], common: int, k: int, rows: int) -> tuple[list[int], torch.Tensor]:
+        """``draft_speculate`` for a feed of at most one chunk, with the same forwards, tokens and
+        positions, but each draft token goes from its argmax straight into the next forward on the
+        device: the call's scalars (rollback, page allocation, positions, feed tokens) reach the
+        device in one copy from pinned memory and the k tokens come back in one copy, instead of a
+        few blocking copies per token."""
+        feed = prefix[common:]
+        f = len(feed)
+        if common + f + rows - 1 > self.max_model_len:
+            raise ValueError("sequence exceeds max_model_len")
+        # [truncate-to, 0, tokens before the feed, tokens to allocate, positions of forwards 1.., feed]
+        vals = [common, 0, common, f + rows - 1] + [common + f + i - 1 for i in range(1, rows)] + feed
+        n = len(vals)
+        if self._scal_ev is not None:
+            self._scal_ev.synchronize()  # the previous call's upload has left the pinned buffer
+        if self._h_scal is None or self._h_scal.numel() < n:
+            self._h_scal = torch.empty(max(256, n), dtype=torch.int32, pin_memory=True)
+            self._d_scal = torch.empty(max(256, n), dtype=torch.int32, device=self.dev)
+            self._d_tok = torch.empty(max(256, n), dtype=torch.int32, device=self.dev)
+            self._scal_ev = torch.cuda.Event()
+        self._h_scal[:n] = torch.tensor(vals, dtype=torch.int32)
+        d = self._d_scal
+        d[:n].copy_(self._h_scal[:n], non_blocking=True)
+        self._scal_ev.record()
+        if common < len(self.cached) or self.pending:
+            self.pm.rollback_rows(0, 1, d[0:1], d[1:2])
+        self.cached = self.cached[:common]
+        self.pending = []
+        self.pm.allocate_rows(0, 1, d[2:3], d[3:4], None)
+        logits = torch.empty((rows, self.vocab_size), dtype=torch.float32, device=self.dev)
+        toks = self._d_tok
+        lg = self._lg1
+        pos0 = 4 + rows - 1
+        self.runner.forward(d[pos0:pos0 + f].view(1, f), d[2:3], self.cache.pages, self.pm.tables, lg,
+                            last_only=True)
+        logits[0].copy_(lg[0])
+        if k > 0:
+            argmax_rows(lg, toks[0:1])
+        for i in range(1, rows):
+            self.runner.forward(toks[i - 1:i].view(1, 1), d[4 + i - 1:4 + i], self.cache.pages, self.pm.tables, lg,
+                                last_only=True)
+            logits[i].copy_(lg[0])
+            if i < k:
+                argmax_rows(lg, toks[i:i + 1])
+        spec = [int(t) for t in toks[:k].cpu().tolist()] if k > 0 else []
+        self.cached = prefix[:common] + feed + spec[:rows - 1]
         return spec, logits
 
     def draft_branches(self, prefix_tokens: list[int], feeds: list[list[int]], k: int,

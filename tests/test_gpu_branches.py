@@ -75,3 +75,59 @@ def test_draft_branches_equal_one_by_one(cuda, preset):
     # the trunk row and the page pool are intact afterwards: the next call reuses the prefix
     assert a.cached == prefix
     assert a.draft_branches(prefix, feeds[:2], k) == want[:2]
+
+
+@pytest.mark.parametrize("preset", ["toy-draft", "tp-draft"])
+def test_draft_speculate_chained_equals_token_by_token(cuda, preset):
+    """``draft_speculate`` (draft tokens chained on the device, one upload and one download per
+    call) gives the tokens, logits, cache contents and page tables of the token-by-token loop
+    (truncate, then one forward and one host-side argmax per token) over a sequence of calls that
+    extend the prefix, roll it back, and ask for the bonus row."""
+    from ssd_b200.algorithm.verify import argmax_rows
+    from ssd_b200.models.gemma import PRESETS, GemmaWeights
+    from ssd_b200.models.gemma_adapter import GemmaAdapter
+
+    dt = torch.float32 if preset.startswith("toy") else torch.bfloat16
+    w = GemmaWeights.random(PRESETS[preset], seed=78, dtype=dt, device=cuda, max_pos=512)
+    fast = GemmaAdapter(w, max_model_len=256, name="draft")
+    slow = GemmaAdapter(w, max_model_len=256, name="draft")
+
+    def token_by_token(a, prefix, k, with_bonus):
+        common = 0
+        for x, y in zip(a.cached, prefix):
+            if x != y:
+                break
+            common += 1
+        common = min(common, len(prefix) - 1)
+        a._truncate(common)
+        rows = k + 1 if with_bonus else k
+        logits = torch.empty((rows, a.vocab_size), dtype=torch.float32, device=cuda)
+        feed, spec = prefix[common:], []
+        nxt = torch.empty(1, dtype=torch.int32, device=cuda)
+        for i in range(rows):
+            lg = a._run(feed, a._lg1, last_only=True)
+            logits[i].copy_(lg[0])
+            if i == k:
+                break
+            argmax_rows(lg, nxt)
+            spec.append(int(nxt.item()))
+            feed = [spec[-1]]
+        return spec, logits
+
+    rng = np.random.default_rng(9)
+    prefix = [int(x) for x in rng.integers(0, w.shape.vocab, 70)]
+    calls = []
+    for step in range(6):
+        k = 4 if step != 3 else 0
+        calls.append((list(prefix), k, step % 2 == 0 or k == 0))
+        prefix = prefix + [int(x) for x in rng.integers(0, w.shape.vocab, 1 + step % 2)]
+        if step == 4:
+            prefix = prefix[:60] + [int(x) for x in rng.integers(0, w.shape.vocab, 3)]  # a rollback
+    for prefix, k, bonus in calls:
+        got, lg_got = fast.draft_speculate(prefix, k, with_bonus=bonus)
+        want, lg_want = token_by_token(slow, prefix, k, bonus)
+        assert got == want
+        assert torch.equal(lg_got, lg_want)
+        assert fast.cached == slow.cached
+        torch.cuda.synchronize()
+        assert torch.equal(fast.pm.tables, slow.pm.tables) and torch.equal(fast.pm.lens, slow.pm.lens)

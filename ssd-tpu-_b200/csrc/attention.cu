@@ -608,8 +608,14 @@ paged_attention_tc_kernel(const bf16* q, const bf16* pages, int num_layers,
 // Rows of a page past the end of the context are zeroed in the stage before
 // P.V (masked probabilities are exact zeros, stale rows must not be NaN).
 // At D = 256: 128 threads and ~106 KB of shared memory, two CTAs per SM, up
-// to 12 pages (192 KB) of K/V in flight per SM.  Batch invariance as for the other
-// kernels: splits, page ownership and every reduction order are fixed.
+// to 12 pages (192 KB) of K/V in flight per SM.  Models with at most two KV heads
+// (a GQA draft, a tensor-parallel shard) launch only one or two CTAs per sequence
+// at decode contexts, so each CTA's consumers walk their pages one after another:
+// they get 6 consumers and 12 stages instead (224 threads, ~203 KB, one CTA per
+// SM), which halves the pages per consumer.  The consumer count is a property of
+// the model's shape, never of the batch or the query count, so batch invariance
+// holds as for the other kernels: splits, page ownership and every reduction
+// order are fixed.
 constexpr int kTmaChunk = 256;                  // positions per split
 constexpr int kTmaPage = 16;                    // rows per page (TMA box height)
 // consumer warps per CTA for head size D; the stage count is a multiple of it
@@ -617,9 +623,10 @@ template <int D>
 constexpr int tma_consumers() {
   return D == 256 ? 3 : 4;
 }
-template <int D>
+constexpr int kTmaWideConsumers = 6;  // D = 256, at most two KV heads
+template <int D, int C>
 constexpr int tma_threads() {
-  return 32 * (1 + tma_consumers<D>());
+  return 32 * (1 + C);
 }
 constexpr uint32_t kTmaWaitLimit = 1u << 24;
 
@@ -658,13 +665,13 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-template <int D>
+template <int D, int C>
 struct TmaSmem {
-  static constexpr int CONS = tma_consumers<D>();
+  static constexpr int CONS = C;
   static constexpr int CHUNKS = D / 64;                          // 128-byte swizzle rows per page row
   static constexpr uint32_t PLANE = kTmaPage * D * 2;            // K (or V) of one page: 16 x D bf16
   static constexpr uint32_t STAGE = 2 * PLANE;
-  static constexpr int STAGES = D == 256 ? 6 : D == 128 ? 12 : 16;
+  static constexpr int STAGES = D == 256 ? 2 * C : D == 128 ? 12 : 16;
   static_assert(STAGES % CONS == 0, "every stage must belong to one consumer (mbarrier parity)");
   static constexpr int QST = D + 8;                              // padded Q rows (ldmatrix conflict-free)
   static constexpr size_t ring = (size_t)STAGES * STAGE;
@@ -683,17 +690,17 @@ __device__ __forceinline__ uint32_t sw_off(int row, int dim) {
   return (uint32_t)(c * (kTmaPage * 128) + row * 128 + ((u ^ (row & 7)) << 4));
 }
 
-template <int D>
-__global__ void __launch_bounds__(tma_threads<D>(), 2)
+template <int D, int C>
+__global__ void __launch_bounds__(tma_threads<D, C>(), C > 4 ? 1 : 2)
 paged_attention_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const bf16* q, int num_layers, int num_blocks,
                            int hkv, int layer, const int32_t* block_tables, int max_blocks, const int32_t* seq_lens,
                            const int32_t* q_lens, bf16* out, float scale, int T, int hq, int row_groups, int nsplit,
                            float* ws_o, float2* ws_ml, unsigned int* counters, unsigned int* err, int early) {
-  using S = TmaSmem<D>;
+  using S = TmaSmem<D, C>;
   constexpr int KSTEPS = D / 16;
   constexpr int NT = D / 8;
   constexpr int NCONS = S::CONS;
-  constexpr int NTHREADS = tma_threads<D>();
+  constexpr int NTHREADS = tma_threads<D, C>();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1095,15 +1102,15 @@ bool kv_map_cached(CUtensorMap* out, const void* pages, int plane_pages, int hkv
   return true;
 }
 
-template <int D>
+template <int D, int C>
 int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int num_layers, int num_blocks, int hkv,
                          int layer, const int32_t* tables, int max_blocks, const int32_t* seq_lens,
                          const int32_t* q_lens, void* out, float scale, int B, int T, int hq, int max_seq_len,
                          const AttnLayout& L, void* ws, int early) {
-  using S = TmaSmem<D>;
+  using S = TmaSmem<D, C>;
   CUtensorMap map;
   if (!kv_map_cached(&map, pages, 2 * num_layers * num_blocks, hkv, D)) return SSD_ERR_LAUNCH;
-  auto kern = paged_attention_tma_kernel<D>;
+  auto kern = paged_attention_tma_kernel<D, C>;
   {
     // the shared-memory attribute belongs to each device's context: set it once per device
     static std::mutex mu;
@@ -1122,7 +1129,8 @@ int launch_attention_tma(cudaStream_t st, const void* q, const void* pages, int 
   char* w = reinterpret_cast<char*>(ws);
   const int nsplit = (max_seq_len + kTmaChunk - 1) / kTmaChunk;  // <= L.nsplit: fits the workspace
   dim3 grid(nsplit, hkv * L.row_groups, B);
-  SSD_PDL(kern, grid, tma_threads<D>(), S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
+  constexpr int threads = tma_threads<D, C>();
+  SSD_PDL(kern, grid, threads, S::total, st, map, reinterpret_cast<const bf16*>(q), num_layers, num_blocks, hkv,
           layer, tables, max_blocks, seq_lens, q_lens, reinterpret_cast<bf16*>(out), scale, T, hq, L.row_groups,
           nsplit, reinterpret_cast<float*>(w + L.off_o), reinterpret_cast<float2*>(w + L.off_ml),
           reinterpret_cast<unsigned int*>(w + L.off_cnt), reinterpret_cast<unsigned int*>(w + kCounterBytes), early);
@@ -1199,16 +1207,19 @@ int ssd::paged_verify_attention_impl(ssd_stream_t stream, const void* q, const v
                                  block_tables, max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, L,  \
                                  workspace)
   const bool aligned16 = !(reinterpret_cast<uintptr_t>(q) & 15) && !(reinterpret_cast<uintptr_t>(pages) & 15);
-#define SSD_ATTN_TMA(DD)                                                                                        \
-  return launch_attention_tma<DD>(st, q, pages, num_layers, num_blocks, num_kv_heads, layer, block_tables,      \
-                                  max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, max_seq_len, L,    \
-                                  workspace, early)
+#define SSD_ATTN_TMA_C(DD, CC)                                                                                  \
+  return launch_attention_tma<DD, CC>(st, q, pages, num_layers, num_blocks, num_kv_heads, layer, block_tables,  \
+                                      max_blocks, seq_lens, q_lens, out, scale, B, T, num_heads, max_seq_len, L, \
+                                      workspace, early)
+#define SSD_ATTN_TMA(DD) SSD_ATTN_TMA_C(DD, tma_consumers<DD>())
   if (dtype == SSD_DTYPE_BF16 && aligned16 && block_size == kTmaPage && (int64_t)2 * num_layers * num_blocks < (1ll << 31)) {
+    if (head_dim == 256 && num_kv_heads <= 2) SSD_ATTN_TMA_C(256, kTmaWideConsumers);
     if (head_dim == 256) SSD_ATTN_TMA(256);
     if (head_dim == 128) SSD_ATTN_TMA(128);
     if (head_dim == 64) SSD_ATTN_TMA(64);
   }
 #undef SSD_ATTN_TMA
+#undef SSD_ATTN_TMA_C
   if (dtype == SSD_DTYPE_BF16 && aligned16) {
     if (head_dim == 256) SSD_ATTN_TC(256);
     if (head_dim == 128) SSD_ATTN_TC(128);

@@ -46,6 +46,7 @@ def _setup(b, t, hq, hkv, d, bs, ctx, dtype_name, seed, table_cols=None):
     ("bf16", 16, 16, 256, 5, 16, 8, 512, 4096, 2e-2),   # op config 2a (Gemma-7B verify attention)
     ("bf16", 8, 1, 256, 1, 16, 3, 1, 700, 2e-2),       # Gemma-2B draft decode (MQA)
     ("bf16", 8, 1, 256, 3, 16, 2, 40, 300, 2e-2),      # G*T = 24 rows -> two row groups
+    ("bf16", 2, 2, 256, 5, 16, 4, 300, 2000, 2e-2),    # Gemma-7B shard at 8 ranks (6-consumer variant)
     ("f32", 4, 1, 64, 5, 16, 4, 5, 200, 1e-5),         # toy pair, fp32
     ("f32", 4, 2, 128, 7, 4, 3, 7, 90, 1e-5),          # small pages, k = 6
 ])

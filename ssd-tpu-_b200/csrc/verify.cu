@@ -534,6 +534,53 @@ constexpr int kTopPCap = 4096;
 constexpr double kTopPFix = 17592186044416.0;  // 2^44: V * 2^44 stays below 2^63 for V < 2^19
 static_assert(kTopPBins == 2 * kTopPThreads, "the bin scan gives every thread two bins");
 
+// ---- thread-block cluster helpers (distributed shared memory; all within one GPU)
+__device__ __forceinline__ uint32_t tp_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every thread of every CTA of the cluster: a hardware barrier, ordering shared-memory
+// writes before it (release) with reads after it (acquire) across the cluster
+__device__ __forceinline__ void tp_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+template <typename T>
+__device__ __forceinline__ uint32_t tp_mapa(const T* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ unsigned long long tp_ld_u64(uint32_t a) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ double tp_ld_f64(uint32_t a) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float tp_ld_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ int tp_ld_s32(uint32_t a) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+
+// CL CTAs per row (a thread-block cluster when CL > 1): CTA r of the cluster streams
+// the r-th contiguous part of the row.  The row max and the fp64 mass below the
+// binned range are combined over the cluster in CTA order, every CTA sums the
+// cluster's integer bin masses for its scan (exact, so each CTA finds the same
+// cutoff bin), the first CTA gathers the cutoff bin's candidates from the others,
+// sorts and walks them, and every CTA masks its part with the cutoff it publishes.
+// With few rows (the draft rows of a batched decode) one CTA per row leaves most
+// SMs idle; CL = 4 gives each row four.
+template <int CL>
 __global__ void __launch_bounds__(kTopPThreads)
 top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
   __shared__ unsigned long long massq[kTopPBins];  // bin masses in units of 2^-44; later candidate masses
@@ -544,12 +591,22 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
   __shared__ int s_bin, s_ncand, s_found;
   __shared__ double s_above;
   __shared__ float s_t;
+  __shared__ float s_mx;     // CL > 1: this CTA's part of the row max
+  __shared__ double s_below; // CL > 1: this CTA's part of the mass below the binned range
   pdl_wait();
-  float* row = x + (int64_t)blockIdx.x * ld;
+  const uint32_t crank = CL > 1 ? tp_cluster_rank() : 0u;
+  float* row = x + (int64_t)(blockIdx.x / CL) * ld;
+  const int j_lo = (int)((int64_t)V * crank / CL), j_hi = (int)((int64_t)V * (crank + 1) / CL);
   float mloc = -INFINITY;
-  for (int j = threadIdx.x; j < V; j += kTopPThreads) mloc = fmaxf(mloc, __ldcg(row + j));  // fmaxf skips NaN
-  const float m = block_reduce(mloc, redf, OpMax());
-  if (!(m > -INFINITY)) {  // no finite logit: nothing to rank
+  for (int j = j_lo + threadIdx.x; j < j_hi; j += kTopPThreads) mloc = fmaxf(mloc, __ldcg(row + j));  // skips NaN
+  float m = block_reduce(mloc, redf, OpMax());
+  if constexpr (CL > 1) {
+    if (threadIdx.x == 0) s_mx = m;
+    tp_cluster_sync();
+    for (int r = 0; r < CL; ++r) m = fmaxf(m, tp_ld_f32(tp_mapa(&s_mx, (uint32_t)r)));
+    tp_cluster_sync();  // every CTA has read the others' parts (none exits before)
+  }
+  if (!(m > -INFINITY)) {  // no finite logit: nothing to rank (the same decision in every CTA)
     pdl_trigger();
     return;
   }
@@ -567,7 +624,7 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
     for (int i = threadIdx.x; i < kTopPBins; i += kTopPThreads) massq[i] = 0ull;
     __syncthreads();
     double below = 0.0;  // mass of the logits below the range (fp64, per thread)
-    for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+    for (int j = j_lo + threadIdx.x; j < j_hi; j += kTopPThreads) {
       const float v = __ldcg(row + j);
       if (!(v > -INFINITY)) continue;  // -inf and NaN carry no mass
       const double d = (md - (double)v) * inv_t;
@@ -582,7 +639,21 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
     // reaches the target -- the same test, on the same sums, as a walk down the bins.
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int b0i = 2 * threadIdx.x;
-    const unsigned long long q0 = massq[b0i], q1 = massq[b0i + 1];
+    unsigned long long q0 = massq[b0i], q1 = massq[b0i + 1];
+    if constexpr (CL > 1) {
+      // the cluster's bins (integer sums: any order, the same in every CTA) and the
+      // mass below (fp64, summed in CTA order)
+      if (threadIdx.x == 0) s_below = below;
+      tp_cluster_sync();
+      q0 = q1 = 0ull;
+      below = 0.0;
+      for (int r = 0; r < CL; ++r) {
+        q0 += tp_ld_u64(tp_mapa(&massq[b0i], (uint32_t)r));
+        q1 += tp_ld_u64(tp_mapa(&massq[b0i + 1], (uint32_t)r));
+        below += tp_ld_f64(tp_mapa(&s_below, (uint32_t)r));
+      }
+      tp_cluster_sync();  // the histograms are read before any CTA clears or reuses them
+    }
     unsigned long long incl = q0 + q1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -626,7 +697,7 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
   if (b >= 0) {
     if (threadIdx.x == 0) s_ncand = 0;
     __syncthreads();
-    for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+    for (int j = j_lo + threadIdx.x; j < j_hi; j += kTopPThreads) {
       const float v = __ldcg(row + j);
       if (!(v > -INFINITY)) continue;
       const double d = (md - (double)v) * inv_t;
@@ -636,55 +707,72 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
       }
     }
     __syncthreads();
-    const unsigned int n = (unsigned int)s_ncand;
-    if (n > (unsigned)kTopPCap) {
-      // too many logits near the cutoff to sort here: keep the whole bin
-      if (threadIdx.x == 0) s_t = (float)(md - (lo + (double)(b + 1) / scale) / inv_t);
-    } else {
-      int np2 = 1;
-      while (np2 < (int)n) np2 <<= 1;
-      for (int i = (int)n + threadIdx.x; i < np2; i += kTopPThreads) cand[i] = -INFINITY;
-      __syncthreads();
-      // bitonic sort, descending
-      for (int size = 2; size <= np2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-          for (int i = threadIdx.x; i < np2; i += kTopPThreads) {
-            const int jx = i ^ stride;
-            if (jx > i) {
-              const bool desc = (i & size) == 0;
-              const float a = cand[i], c = cand[jx];
-              if (desc ? (a < c) : (a > c)) {
-                cand[i] = c;
-                cand[jx] = a;
-              }
-            }
-          }
-          __syncthreads();
+    unsigned int n = (unsigned int)s_ncand;
+    if constexpr (CL > 1) {
+      // the first CTA appends the others' candidates (their order does not matter: sorted next)
+      tp_cluster_sync();
+      if (crank == 0) {
+        unsigned int off = min(n, (unsigned int)kTopPCap);
+        for (int r = 1; r < CL; ++r) {
+          const unsigned int nr = (unsigned int)tp_ld_s32(tp_mapa(&s_ncand, (uint32_t)r));
+          for (unsigned int i = threadIdx.x; i < nr && off + i < (unsigned)kTopPCap; i += kTopPThreads)
+            cand[off + i] = tp_ld_f32(tp_mapa(&cand[i], (uint32_t)r));
+          n += nr;
+          off = min(off + nr, (unsigned int)kTopPCap);
         }
       }
-      // Walk down the sorted candidates until the running mass reaches the target: the masses
-      // are computed by all threads (kTopPBins at a time, into the histogram's storage), the
-      // running sum stays one thread's sequential fp64 sum, in candidate order.
-      double* wv = reinterpret_cast<double*>(massq);
-      double cum = above;  // thread 0's running mass
-      if (threadIdx.x == 0) {
-        s_found = 0;
-        s_t = n > 0 ? cand[n - 1] : -INFINITY;
-      }
-      for (unsigned int base = 0; base < n; base += kTopPBins) {
-        __syncthreads();  // the previous part has been walked (and s_found set)
-        if (s_found) break;
-        const unsigned int cnt = min(n - base, (unsigned int)kTopPBins);
-        for (unsigned int i = threadIdx.x; i < cnt; i += kTopPThreads)
-          wv[i] = exp(-(md - (double)cand[base + i]) * inv_t);
+      tp_cluster_sync();  // the others' candidates have been read
+    }
+    if (CL == 1 || crank == 0) {
+      if (n > (unsigned)kTopPCap) {
+        // too many logits near the cutoff to sort here: keep the whole bin
+        if (threadIdx.x == 0) s_t = (float)(md - (lo + (double)(b + 1) / scale) / inv_t);
+      } else {
+        int np2 = 1;
+        while (np2 < (int)n) np2 <<= 1;
+        for (int i = (int)n + threadIdx.x; i < np2; i += kTopPThreads) cand[i] = -INFINITY;
         __syncthreads();
+        // bitonic sort, descending
+        for (int size = 2; size <= np2; size <<= 1) {
+          for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < np2; i += kTopPThreads) {
+              const int jx = i ^ stride;
+              if (jx > i) {
+                const bool desc = (i & size) == 0;
+                const float a = cand[i], c = cand[jx];
+                if (desc ? (a < c) : (a > c)) {
+                  cand[i] = c;
+                  cand[jx] = a;
+                }
+              }
+            }
+            __syncthreads();
+          }
+        }
+        // Walk down the sorted candidates until the running mass reaches the target: the masses
+        // are computed by all threads (kTopPBins at a time, into the histogram's storage), the
+        // running sum stays one thread's sequential fp64 sum, in candidate order.
+        double* wv = reinterpret_cast<double*>(massq);
+        double cum = above;  // thread 0's running mass
         if (threadIdx.x == 0) {
-          for (unsigned int i = 0; i < cnt; ++i) {
-            cum += wv[i];
-            if (cum >= target) {
-              s_t = cand[base + i];
-              s_found = 1;
-              break;
+          s_found = 0;
+          s_t = n > 0 ? cand[n - 1] : -INFINITY;
+        }
+        for (unsigned int base = 0; base < n; base += kTopPBins) {
+          __syncthreads();  // the previous part has been walked (and s_found set)
+          if (s_found) break;
+          const unsigned int cnt = min(n - base, (unsigned int)kTopPBins);
+          for (unsigned int i = threadIdx.x; i < cnt; i += kTopPThreads)
+            wv[i] = exp(-(md - (double)cand[base + i]) * inv_t);
+          __syncthreads();
+          if (threadIdx.x == 0) {
+            for (unsigned int i = 0; i < cnt; ++i) {
+              cum += wv[i];
+              if (cum >= target) {
+                s_t = cand[base + i];
+                s_found = 1;
+                break;
+              }
             }
           }
         }
@@ -692,11 +780,16 @@ top_p_mask_kernel(float* x, int64_t ld, int V, double inv_t, double top_p) {
     }
   }
   __syncthreads();
-  const float t = s_t;
-  for (int j = threadIdx.x; j < V; j += kTopPThreads) {
+  float t = s_t;
+  if constexpr (CL > 1) {
+    tp_cluster_sync();  // the first CTA's cutoff is published
+    t = tp_ld_f32(tp_mapa(&s_t, 0u));
+  }
+  for (int j = j_lo + threadIdx.x; j < j_hi; j += kTopPThreads) {
     const float v = __ldcg(row + j);
     if (!(v >= t)) row[j] = -INFINITY;
   }
+  if constexpr (CL > 1) tp_cluster_sync();  // no CTA leaves while another may still read its shared memory
   pdl_trigger();
 }
 
@@ -897,7 +990,16 @@ extern "C" int ssd_top_p_mask(ssd_stream_t stream, float* x, int64_t ld, int row
   if (top_p >= 1.0f) return SSD_OK;  // the whole distribution
   if (V >= (1 << 19)) return SSD_ERR_UNSUPPORTED;  // fixed-point bin masses would overflow
   cudaStream_t st = (cudaStream_t)stream;
-  SSD_PDL(top_p_mask_kernel, dim3(rows), kTopPThreads, 0, st, x, ld, V, 1.0 / (double)temperature, (double)top_p);
+  const double inv_t = 1.0 / (double)temperature, p = (double)top_p;
+  if (rows <= 74) {  // up to half the SMs' worth of rows: four CTAs per row
+    if (launch_pdl_cluster(top_p_mask_kernel<4>, dim3(rows * 4), dim3(kTopPThreads), 0, st, 4u, x, ld, V, inv_t, p) !=
+        cudaSuccess) {
+      (void)cudaGetLastError();
+      return SSD_ERR_LAUNCH;
+    }
+    return SSD_OK;
+  }
+  SSD_PDL(top_p_mask_kernel<1>, dim3(rows), kTopPThreads, 0, st, x, ld, V, inv_t, p);
   SSD_CHECK_LAUNCH();
   return SSD_OK;
 }

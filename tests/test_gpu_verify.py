@@ -172,9 +172,9 @@ def test_sample_seeded_key_is_deterministic(cuda):
     assert r3.recovery_tokens.tolist() == r1.recovery_tokens.tolist()
 
 
-def _top_p_rows(v, seed):
+def _top_p_rows(v, seed, n=6):
     rng = np.random.default_rng(seed)
-    rows = (3.0 * rng.standard_normal((6, v))).astype(np.float32)
+    rows = (3.0 * rng.standard_normal((max(n, 6), v))).astype(np.float32)
     rows[1] = np.round(rows[1] * 4) / 4                 # many ties
     rows[2, ::7] = -np.inf                              # already masked entries
     rows[2, 5] = np.nan
@@ -183,15 +183,17 @@ def _top_p_rows(v, seed):
     return rows
 
 
-@pytest.mark.parametrize("v,t,p", [(256000, 1.0, 0.95), (256000, 0.7, 0.5), (32000, 1.3, 0.9), (4099, 1.0, 1e-4)])
-def test_top_p_mask_matches_oracle(cuda, v, t, p):
-    """ssd_top_p_mask keeps exactly the oracle's nucleus (same values, everything else -inf)."""
+@pytest.mark.parametrize("v,t,p,n", [(256000, 1.0, 0.95, 6), (256000, 0.7, 0.5, 6), (32000, 1.3, 0.9, 6),
+                                     (4099, 1.0, 1e-4, 6), (32000, 1.0, 0.95, 80), (4099, 0.8, 0.7, 75)])
+def test_top_p_mask_matches_oracle(cuda, v, t, p, n):
+    """ssd_top_p_mask keeps exactly the oracle's nucleus (same values, everything else -inf); up to 74
+    rows run four CTAs per row (a cluster), more rows one CTA per row."""
     import torch
 
     from oracle.verify import top_p_mask as o_mask
     from ssd_b200.algorithm.verify import top_p_mask_
 
-    rows = _top_p_rows(v, seed=v + int(100 * p))
+    rows = _top_p_rows(v, seed=v + int(100 * p), n=n)
     got = top_p_mask_(torch.from_numpy(rows).cuda(), t, p).cpu().numpy()
     want = o_mask(rows, t, p)
     np.testing.assert_array_equal(got, want)

@@ -66,7 +66,8 @@ class GemmaShape:
         return elem * 2 * self.num_layers * self.num_kv_heads * self.head_dim
 
 
-# the toy pair (config 0) and the Gemma-7B / Gemma-2B pair.
+# The model shapes the engine and the benchmark use: the small toy pair (2-layer target, 1-layer draft,
+# d_model 256, vocab 1024), the Gemma-7B / Gemma-2B pair, and small bf16 pairs for tensor-parallel checks.
 PRESETS = {
     "toy-target": GemmaShape(2, 256, 4, 1, 64, 1024, 1024),
     "toy-draft": GemmaShape(1, 256, 4, 1, 64, 1024, 1024),
